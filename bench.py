@@ -1,0 +1,533 @@
+#!/usr/bin/env python
+"""Benchmark of the fused FP8-replay GDN decode step on B200.
+
+Workload (BASELINE config 3 at the metric's point, batch 64, L = 16): one
+*step* is one decode token through a stack of NL independent GDN layers,
+each a single ``gdn_fused_step`` launch (prep + ring append + replay, and the
+flush/re-quantisation on the L-th token of the ring cycle) at batch 64,
+H = 16, HV = 32, K = V = 128.  Steps walk the ring cycle, so the flush cost
+is amortised exactly as in the reference's cycle model
+(prototype/bench_gdn_full_contract.py:225-308).  NL layers x ~46 MB of state
+(> 2x the 126 MB L2) keep every launch reading its state from HBM.
+
+The metric is decode steps.seq/s per GDN layer: (steps x NL x batch) / time.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Multi-GPU: one process per GPU (torchrun), each rank runs its own batch of
+64 sequences (weak scaling over independent sequence shards); no collective
+on the data path -- only the barrier and the max-over-ranks of the timing.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import pathlib
+import statistics
+import sys
+import threading
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "fp8-replayssm-gdn-kernel_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "GDN decode steps·seq/s @batch64 L=16; achieved HBM GB/s vs B200 peak"
+UNIT = "steps·seq/s"
+H, HV, KD = 16, 32, 128
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1024)
+    ap.add_argument("--warmup", type=int, default=32)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--ring", type=int, default=16)
+    ap.add_argument("--layers", type=int, default=8, help="independent layer states (default 8: 368 MB > 2x L2)")
+    ap.add_argument("--e2e-steps", type=int, default=64)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-core", action="store_true", help="skip the core-replay (config 2) block-V sweep")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------- helpers
+
+def measured_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profile_traffic():
+    """dram bytes per launch of the step kernel from the committed ncu summary."""
+    p = ROOT / "profiles" / "step_kernel_b64_l16.txt"
+    try:
+        for line in p.read_text().splitlines():
+            if line.startswith("dram_bytes_per_launch_cycle_avg"):
+                return int(float(line.split("=")[1].strip()))
+    except Exception:
+        pass
+    return None
+
+
+class ClockSampler:
+    """NVML sampling of SM clock and clock-event reasons during the timed region."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+        0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+        0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device_index: int):
+        self.samples, self.reasons, self.ok = [], set(), False
+        self._stop = threading.Event()
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.handle = self._handle(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # no NVML: report that instead of numbers
+            self.err = repr(e)
+
+    def _handle(self, idx):
+        import torch
+
+        pynvml = self.nvml
+        try:
+            props = torch.cuda.get_device_properties(idx)
+            bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+            return pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+        except Exception:
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            phys = int(vis.split(",")[idx]) if vis else idx
+            return pynvml.nvmlDeviceGetHandleByIndex(phys)
+
+    def _run(self):
+        n = self.nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append(n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM))
+                try:
+                    r = n.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                except AttributeError:
+                    r = n.nvmlDeviceGetCurrentClocksThrottleReasons(self.handle)
+                for bit, name in self.REASONS.items():
+                    if r & bit and bit != 0x1:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.002)
+
+    def __enter__(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ok:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": f"NVML unavailable: {self.err}"}
+        med = statistics.median(self.samples) if self.samples else None
+        return {"sm_mhz": med, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                "samples": len(self.samples)}
+
+
+def dist_init():
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    import torch
+
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+# ---------------------------------------------------------------- CPU baseline (oracle port)
+
+def cpu_units(units_per_worker: int, workers: int, seed: int, ring_len: int):
+    """Run the oracle port on `workers` spawned processes; returns (units, seconds)."""
+    import multiprocessing as mp
+
+    from oracle import cpu_bench
+
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(workers, initializer=cpu_bench.worker_init, initargs=(seed, ring_len)) as pool:
+        pool.map(cpu_bench.run_units, [1] * workers)  # warm the workers
+        t0 = time.perf_counter()
+        res = pool.map(cpu_bench.run_units, [units_per_worker] * workers)
+        wall = time.perf_counter() - t0
+    return sum(r[0] for r in res), wall
+
+
+def cpu_workers():
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except AttributeError:
+        return max(1, os.cpu_count() or 1)
+
+
+def cpu_baseline(seed: int, ring_len: int):
+    workers = cpu_workers()
+    units, wall = cpu_units(ring_len, workers, seed, ring_len)  # one full ring cycle per worker
+    return {"value": units / wall, "unit": UNIT, "cores": workers, "kind": "port",
+            "sample": f"{units} sequence-layer steps ({workers} sequences x one L={ring_len} ring cycle incl. flush) "
+                      f"of the numpy oracle port of replay_decode, {wall:.1f} s wall"}
+
+
+def run_reference(args, world, rank):
+    """--impl reference: the reference's CPU implementation of the path (oracle port)."""
+    if rank != 0:
+        return
+    workers = cpu_workers()
+    # size each step's sample so the whole run stays within a few minutes:
+    # one unit per worker per step; cap total steps timed by the budget
+    budget_s = 150.0
+    probe_units, probe_wall = cpu_units(1, workers, args.seed, args.ring)
+    per_step = probe_wall if probe_wall > 0 else 0.05
+    steps = args.steps
+    units_per_step = workers
+    while steps * per_step > budget_s and steps > 1:
+        steps //= 2
+    t_units, t_wall = cpu_units(max(1, steps), workers, args.seed, args.ring)
+    value = t_units / t_wall
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": args.gpus,
+        "steps": steps,
+        "warmup": 1,
+        "ms_per_step": 1e3 * t_wall / max(1, steps),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded, BASELINE config 1/3 distributions)",
+        "config": {"workload": f"config3 full-contract step, one GDN layer, L={args.ring}, CPU sample",
+                   "global_batch": units_per_step, "seq_len": args.ring, "parallelism": f"{workers} processes"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": workers, "kind": "port",
+                         "sample": f"{t_units} sequence-layer steps ({units_per_step} sequences per step, "
+                                   f"{steps} steps) of the numpy oracle port of replay_decode"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference is a Python/Triton prototype that cannot be installed (no setup.py/pyproject); "
+                "its CPU path (ref.py replay_decode) is timed through the repo's numpy restatement",
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- GPU arm
+
+def build_stack(args, device):
+    import torch
+
+    import gdnr
+    from gdnr import inputs as gin
+
+    B, L, NL = args.batch, args.ring, args.layers
+    layers, step_inputs = [], []
+    for li in range(NL):
+        st = gdnr.ReplayState.allocate(B, H, HV, L, device=device, scale_dtype=torch.float32,
+                                       gate_dtype=torch.float32)
+        raw = gin.raw_step_inputs(B, L, seed=args.seed * 1000 + li, device=device)
+        st.load_state(raw["state"])
+        layers.append({"state": st, "a_log": raw["a_log"], "dt_bias": raw["dt_bias"],
+                       "out": torch.empty(B, HV, KD, dtype=torch.bfloat16, device=device)})
+        # distinct raw inputs per (layer, ring position), resident in HBM
+        step_inputs.append([(raw["mixed_qkv"][:, s].contiguous(), raw["a"][:, s].contiguous(),
+                             raw["b"][:, s].contiguous()) for s in range(L)])
+        del raw
+    pos = [torch.full((B,), s, dtype=torch.int32, device=device) for s in range(L)]
+    err = torch.zeros(1, dtype=torch.int32, device=device)
+    return layers, step_inputs, pos, err
+
+
+def launch_position(layers, step_inputs, pos, err, s):
+    import gdnr
+
+    for li, lay in enumerate(layers):
+        st = lay["state"]
+        mixed, a, b = step_inputs[li][s]
+        gdnr.gdn_fused_step(mixed, a, b, lay["a_log"], lay["dt_bias"], pos[s], st.checkpoint, st.scale, st.k_ring,
+                            st.v_ring, st.g_ring, st.beta_ring, out=lay["out"], error_flag=err)
+
+
+def run_ours(args, world, rank, local):
+    import torch
+
+    import gdnr
+    from oracle import gdn_oracle as O
+
+    device = torch.device("cuda", local)
+    B, L, NL = args.batch, args.ring, args.layers
+    cpu_line = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu_line = cpu_baseline(args.seed, L)  # spawn pool; GPU untouched so far
+
+    layers, step_inputs, pos, err = build_stack(args, device)
+    stream = torch.cuda.Stream(device)
+    torch.cuda.synchronize()
+    # one graph per ring position: NL fused launches
+    graphs = []
+    with torch.cuda.stream(stream):
+        for s in range(L):  # eager pass: lazy loading + smem attribute before capture
+            launch_position(layers, step_inputs, pos, err, s)
+    torch.cuda.synchronize()
+    for s in range(L):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            launch_position(layers, step_inputs, pos, err, s)
+        graphs.append(g)
+    torch.cuda.synchronize()
+
+    step_idx = 0
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            graphs[step_idx % L].replay()
+            step_idx += 1
+    barrier(world)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local)
+    with sampler:
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for _ in range(args.steps):
+                graphs[step_idx % L].replay()
+                step_idx += 1
+            ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = ev0.elapsed_time(ev1)
+    ms_max = max_over_ranks(ms, world)
+    dev_err = int(err.item())
+
+    launches = args.steps * NL
+    units = launches * B * world
+    value = units / (ms_max / 1e3)
+    # algorithmic bytes, averaged over the ring cycle actually timed
+    first = args.warmup
+    cyc = [O.algorithmic_bytes(B, (first + i) % L + 1, L, scale_bytes=4, gate_bytes=4, ab_bytes=2)
+           for i in range(args.steps)]
+    bytes_per_launch = sum(cyc) / len(cyc)
+    launch_s = (ms / 1e3) / launches
+    achieved = bytes_per_launch / launch_s / 1e9
+    peak, peak_kind = measured_peak()
+
+    # ---- end to end through the public API with host buffers (pinned), per layer-step
+    e2e = run_e2e(args, layers, step_inputs, pos, stream, world) if args.e2e_steps > 0 else None
+
+    core = None
+    if not args.no_core and world == 1:
+        core = run_core(args, device, stream)
+
+    del graphs
+    torch.cuda.synchronize()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_max / args.steps,
+        "us_per_layer_step": 1e3 * ms_max / launches,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "e4m3/f32",
+        "data": "synthetic (seeded; BASELINE config 1/3 distributions; random state N(0,0.02))",
+        "config": {
+            "workload": f"config3 fused full-contract step (prep+ring append+replay, flush every {L}), "
+                        f"batch {B}/GPU, L={L}, cycle-amortised; one step = one token through {NL} independent "
+                        "GDN layers (one launch each)",
+            "global_batch": B * world, "seq_len": L, "parallelism": f"sequence-shard x{world} (no collective)",
+            "heads": H, "value_heads": HV, "head_dim": KD, "layers": NL,
+            "l2": f"inputs larger than L2: {NL} layer states x {layers[0]['state'].nbytes() / 1e6:.1f} MB",
+        },
+        "gpu_launches": launches,
+        "device_error_word": dev_err,
+        "clocks": sampler.summary(),
+        "roofline": {
+            "bound": "hbm",
+            "kernel": "gdnr::step_kernel<fused,e4m3,G=2>",
+            "achieved": achieved,
+            "peak": peak,
+            "peak_kind": peak_kind,
+            "unit": "GB/s",
+            "frac": achieved / peak,
+            "traffic": profile_traffic(),
+            "algorithmic_bytes_per_launch": bytes_per_launch,
+            "note": "achieved = cycle-averaged algorithmic bytes per launch / (timed region / launches)",
+        },
+    }
+    if e2e is not None:
+        line["e2e"] = e2e
+    if core is not None:
+        line["core_replay"] = core
+    if cpu_line is not None:
+        line["cpu_baseline"] = cpu_line
+    print(json.dumps(line), flush=True)
+
+
+def run_e2e(args, layers, step_inputs, pos, stream, world):
+    """Public-API step with the step's inputs copied from pinned host memory and
+    the output read back to pinned host memory, inside the timed region."""
+    import torch
+
+    import gdnr
+
+    B, L = args.batch, args.ring
+    host_in = [[tuple(t.cpu().pin_memory() for t in step_inputs[li][s]) for s in range(L)] for li in range(len(layers))]
+    dev_in = [tuple(torch.empty_like(t) for t in step_inputs[0][0]) for _ in layers]
+    host_out = [torch.empty(B, HV, KD, dtype=torch.bfloat16).pin_memory() for _ in layers]
+    h2d = sum(t.numel() * t.element_size() for t in host_in[0][0])
+    d2h = host_out[0].numel() * host_out[0].element_size()
+
+    def one(i):
+        s = i % L
+        with torch.cuda.stream(stream):
+            for li, lay in enumerate(layers):
+                mixed, a, b = dev_in[li]
+                hm, ha, hb = host_in[li][s]
+                mixed.copy_(hm, non_blocking=True)
+                a.copy_(ha, non_blocking=True)
+                b.copy_(hb, non_blocking=True)
+                st = lay["state"]
+                gdnr.gdn_fused_step(mixed, a, b, lay["a_log"], lay["dt_bias"], pos[s], st.checkpoint, st.scale,
+                                    st.k_ring, st.v_ring, st.g_ring, st.beta_ring, out=lay["out"])
+                host_out[li].copy_(lay["out"], non_blocking=True)
+
+    for i in range(L):
+        one(i)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.e2e_steps):
+        one(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), world)
+    units = args.e2e_steps * len(layers) * B * world
+    return {"value": units / (ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d * len(layers),
+            "d2h_bytes_per_step": d2h * len(layers), "steps": args.e2e_steps,
+            "path": "gdnr.gdn_fused_step (Python) -> libgdnr C ABI, eager launches, pinned host buffers"}
+
+
+def run_core(args, device, stream):
+    """core replay (non-flush) of a full L=16 ring, block-V sweep."""
+    import torch
+
+    import gdnr
+    from gdnr import inputs as gin
+    from oracle import gdn_oracle as O
+
+    B, L, NL = args.batch, args.ring, args.layers
+    sets = []
+    for li in range(NL):
+        d = gin.replay_ring_inputs(B, L, seed=args.seed * 7 + li, device=device)
+        ck = gdnr.quantize_checkpoint(d["state"], scale_dtype=torch.float32, compute_saturation=False)
+        sets.append((ck, d, torch.full((B,), L, dtype=torch.int32, device=device),
+                     torch.zeros(B, dtype=torch.bool, device=device),
+                     torch.empty(B, HV, KD, dtype=torch.bfloat16, device=device)))
+    res = {}
+    nbytes = O.algorithmic_bytes(B, L, L, scale_bytes=4, gate_bytes=4, fused=False)
+    for bv in (32, 64, 128):
+        def run():
+            for ck, d, vl, fl, out in sets:
+                gdnr.gdn_replay_fp8(ck.payload, ck.scale, d["q"], d["k"], d["v"], d["g"], d["beta"], vl, fl,
+                                    block_v=bv, out=out)
+        with torch.cuda.stream(stream):
+            run()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            run()
+        reps = 50
+        with torch.cuda.stream(stream):
+            for _ in range(5):
+                g.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(reps):
+                g.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        us = 1e3 * e0.elapsed_time(e1) / (reps * NL)
+        res[f"block_v{bv}"] = {"us_per_launch": us, "GB_s": nbytes / (us * 1e-6) / 1e9,
+                               "steps_seq_per_s": B / (us * 1e-6)}
+        del g
+    res["algorithmic_bytes_per_launch"] = nbytes
+    res["workload"] = "config2: gdn_replay_fp8 non-flush, B=64, full L=16 ring, f32 scales/gates"
+    return res
+
+
+def main():
+    args = parse_args()
+    world, rank, local = dist_init() if args.impl == "ours" else (
+        int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), 0)
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_ours(args, world, rank, local)
+    finally:
+        if args.impl == "ours" and world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

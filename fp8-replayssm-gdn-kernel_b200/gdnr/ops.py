@@ -1,0 +1,310 @@
+"""Operator API -- drop-in mirror of the reference prototype's call contract.
+
+Same names, argument order, argument meaning and in-place side effects as
+``prototype/gdn_replayssm_fp8_kernel.py`` (zz774ever/fp8-replayssm-gdn-kernel):
+
+* :func:`gdn_replay_fp8`        <- ``gdn_replay_fp8``        (:344-405)
+* :func:`gdn_replay_fp8_split`  <- ``gdn_replay_fp8_split``  (:1129-1235)
+* :func:`gdn_prep_ring`         <- ``gdn_prep_ring``         (:710-795)
+* :func:`gdn_bf16_step`         <- ``gdn_bf16_step``         (:408-450)
+
+plus the fused full-contract step (:func:`gdn_fused_step`, prep + replay +
+flush in one launch) and the GPU vblock32 codec (:func:`quantize_checkpoint`,
+:func:`dequantize_checkpoint`, mirrors of
+``prototype/gdn_replay_fp8_reference.py:40-134``).
+
+All work runs in libgdnr (hand-written sm_100a CUDA) on the current torch
+stream; nothing falls back to the CPU.  Triton-specific tuning knobs
+(``num_warps``, ``num_stages``, ``block_kc``, ``precompute_grouped``,
+``fused``) are accepted for signature compatibility and ignored.
+Invalid arguments raise ``ValueError`` (``GdnrValueError``).
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+
+_DIVISOR = {"oracle": 0, "rounded": 1}
+
+
+def _divisor(mode: str | int) -> int:
+    if isinstance(mode, int):
+        return mode
+    try:
+        return _DIVISOR[mode]
+    except KeyError:
+        raise ValueError(f"quant_divisor must be one of {sorted(_DIVISOR)}") from None
+
+
+def _as_bhv(out: torch.Tensor) -> torch.Tensor:
+    # accept the production layout [B,1,HV,V] as well as [B,HV,V]
+    if out.dim() == 4 and out.shape[1] == 1:
+        return out.squeeze(1)
+    return out
+
+
+def _err_ptr(error_flag: torch.Tensor | None) -> int | None:
+    if error_flag is None:
+        return None
+    if error_flag.dtype not in (torch.int32, torch.uint32) or error_flag.numel() < 1 or error_flag.device.type != "cuda":
+        raise ValueError("error_flag must be a CUDA int32 tensor with at least one element")
+    return error_flag.data_ptr()
+
+
+def gdn_replay_fp8(
+    checkpoint: torch.Tensor,
+    checkpoint_scale: torch.Tensor | None,
+    q: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    g_cache: torch.Tensor,
+    beta_cache: torch.Tensor,
+    valid_len: torch.Tensor,
+    flush: torch.Tensor,
+    block_v: int = 32,
+    num_warps: int = 4,
+    out: torch.Tensor | None = None,
+    quant_divisor: str = "oracle",
+    error_flag: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Replay (and, where ``flush[b]``, rebuild + re-quantise in place).
+
+    checkpoint [B,HV,V,K] float8_e4m3fn (or float32: full-precision variant),
+    checkpoint_scale [B,HV,V/32] float16|float32, q [B,H,K], rings
+    k [B,L,H,K] / v [B,L,HV,V] bf16, g/beta [B,L,HV], valid_len [B] int32,
+    flush [B] bool.  Returns out [B,HV,V] in q's dtype unless ``out`` given.
+    """
+    del num_warps
+    batch, _, _, _ = k_cache.shape
+    value_heads, value_dim = v_cache.shape[2], v_cache.shape[3]
+    if out is None:
+        out = torch.empty(batch, value_heads, value_dim, dtype=q.dtype, device=q.device)
+    args = _lib.ReplayArgs()
+    args.checkpoint = _lib.tensor_desc(checkpoint)
+    args.scale = _lib.tensor_desc(checkpoint_scale if checkpoint.dtype != torch.float32 else None)
+    args.q = _lib.tensor_desc(q)
+    args.k_ring = _lib.tensor_desc(k_cache)
+    args.v_ring = _lib.tensor_desc(v_cache)
+    args.g_ring = _lib.tensor_desc(g_cache)
+    args.beta_ring = _lib.tensor_desc(beta_cache)
+    args.valid_len = _lib.tensor_desc(valid_len)
+    args.flush = _lib.tensor_desc(flush)
+    args.out = _lib.tensor_desc(_as_bhv(out))
+    args.block_v = int(block_v)
+    args.quant_divisor = _divisor(quant_divisor)
+    args.error_flag = _err_ptr(error_flag)
+    _lib.check(_lib.load().gdnr_replay(ctypes.byref(args), _lib.stream_handle(q.device)))
+    return out
+
+
+def gdn_replay_fp8_split(
+    checkpoint: torch.Tensor,
+    checkpoint_scale: torch.Tensor,
+    q: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    g_cache: torch.Tensor,
+    beta_cache: torch.Tensor,
+    valid_len: torch.Tensor,
+    transformed_query_buffer: torch.Tensor,
+    coefficient_buffer: torch.Tensor,
+    block_v: int = 32,
+    num_warps: int = 4,
+    block_kc: int = 128,
+    precompute_grouped: bool = True,
+    num_stages: int = 2,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Non-flush replay as precompute + apply (kern.py:1129-1235).
+
+    ``transformed_query_buffer`` [B,HV,K] float32 and ``coefficient_buffer``
+    [B,HV,L] float32 are caller-owned and receive T and c_t (t < valid_len).
+    """
+    del num_warps, block_kc, precompute_grouped, num_stages
+    batch = k_cache.shape[0]
+    value_heads, value_dim = v_cache.shape[2], v_cache.shape[3]
+    if out is None:
+        out = torch.empty(batch, value_heads, value_dim, dtype=q.dtype, device=q.device)
+    args = _lib.ReplaySplitArgs()
+    args.checkpoint = _lib.tensor_desc(checkpoint)
+    args.scale = _lib.tensor_desc(checkpoint_scale)
+    args.q = _lib.tensor_desc(q)
+    args.k_ring = _lib.tensor_desc(k_cache)
+    args.v_ring = _lib.tensor_desc(v_cache)
+    args.g_ring = _lib.tensor_desc(g_cache)
+    args.beta_ring = _lib.tensor_desc(beta_cache)
+    args.valid_len = _lib.tensor_desc(valid_len)
+    args.tq = _lib.tensor_desc(transformed_query_buffer)
+    args.coef = _lib.tensor_desc(coefficient_buffer)
+    args.out = _lib.tensor_desc(_as_bhv(out))
+    args.block_v = int(block_v)
+    _lib.check(_lib.load().gdnr_replay_split(ctypes.byref(args), _lib.stream_handle(q.device)))
+    return out
+
+
+def gdn_prep_ring(
+    mixed_qkv: torch.Tensor,
+    a: torch.Tensor,
+    b: torch.Tensor,
+    a_log: torch.Tensor,
+    dt_bias: torch.Tensor,
+    pos: torch.Tensor,
+    q_out: torch.Tensor,
+    k_ring: torch.Tensor,
+    v_ring: torch.Tensor,
+    g_ring: torch.Tensor,
+    beta_ring: torch.Tensor,
+    num_warps: int = 1,
+    fused: bool = True,
+    error_flag: torch.Tensor | None = None,
+) -> None:
+    """q/k L2 norm, gating, ring append of slot ``pos[b]`` (kern.py:710-795)."""
+    del num_warps, fused
+    args = _lib.PrepArgs()
+    for name, t in (("mixed_qkv", mixed_qkv), ("a", a), ("b", b), ("a_log", a_log), ("dt_bias", dt_bias),
+                    ("pos", pos), ("q_out", q_out), ("k_ring", k_ring), ("v_ring", v_ring), ("g_ring", g_ring),
+                    ("beta_ring", beta_ring)):
+        setattr(args, name, _lib.tensor_desc(t))
+    args.error_flag = _err_ptr(error_flag)
+    _lib.check(_lib.load().gdnr_prep_ring(ctypes.byref(args), _lib.stream_handle(mixed_qkv.device)))
+
+
+def gdn_fused_step(
+    mixed_qkv: torch.Tensor,
+    a: torch.Tensor,
+    b: torch.Tensor,
+    a_log: torch.Tensor,
+    dt_bias: torch.Tensor,
+    pos: torch.Tensor,
+    checkpoint: torch.Tensor,
+    checkpoint_scale: torch.Tensor | None,
+    k_ring: torch.Tensor,
+    v_ring: torch.Tensor,
+    g_ring: torch.Tensor,
+    beta_ring: torch.Tensor,
+    out: torch.Tensor | None = None,
+    q_out: torch.Tensor | None = None,
+    pos_out: torch.Tensor | None = None,
+    quant_divisor: str = "oracle",
+    error_flag: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """One full-contract decode step in one launch.
+
+    Appends this token (prep of ``mixed_qkv``/``a``/``b``) to ring slot
+    ``pos[b]``, replays slots ``0..pos[b]`` against the FP8 checkpoint, writes
+    ``out`` [B,HV,V] (or [B,1,HV,V]), and when ``pos[b] == L-1`` rebuilds the
+    state and re-quantises the checkpoint in place.  ``pos_out`` (optional,
+    distinct from ``pos``) receives ``(pos+1) % L``.
+    """
+    batch = mixed_qkv.shape[0]
+    value_heads = v_ring.shape[2]
+    if out is None:
+        out = torch.empty(batch, value_heads, v_ring.shape[3], dtype=mixed_qkv.dtype, device=mixed_qkv.device)
+    args = _lib.StepArgs()
+    args.mixed_qkv = _lib.tensor_desc(mixed_qkv)
+    args.a = _lib.tensor_desc(a)
+    args.b = _lib.tensor_desc(b)
+    args.a_log = _lib.tensor_desc(a_log)
+    args.dt_bias = _lib.tensor_desc(dt_bias)
+    args.pos = _lib.tensor_desc(pos)
+    args.pos_out = _lib.tensor_desc(pos_out)
+    args.checkpoint = _lib.tensor_desc(checkpoint)
+    args.scale = _lib.tensor_desc(checkpoint_scale if checkpoint.dtype != torch.float32 else None)
+    args.k_ring = _lib.tensor_desc(k_ring)
+    args.v_ring = _lib.tensor_desc(v_ring)
+    args.g_ring = _lib.tensor_desc(g_ring)
+    args.beta_ring = _lib.tensor_desc(beta_ring)
+    args.out = _lib.tensor_desc(_as_bhv(out))
+    args.q_out = _lib.tensor_desc(q_out)
+    args.quant_divisor = _divisor(quant_divisor)
+    args.error_flag = _err_ptr(error_flag)
+    _lib.check(_lib.load().gdnr_fused_step(ctypes.byref(args), _lib.stream_handle(mixed_qkv.device)))
+    return out
+
+
+def gdn_bf16_step(state, q, k, v, g, beta) -> torch.Tensor:
+    """One-token GDN step on a bf16 state, read-modify-write (kern.py:408-450)."""
+    batch, value_heads, value_dim, _ = state.shape
+    out = torch.empty(batch, value_heads, value_dim, dtype=q.dtype, device=q.device)
+    args = _lib.Bf16StepArgs()
+    for name, t in (("state", state), ("q", q), ("k", k), ("v", v), ("g", g), ("beta", beta), ("out", out)):
+        setattr(args, name, _lib.tensor_desc(t))
+    _lib.check(_lib.load().gdnr_bf16_step(ctypes.byref(args), _lib.stream_handle(q.device)))
+    return out
+
+
+@dataclass
+class QuantizedCheckpoint:
+    """Mirror of ``QuantizedCheckpoint`` (ref.py:21-33), on the GPU."""
+
+    payload: torch.Tensor
+    scale: torch.Tensor
+    granularity: str
+    tile_size: int
+    saturation_fraction: float
+
+    @property
+    def storage_bytes(self) -> int:
+        return self.payload.numel() * self.payload.element_size() + self.scale.numel() * self.scale.element_size()
+
+
+def quantize_checkpoint(
+    state: torch.Tensor,
+    granularity: str = "vblock",
+    tile_size: int = 32,
+    scale_dtype: torch.dtype = torch.float16,
+    quant_divisor: str = "oracle",
+    payload: torch.Tensor | None = None,
+    scale: torch.Tensor | None = None,
+    compute_saturation: bool = True,
+) -> QuantizedCheckpoint:
+    """GPU vblock32 FP8 quantiser, bit-exact with ``quantize_checkpoint(state, 'vblock', 32)``.
+
+    ``state`` [B,HV,V,K] float32 on CUDA.  ``compute_saturation`` reads the
+    saturation count back (one synchronisation), like the reference's
+    ``.item()`` at ref.py:95.
+    """
+    if granularity != "vblock" or tile_size != 32:
+        raise ValueError("the GPU codec implements granularity='vblock', tile_size=32 only")
+    state = state if state.dtype == torch.float32 else state.float()
+    b, hv, v, k = state.shape
+    if payload is None:
+        payload = torch.empty(b, hv, v, k, dtype=torch.float8_e4m3fn, device=state.device)
+    if scale is None:
+        scale = torch.empty(b, hv, v // 32, dtype=scale_dtype, device=state.device)
+    sat = torch.zeros(1, dtype=torch.int32, device=state.device) if compute_saturation else None
+    args = _lib.CodecArgs()
+    args.state = _lib.tensor_desc(state)
+    args.payload = _lib.tensor_desc(payload)
+    args.scale = _lib.tensor_desc(scale)
+    args.quant_divisor = _divisor(quant_divisor)
+    args.saturation_count = sat.data_ptr() if sat is not None else None
+    _lib.check(_lib.load().gdnr_quantize_vblock32(ctypes.byref(args), _lib.stream_handle(state.device)))
+    frac = float(sat.item()) / max(state.numel(), 1) if sat is not None else 0.0
+    return QuantizedCheckpoint(payload, scale, "vblock", 32, frac)
+
+
+def dequantize_checkpoint(ckpt: QuantizedCheckpoint, out: torch.Tensor | None = None) -> torch.Tensor:
+    """payload * scale[row/32] as float32 (ref.py:109-134), on the GPU."""
+    if ckpt.granularity != "vblock" or ckpt.tile_size != 32:
+        raise ValueError("the GPU codec implements granularity='vblock', tile_size=32 only")
+    if out is None:
+        out = torch.empty(ckpt.payload.shape, dtype=torch.float32, device=ckpt.payload.device)
+    args = _lib.CodecArgs()
+    args.state = _lib.tensor_desc(out)
+    args.payload = _lib.tensor_desc(ckpt.payload)
+    args.scale = _lib.tensor_desc(ckpt.scale)
+    _lib.check(_lib.load().gdnr_dequantize_vblock32(ctypes.byref(args), _lib.stream_handle(out.device)))
+    return out
+
+
+def read_device_error(clear: bool = True) -> int:
+    """Read (and clear) the library's default device error word (synchronous)."""
+    v = ctypes.c_uint32(0)
+    _lib.check(_lib.load().gdnr_read_device_error(ctypes.byref(v), int(clear)))
+    return int(v.value)

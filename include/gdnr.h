@@ -1,0 +1,166 @@
+/*
+ * gdnr.h -- C ABI of the B200-native FP8-checkpoint replay GDN decode path.
+ *
+ * Every entry point takes plain pointers + shapes + strides (gdnr_tensor),
+ * never allocates, never synchronises, and enqueues its work on the CUDA
+ * stream it is given (a cudaStream_t passed as void*; NULL = legacy default
+ * stream).  Return value: GDNR_OK (0) or a negative gdnr_status; the message
+ * of the last failure on the calling thread is gdnr_last_error().
+ *
+ * Reference interfaces replaced (paths inside zz774ever/fp8-replayssm-gdn-kernel):
+ *   gdnr_replay          <- gdn_replay_fp8           prototype/gdn_replayssm_fp8_kernel.py:344-405
+ *   gdnr_replay_split    <- gdn_replay_fp8_split     prototype/gdn_replayssm_fp8_kernel.py:1129-1235
+ *   gdnr_prep_ring       <- gdn_prep_ring            prototype/gdn_replayssm_fp8_kernel.py:710-795
+ *   gdnr_bf16_step       <- gdn_bf16_step            prototype/gdn_replayssm_fp8_kernel.py:408-450
+ *   gdnr_quantize_vblock32   <- quantize_checkpoint(state, "vblock", 32)
+ *                                                   prototype/gdn_replay_fp8_reference.py:40-106
+ *   gdnr_dequantize_vblock32 <- dequantize_checkpoint prototype/gdn_replay_fp8_reference.py:109-134
+ *   gdnr_fused_step      <- gdn_prep_ring + gdn_replay_fp8 (+ flush) as one call, the
+ *                          full-contract step of prototype/bench_gdn_full_contract.py:138-308
+ *
+ * Geometry supported by the kernels: K = V = 128 (Qwen3.5 GDN head dims),
+ * HV = G*H with G in {1,2,4}, ring length L in [1, 64], one scale per
+ * 32 value rows ("vblock32").
+ */
+#ifndef GDNR_H
+#define GDNR_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GDNR_ABI_VERSION 1
+
+typedef enum {
+  GDNR_DT_NONE = 0,
+  GDNR_F32 = 1,
+  GDNR_F16 = 2,
+  GDNR_BF16 = 3,
+  GDNR_E4M3 = 4, /* float8_e4m3fn, one byte */
+  GDNR_I32 = 5,
+  GDNR_U8 = 6,   /* torch.bool / uint8 */
+  GDNR_I8 = 7
+} gdnr_dtype;
+
+typedef enum {
+  GDNR_OK = 0,
+  GDNR_ERR_ARG = -1,         /* null pointer, wrong rank, inconsistent shapes */
+  GDNR_ERR_DTYPE = -2,       /* unsupported dtype for that argument */
+  GDNR_ERR_LAYOUT = -3,      /* stride / 16-byte alignment requirement not met */
+  GDNR_ERR_ALIAS = -4,       /* two buffers that must be distinct overlap */
+  GDNR_ERR_UNSUPPORTED = -5, /* geometry outside what the kernels implement */
+  GDNR_ERR_CUDA = -6         /* launch failed (message has the CUDA error) */
+} gdnr_status;
+
+/* Bits of the device error word (see error_flag below). */
+#define GDNR_DEVERR_WAIT_TIMEOUT 0x1u /* a bounded mbarrier wait gave up */
+#define GDNR_DEVERR_BAD_POS 0x2u      /* fused step: pos[b] outside [0, L) */
+
+/* Strided view of a device (or, for validation only, any) buffer. */
+typedef struct {
+  void* data;
+  int32_t dtype; /* gdnr_dtype */
+  int32_t ndim;  /* 0 = absent (optional argument) */
+  int64_t shape[4];
+  int64_t stride[4]; /* in elements */
+} gdnr_tensor;
+
+/* ---- gdnr_replay: mirror of gdn_replay_fp8 ---------------------------- */
+typedef struct {
+  gdnr_tensor checkpoint; /* [B,HV,V,K] E4M3, or F32 for the full-precision variant; in/out */
+  gdnr_tensor scale;      /* [B,HV,V/32] F16|F32 (absent for an F32 checkpoint); in/out */
+  gdnr_tensor q;          /* [B,H,K] BF16|F32, already L2-normalised */
+  gdnr_tensor k_ring;     /* [B,L,H,K] BF16 */
+  gdnr_tensor v_ring;     /* [B,L,HV,V] BF16 */
+  gdnr_tensor g_ring;     /* [B,L,HV] F32|BF16 (log decay) */
+  gdnr_tensor beta_ring;  /* [B,L,HV] F32|BF16 */
+  gdnr_tensor valid_len;  /* [B] I32: slots 0..valid_len-1 are replayed (clamped to [0,L]) */
+  gdnr_tensor flush;      /* [B] U8|I32: nonzero -> rebuild + re-quantise in place */
+  gdnr_tensor out;        /* [B,HV,V] BF16|F32 */
+  int32_t block_v;        /* value rows per CTA: 32, 64 or 128 (0 -> 128) */
+  int32_t quant_divisor;  /* 0: x/(amax/448) like ref.py:94; 1: x/fp16(amax/448) like kern.py:234 */
+  uint32_t* error_flag;   /* optional device word, OR-ed with GDNR_DEVERR_* */
+} gdnr_replay_args;
+
+int gdnr_replay(const gdnr_replay_args* args, void* stream);
+
+/* ---- gdnr_replay_split: mirror of gdn_replay_fp8_split ----------------- */
+typedef struct {
+  gdnr_tensor checkpoint, scale, q, k_ring, v_ring, g_ring, beta_ring, valid_len;
+  gdnr_tensor tq;   /* [B,HV,K] F32 caller buffer: receives the transformed query */
+  gdnr_tensor coef; /* [B,HV,L] F32 caller buffer: receives c_t for t < valid_len */
+  gdnr_tensor out;  /* [B,HV,V] BF16|F32 */
+  int32_t block_v;
+  uint32_t* error_flag;
+} gdnr_replay_split_args;
+
+int gdnr_replay_split(const gdnr_replay_split_args* args, void* stream);
+
+/* ---- gdnr_prep_ring: mirror of gdn_prep_ring --------------------------- */
+typedef struct {
+  gdnr_tensor mixed_qkv; /* [B, 2*H*K + HV*V] BF16|F32, inner stride 1 */
+  gdnr_tensor a, b;      /* [B,HV] BF16|F32 */
+  gdnr_tensor a_log;     /* [HV] F32 */
+  gdnr_tensor dt_bias;   /* [HV] F32 */
+  gdnr_tensor pos;       /* [B] I32 ring slot written */
+  gdnr_tensor q_out;     /* [B,H,K] BF16|F32 */
+  gdnr_tensor k_ring, v_ring, g_ring, beta_ring;
+  uint32_t* error_flag;
+} gdnr_prep_args;
+
+int gdnr_prep_ring(const gdnr_prep_args* args, void* stream);
+
+/* ---- gdnr_fused_step: prep + ring append + replay + flush, one launch -- */
+typedef struct {
+  gdnr_tensor mixed_qkv, a, b, a_log, dt_bias; /* as gdnr_prep_args */
+  gdnr_tensor pos;        /* [B] I32: slot of this token; the step flushes when pos == L-1 */
+  gdnr_tensor pos_out;    /* optional [B] I32 (distinct from pos): receives (pos+1) % L */
+  gdnr_tensor checkpoint; /* [B,HV,V,K] E4M3 | F32, in/out */
+  gdnr_tensor scale;      /* [B,HV,V/32] F16|F32 (absent for F32 checkpoint), in/out */
+  gdnr_tensor k_ring, v_ring, g_ring, beta_ring; /* in/out: slot pos is written */
+  gdnr_tensor out;        /* [B,HV,V] BF16|F32 */
+  gdnr_tensor q_out;      /* optional [B,H,K]: normalised q as the reference's prep writes it */
+  int32_t quant_divisor;
+  uint32_t* error_flag;
+} gdnr_step_args;
+
+int gdnr_fused_step(const gdnr_step_args* args, void* stream);
+
+/* ---- FP8 vblock32 codec ------------------------------------------------ */
+typedef struct {
+  gdnr_tensor state;      /* [B,HV,V,K] F32 (quantize: in; dequantize: out) */
+  gdnr_tensor payload;    /* [B,HV,V,K] E4M3 */
+  gdnr_tensor scale;      /* [B,HV,V/32] F16|F32 */
+  int32_t quant_divisor;  /* as gdnr_replay_args */
+  uint32_t* saturation_count; /* optional device counter: += #{|x/divisor| > 448} */
+} gdnr_codec_args;
+
+int gdnr_quantize_vblock32(const gdnr_codec_args* args, void* stream);
+int gdnr_dequantize_vblock32(const gdnr_codec_args* args, void* stream);
+
+/* ---- gdnr_bf16_step: mirror of gdn_bf16_step (bf16 state RMW control) -- */
+typedef struct {
+  gdnr_tensor state; /* [B,HV,V,K] BF16, in/out */
+  gdnr_tensor q, k;  /* [B,H,K] BF16|F32 */
+  gdnr_tensor v;     /* [B,HV,V] BF16|F32 */
+  gdnr_tensor g, beta; /* [B,HV] BF16|F32 */
+  gdnr_tensor out;   /* [B,HV,V] BF16|F32 */
+} gdnr_bf16_step_args;
+
+int gdnr_bf16_step(const gdnr_bf16_step_args* args, void* stream);
+
+/* ---- misc --------------------------------------------------------------- */
+const char* gdnr_last_error(void);
+const char* gdnr_version(void);
+int gdnr_abi_version(void);
+/* Library-owned device error word used when a call passes error_flag = NULL.
+ * Reads it (synchronously, on the current device) and optionally clears it. */
+int gdnr_read_device_error(uint32_t* value, int clear);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GDNR_H */
