@@ -218,4 +218,141 @@ __device__ __forceinline__ uint4 quantize16(const float* x, float divisor, uint3
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
+
+// ---------------------------------------------------------------- fast exact quantiser
+// y = x / divisor computed as x * (1/divisor); that product is within 2.5 ulp
+// of the IEEE quotient, so the e4m3 rounding of the two can differ only when
+// y lies within a few ulp of an e4m3 rounding midpoint (mantissa bits below
+// the 3 kept ones == 0x80000) or in the e4m3 subnormal range; those elements
+// take the IEEE division instead, and so do quotients within a few ulp of 448
+// (where the saturation count |x/divisor| > 448 is decided).  `fast_ok` is false when the divisor or its
+// reciprocal is not a normal float (then every element is divided exactly).
+__device__ __forceinline__ float quant_quotient(float x, float divisor, float rcp, bool fast_ok) {
+  float y = x * rcp;
+  const uint32_t u = __float_as_uint(y) & 0x7FFFFFFFu;
+  const bool near_mid = ((u & 0xFFFFFu) - 0x7FFF8u) <= 16u;
+  const bool near_max = (u - 0x43DFFFF8u) <= 16u;              // |y| within 8 ulp of 448 (saturation test)
+  const bool subnormal_e4m3 = (u != 0u) && (u < 0x3C800000u);  // |y| < 2^-6
+  if (!fast_ok || near_mid || near_max || subnormal_e4m3) y = __fdiv_rn(x, divisor);
+  return y;
+}
+
+__device__ __forceinline__ bool quant_fast_ok(float divisor, float rcp) {
+  return isfinite(divisor) && isfinite(rcp) && divisor >= 1.17549435e-38f && rcp >= 1.17549435e-38f;
+}
+
+// e4m3 pair with satfinite: RNE, then |y| > 448 -> 448 and NaN -> NaN, which
+// equals clamp(+-448) followed by the cast (ref.py:99).
+__device__ __forceinline__ uint32_t e4m3x2_sat(float lo, float hi) { return f2_to_e4m3x2(lo, hi); }
+
+// 16 values with the fast exact quotient; counts |x/divisor| > 448.
+__device__ __forceinline__ uint4 quantize16_fast(const float* x, float divisor, float rcp, bool fast_ok,
+                                                 uint32_t& sat) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float y0 = quant_quotient(x[4 * i + 0], divisor, rcp, fast_ok);
+    const float y1 = quant_quotient(x[4 * i + 1], divisor, rcp, fast_ok);
+    const float y2 = quant_quotient(x[4 * i + 2], divisor, rcp, fast_ok);
+    const float y3 = quant_quotient(x[4 * i + 3], divisor, rcp, fast_ok);
+    sat += (fabsf(y0) > FP8_MAX) + (fabsf(y1) > FP8_MAX) + (fabsf(y2) > FP8_MAX) + (fabsf(y3) > FP8_MAX);
+    w[i] = e4m3x2_sat(y0, y1) | (e4m3x2_sat(y2, y3) << 16);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// ---------------------------------------------------------------- tensor-core helpers (mma.sync m16n8k16)
+// Fragment layout (g = lane/4, t4 = lane%4):
+//   A: a0 = (row g, k 2t4..+1), a1 = (row g+8, k 2t4..+1), a2 = (row g, k 2t4+8..+9), a3 = (row g+8, k 2t4+8..+9)
+//   B: b0 = (k 2t4..+1, col g), b1 = (k 2t4+8..+9, col g)
+//   C: c0,c1 = (row g, col 2t4..+1), c2,c3 = (row g+8, col 2t4..+1)
+__device__ __forceinline__ void mma16816(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// two e4m3 bytes (low byte = lower index) -> f16x2 (exact)
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t two_bytes) {
+  __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(two_bytes & 0xFFFFu), __NV_E4M3);
+  return uint32_t(h.x) | (uint32_t(h.y) << 16);
+}
+
+// bf16x2 -> f16x2 (RNE; exact for the normalised keys except magnitudes < 2^-14)
+__device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t w) {
+  const float2 f = bf16x2_to_f2(w);
+  return pack_f16x2(f.x, f.y);
+}
+
+__device__ __forceinline__ uint4 ldg_stream_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+
+__device__ __forceinline__ void mma16816_bf16(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// power of two p with max_abs * p in [2^13, 2^14) (1 when max_abs is 0 or not finite);
+// scaling f16 operands by it keeps them in the normal range without rounding
+__device__ __forceinline__ float pow2_scale_for(float max_abs) {
+  if (!(max_abs > 0.0f) || !isfinite(max_abs)) return 1.0f;
+  int e;
+  frexpf(max_abs, &e);  // max_abs in [2^(e-1), 2^e)
+  // clamped so that the scale itself stays a normal float (values below
+  // 2^-110 contribute nothing representable either way)
+  const int k = 14 - e;
+  return ldexpf(1.0f, k > 124 ? 124 : (k < -124 ? -124 : k));
+}
+
+
+// m16n8k32 with e4m3 A and B (A fragment: a0 = (row g, k 4t4..+3), a1 = (row g+8, ..),
+// a2 = (row g, k 16+4t4..+3), a3 = (row g+8, ..); B: b0 = (k 4t4..+3, col g), b1 = (k 16+4t4.., col g))
+__device__ __forceinline__ void mma16832_e4m3(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  return uint32_t(f_to_bf16(lo)) | (uint32_t(f_to_bf16(hi)) << 16);
+}
+
+// e4m3 byte -> float (exact)
+__device__ __forceinline__ float e4m3_to_f(uint32_t byte) {
+  const uint32_t h = e4m3x2_to_f16x2(byte & 0xFFu);
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(h & 0xFFFFu)));
+}
+
+
+// ---------------------------------------------------------------- cp.async (LDGSTS)
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async8(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 }  // namespace gdnr

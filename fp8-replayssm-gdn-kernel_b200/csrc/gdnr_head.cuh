@@ -1,0 +1,530 @@
+// Per-head compute of the FP8 replay step on sm_100a (rings of L <= 16), shared
+// by the one-CTA-per-head kernel (gdnr_step2.cu) and the persistent pipelined
+// kernel (gdnr_step3.cu).  Everything here works on one value head whose
+// checkpoint tile, ring and query already sit in shared memory; `Sync` is
+// the barrier of the 4 warps that own the head (a CTA barrier or a named
+// barrier of one pipeline).
+//
+//  * head_nonflush: backward replay of the ring
+//    (prototype/gdn_replayssm_fp8_kernel.py:121-176) in Gram form
+//        G = K [K;q]^T (bf16 MMA),  c_t = beta_t (d_t kq_t - sum_{j>t} c_j M[t][j]),
+//        T = a_{n-1} q - sum_j c_j a_j k_j,
+//    then the readout o = scale (S_fp8 . T) + sum_t c_t v_t on tensor cores:
+//    S_fp8 straight from the e4m3 tile against T split into five
+//    power-of-two-scaled e4m3 terms (m16n8k32 e4m3 MMA), plus V^T c as a bf16
+//    MMA into spare accumulator columns.
+//  * head_flush: the state rebuild of the ring in WY/Gram form
+//        E = S0 [K;q]^T,  r_t = a_t E_t + sum_{j<t} u_j M[j][t],
+//        u_t = beta_t (v_t - r_t),  S_L = a_{n-1} S0 + W K,  W_t = u_t d_t
+//    (algebraically the token loop of ref.py:137-163), the readout, and the
+//    vblock32 re-quantisation (ref.py:40-106) written back in place.
+// a_t = prod_{m<=t} gamma_m, d_t = prod_{t<m<n} gamma_m, gamma_m = exp(g_m),
+// M[j][t] = prod_{j<m<=t} gamma_m (k_j . k_t).
+#pragma once
+
+#include "gdnr_device.cuh"
+
+namespace gdnr {
+
+constexpr float KSCALE_H = 0.08838834764831845f;  // 128^-1/2 (kern.py:175)
+constexpr int KSTR = 136;                          // padded k-ring row (bf16): 272 B
+constexpr int KTSTR = 24;                          // K^T row (f16): 48 B, 16 used
+constexpr float KPOW = 256.0f;                     // f16 operand scale of k and q
+constexpr float INV_KPOW = 1.0f / 256.0f;
+constexpr int T8STR = 144;                         // e4m3 T-term row (bytes), padded
+constexpr uint32_t KX_BYTES = (18u * KSTR * 2 > 128u * KTSTR * 2) ? 18u * KSTR * 2 : 128u * KTSTR * 2;
+
+struct CtaSync {
+  __device__ __forceinline__ void operator()() const { __syncthreads(); }
+};
+
+struct GroupSync {  // named barrier of the 128 threads of one pipeline
+  int id;
+  __device__ __forceinline__ void operator()() const { asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory"); }
+};
+
+// The head's inputs in shared memory.
+struct HeadTile {
+  uint8_t* s0;   // [rows][128 B] e4m3, 16-byte chunk c of row r at c ^ (r & 7)
+  uint16_t* kr;  // [16][KSTR] bf16 keys of the ring
+  uint16_t* vr;  // [16][vstr] bf16 value rows of the ring (this tile's rows)
+  float* gr;     // [16] g_t
+  float* br;     // [16] beta_t
+  int vstr;
+};
+
+// Working space of one head computation in shared memory.
+struct HeadScratch {
+  float* qs;      // [128] q (f32)
+  float* cf;      // [16]
+  uint16_t* cb;   // [48] c split into 3 bf16
+  uint16_t* qb;   // [384] q split into 3 bf16
+  uint8_t* t8;    // [8][T8STR] T split into e4m3 terms
+  float* gram;    // [16][24]
+  float* mg;      // [16][16]
+  float* ad;      // [64] gamma, a, d, kq
+  uint16_t* kx;   // KX_BYTES: k16 / K^T staging of the flush
+  float* ow;      // [warps][32] output rows
+  float* misc;    // [4]
+};
+
+__device__ __forceinline__ uint32_t s0_off(int r, int c) { return uint32_t(r) * 128u + 16u * uint32_t(c ^ (r & 7)); }
+
+// A fragment (f16) of checkpoint rows rbase..rbase+15, key step ks (16 key columns)
+__device__ __forceinline__ void s0_afrag_f16(const uint8_t* s0, int rbase, int ks, int g8, int t4, uint32_t* a) {
+  const int r0 = rbase + g8, r1 = r0 + 8;
+  const uint8_t* p0 = s0 + uint32_t(r0) * 128u + 16u * uint32_t(ks ^ (r0 & 7));
+  const uint8_t* p1 = s0 + uint32_t(r1) * 128u + 16u * uint32_t(ks ^ (r1 & 7));
+  a[0] = e4m3x2_to_f16x2(*reinterpret_cast<const uint16_t*>(p0 + 2 * t4));
+  a[1] = e4m3x2_to_f16x2(*reinterpret_cast<const uint16_t*>(p1 + 2 * t4));
+  a[2] = e4m3x2_to_f16x2(*reinterpret_cast<const uint16_t*>(p0 + 8 + 2 * t4));
+  a[3] = e4m3x2_to_f16x2(*reinterpret_cast<const uint16_t*>(p1 + 8 + 2 * t4));
+}
+
+// ============================================================== non-flush
+// n: ring slots replayed (0..16); sc: the vblock scale of this warp's rows.
+// Writes X.ow[32 warp + i] = output row i of the warp's vblock (already * K^-1/2).
+template <class Sync>
+__device__ __forceinline__ void head_nonflush(const HeadTile& T, const HeadScratch& X, int n, float sc, int warp,
+                                              int lane, Sync sync) {
+  const int g8 = lane >> 2, t4 = lane & 3;
+  const int VSTR = T.vstr;
+  const uint16_t* kr_s = T.kr;
+  const uint16_t* vr_s = T.vr;
+  float* gam_s = X.ad;
+  float* mgT = X.mg;  // mgT[t][i] = M[i][t], i < t
+  if (warp == 0) {
+    // q split into three bf16 rows (exact for bf16 q, ~24 bits for f32 q)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float q = X.qs[lane * 4 + i];
+      const uint16_t q0 = f_to_bf16(q);
+      const float r1 = q - bf16_to_f(q0);
+      const uint16_t q1 = f_to_bf16(r1);
+      const uint16_t q2 = f_to_bf16(r1 - bf16_to_f(q1));
+      X.qb[lane * 4 + i] = q0;
+      X.qb[128 + lane * 4 + i] = q1;
+      X.qb[256 + lane * 4 + i] = q2;
+    }
+    if (lane < 16) gam_s[lane] = lane < n ? expf(T.gr[lane]) : 0.0f;
+    __syncwarp();
+    // G = K [K; q]^T by bf16 MMA from the ring (tokens >= n masked to zero)
+    float gacc[3][4];
+#pragma unroll
+    for (int nt = 0; nt < 3; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) gacc[nt][i] = 0.0f;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      const int col = 16 * ks + 2 * t4;
+      uint32_t a[4];
+      a[0] = g8 < n ? *reinterpret_cast<const uint32_t*>(kr_s + g8 * KSTR + col) : 0u;
+      a[1] = g8 + 8 < n ? *reinterpret_cast<const uint32_t*>(kr_s + (g8 + 8) * KSTR + col) : 0u;
+      a[2] = g8 < n ? *reinterpret_cast<const uint32_t*>(kr_s + g8 * KSTR + col + 8) : 0u;
+      a[3] = g8 + 8 < n ? *reinterpret_cast<const uint32_t*>(kr_s + (g8 + 8) * KSTR + col + 8) : 0u;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const int tok = 8 * nt + g8;
+        const uint32_t b0 = tok < n ? *reinterpret_cast<const uint32_t*>(kr_s + tok * KSTR + col) : 0u;
+        const uint32_t b1 = tok < n ? *reinterpret_cast<const uint32_t*>(kr_s + tok * KSTR + col + 8) : 0u;
+        mma16816_bf16(gacc[nt], a, b0, b1);
+      }
+      const uint32_t b0 = g8 < 3 ? *reinterpret_cast<const uint32_t*>(X.qb + g8 * 128 + col) : 0u;
+      const uint32_t b1 = g8 < 3 ? *reinterpret_cast<const uint32_t*>(X.qb + g8 * 128 + col + 8) : 0u;
+      mma16816_bf16(gacc[2], a, b0, b1);
+    }
+#pragma unroll
+    for (int nt = 0; nt < 3; ++nt) {
+      X.gram[g8 * 24 + 8 * nt + 2 * t4] = gacc[nt][0];
+      X.gram[g8 * 24 + 8 * nt + 2 * t4 + 1] = gacc[nt][1];
+      X.gram[(g8 + 8) * 24 + 8 * nt + 2 * t4] = gacc[nt][2];
+      X.gram[(g8 + 8) * 24 + 8 * nt + 2 * t4 + 1] = gacc[nt][3];
+    }
+    __syncwarp();
+    float a_j = 1.0f, d_j = 1.0f, kq_j = 0.0f;
+    if (lane < n) {
+      const int j = lane;
+      for (int m = 0; m <= j; ++m) a_j *= gam_s[m];
+      float pm = 1.0f;
+      for (int t = j + 1; t < n; ++t) {
+        pm *= gam_s[t];
+        mgT[t * 16 + j] = pm * X.gram[j * 24 + t];
+      }
+      d_j = pm;
+      kq_j = X.gram[j * 24 + 16] + X.gram[j * 24 + 17] + X.gram[j * 24 + 18];
+    }
+    __syncwarp();
+    // triangular solve, t = n-1 .. 0: c_t = beta_t (d_t kq_t - sum_{j>t} c_j M[t][j])
+    float acc = d_j * kq_j, cval = 0.0f;
+    for (int t = n - 1; t >= 0; --t) {
+      const float ct = __shfl_sync(0xffffffffu, T.br[t] * acc, t);
+      if (lane == t) cval = ct;
+      if (lane < t) acc = fmaf(-ct, mgT[t * 16 + lane], acc);
+    }
+    // T_0 = a_{n-1} q - sum_j c_j a_j k_j  (lane: elements 4 lane .. 4 lane + 3)
+    const float alast = n > 0 ? __shfl_sync(0xffffffffu, a_j, n - 1) : 1.0f;
+    float Tq[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) Tq[i] = alast * X.qs[lane * 4 + i];
+    const float wj = cval * a_j;
+    for (int j = 0; j < n; ++j) {
+      const float w = __shfl_sync(0xffffffffu, wj, j);
+      const uint2 kw = *reinterpret_cast<const uint2*>(kr_s + j * KSTR + lane * 4);
+      const float2 k01 = bf16x2_to_f2(kw.x), k23 = bf16x2_to_f2(kw.y);
+      Tq[0] = fmaf(-w, k01.x, Tq[0]);
+      Tq[1] = fmaf(-w, k01.y, Tq[1]);
+      Tq[2] = fmaf(-w, k23.x, Tq[2]);
+      Tq[3] = fmaf(-w, k23.y, Tq[3]);
+    }
+    // c -> [c_hi; c_mid; c_lo] bf16
+    if (lane < 16) {
+      const float c = lane < n ? cval : 0.0f;
+      const uint16_t chi = f_to_bf16(c);
+      const float r1 = c - bf16_to_f(chi);
+      const uint16_t cmid = f_to_bf16(r1);
+      const uint16_t clo = f_to_bf16(r1 - bf16_to_f(cmid));
+      X.cb[lane] = chi;
+      X.cb[16 + lane] = cmid;
+      X.cb[32 + lane] = clo;
+    }
+    // T -> 5 e4m3 terms: T sigma = sum_i term_i 16^-i, max |T sigma| in [128, 256)
+    float m = fmaxf(fmaxf(fabsf(Tq[0]), fabsf(Tq[1])), fmaxf(fabsf(Tq[2]), fabsf(Tq[3])));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float sig = pow2_scale_for(m) * (1.0f / 64.0f);
+    float x[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) x[i] = Tq[i] * sig;
+#pragma unroll
+    for (int j = 0; j < 5; ++j) {
+      const uint32_t p01 = e4m3x2_sat(x[0], x[1]);
+      const uint32_t p23 = e4m3x2_sat(x[2], x[3]);
+      *reinterpret_cast<uint32_t*>(X.t8 + j * T8STR + lane * 4) = p01 | (p23 << 16);
+      const uint32_t h01 = e4m3x2_to_f16x2(p01), h23 = e4m3x2_to_f16x2(p23);
+      const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&h01));
+      const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&h23));
+      x[0] = (x[0] - f01.x) * 16.0f;
+      x[1] = (x[1] - f01.y) * 16.0f;
+      x[2] = (x[2] - f23.x) * 16.0f;
+      x[3] = (x[3] - f23.y) * 16.0f;
+    }
+#pragma unroll
+    for (int j = 5; j < 8; ++j) *reinterpret_cast<uint32_t*>(X.t8 + j * T8STR + lane * 4) = 0u;
+    if (lane == 0) X.misc[0] = 1.0f / sig;
+  }
+  sync();
+  // readout on tensor cores.  Columns 0..4: S_fp8 . term_j (e4m3 MMA); 5..7: V^T . c (bf16 MMA)
+  uint32_t bt[4][2];
+#pragma unroll
+  for (int ks = 0; ks < 4; ++ks) {
+    bt[ks][0] = *reinterpret_cast<const uint32_t*>(X.t8 + g8 * T8STR + 32 * ks + 4 * t4);
+    bt[ks][1] = *reinterpret_cast<const uint32_t*>(X.t8 + g8 * T8STR + 32 * ks + 16 + 4 * t4);
+  }
+  const bool rcol = g8 >= 5;
+  const uint32_t rb0 = rcol ? *reinterpret_cast<const uint32_t*>(X.cb + (g8 - 5) * 16 + 2 * t4) : 0u;
+  const uint32_t rb1 = rcol ? *reinterpret_cast<const uint32_t*>(X.cb + (g8 - 5) * 16 + 8 + 2 * t4) : 0u;
+  // column weights: t4 = 0 -> terms 0,1; 1 -> terms 2,3; 2 -> term 4, ring; 3 -> ring, ring
+  const float wbase = X.misc[0] * sc;
+  const float w0 = t4 == 0 ? wbase : (t4 == 1 ? wbase * (1.0f / 256.0f) : (t4 == 2 ? wbase * (1.0f / 65536.0f) : 1.0f));
+  const float w1 = t4 == 0 ? wbase * (1.0f / 16.0f) : (t4 == 1 ? wbase * (1.0f / 4096.0f) : 1.0f);
+  const int rw0 = 32 * warp;
+  float* ow = X.ow + 32 * warp;
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt) {
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    const int r0 = rw0 + 16 * mt + g8, r1 = r0 + 8;
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      uint32_t a[4];
+      a[0] = *reinterpret_cast<const uint32_t*>(T.s0 + s0_off(r0, 2 * ks) + 4 * t4);
+      a[1] = *reinterpret_cast<const uint32_t*>(T.s0 + s0_off(r1, 2 * ks) + 4 * t4);
+      a[2] = *reinterpret_cast<const uint32_t*>(T.s0 + s0_off(r0, 2 * ks + 1) + 4 * t4);
+      a[3] = *reinterpret_cast<const uint32_t*>(T.s0 + s0_off(r1, 2 * ks + 1) + 4 * t4);
+      mma16832_e4m3(acc, a, bt[ks][0], bt[ks][1]);
+    }
+    {
+      const int t0 = 2 * t4, t1 = 2 * t4 + 8;
+      uint32_t a[4];
+      a[0] = (t0 < n ? uint32_t(vr_s[t0 * VSTR + r0]) : 0u) | (t0 + 1 < n ? uint32_t(vr_s[(t0 + 1) * VSTR + r0]) << 16 : 0u);
+      a[1] = (t0 < n ? uint32_t(vr_s[t0 * VSTR + r1]) : 0u) | (t0 + 1 < n ? uint32_t(vr_s[(t0 + 1) * VSTR + r1]) << 16 : 0u);
+      a[2] = (t1 < n ? uint32_t(vr_s[t1 * VSTR + r0]) : 0u) | (t1 + 1 < n ? uint32_t(vr_s[(t1 + 1) * VSTR + r0]) << 16 : 0u);
+      a[3] = (t1 < n ? uint32_t(vr_s[t1 * VSTR + r1]) : 0u) | (t1 + 1 < n ? uint32_t(vr_s[(t1 + 1) * VSTR + r1]) << 16 : 0u);
+      mma16816_bf16(acc, a, rb0, rb1);
+    }
+    float o0 = fmaf(acc[1], w1, acc[0] * w0);
+    float o1 = fmaf(acc[3], w1, acc[2] * w0);
+    o0 += __shfl_xor_sync(0xffffffffu, o0, 1);
+    o1 += __shfl_xor_sync(0xffffffffu, o1, 1);
+    o0 += __shfl_xor_sync(0xffffffffu, o0, 2);
+    o1 += __shfl_xor_sync(0xffffffffu, o1, 2);
+    if (t4 == 0) {
+      ow[16 * mt + g8] = o0 * KSCALE_H;
+      ow[16 * mt + g8 + 8] = o1 * KSCALE_H;
+    }
+  }
+  __syncwarp();
+}
+
+// ============================================================== flush
+// The checkpoint tile is overwritten in shared memory and copied to
+// ck_tile_global (row 0 of this tile in the global checkpoint); the warp's
+// new scale goes to scale_ptr[sc_index] (f16 or f32 holding the f16 value).
+// gtid / nthreads: thread index within / size of the group owning the head.
+template <class Sync>
+__device__ __forceinline__ void head_flush(const HeadTile& T, const HeadScratch& X, int n, float sc, int quant_rounded,
+                                           uint8_t* ck_tile_global, void* scale_ptr, int64_t sc_index, int sc_dt,
+                                           int warp, int lane, int gtid, int nthreads, Sync sync) {
+  const int g8 = lane >> 2, t4 = lane & 3, c8 = lane & 7;
+  const int VSTR = T.vstr;
+  const uint16_t* kr_s = T.kr;
+  const uint16_t* vr_s = T.vr;
+  uint8_t* s0 = T.s0;
+  float* gram = X.gram;
+  float* mg = X.mg;
+  float* gam_s = X.ad;
+  float* av = gam_s + 16;
+  float* dv = gam_s + 32;
+  float* kqv = gam_s + 48;
+  uint16_t* k16 = X.kx;
+  const int rw0 = 32 * warp;
+  float* ow = X.ow + 32 * warp;
+  // k16 = [K; q_hi; q_lo] * 256 as f16 (rows >= n zero); gamma_t
+  for (int i = gtid; i < 18 * 64; i += nthreads) {
+    const int row = i >> 6, col = 2 * (i & 63);
+    float x0, x1;
+    if (row < 16) {
+      const uint32_t w = *reinterpret_cast<const uint32_t*>(kr_s + row * KSTR + col);
+      const float2 f = bf16x2_to_f2(w);
+      x0 = row < n ? f.x : 0.0f;
+      x1 = row < n ? f.y : 0.0f;
+    } else {
+      const float q0 = X.qs[col], q1 = X.qs[col + 1];
+      const float h0 = __half2float(__float2half_rn(q0 * KPOW)) * INV_KPOW;
+      const float h1 = __half2float(__float2half_rn(q1 * KPOW)) * INV_KPOW;
+      x0 = row == 16 ? h0 : q0 - h0;
+      x1 = row == 16 ? h1 : q1 - h1;
+    }
+    *reinterpret_cast<uint32_t*>(k16 + row * KSTR + col) = pack_f16x2(x0 * KPOW, x1 * KPOW);
+  }
+  if (gtid < 16) gam_s[gtid] = gtid < n ? expf(T.gr[gtid]) : 0.0f;
+  sync();
+  // Gram (warp 0): [K][K;q]^T -> G[t][s] (s < 16), kq_t; then decay products
+  if (warp == 0) {
+    float gacc[3][4];
+#pragma unroll
+    for (int nt = 0; nt < 3; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) gacc[nt][i] = 0.0f;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      const int col = 16 * ks + 2 * t4;
+      uint32_t a[4];
+      a[0] = *reinterpret_cast<const uint32_t*>(k16 + g8 * KSTR + col);
+      a[1] = *reinterpret_cast<const uint32_t*>(k16 + (g8 + 8) * KSTR + col);
+      a[2] = *reinterpret_cast<const uint32_t*>(k16 + g8 * KSTR + col + 8);
+      a[3] = *reinterpret_cast<const uint32_t*>(k16 + (g8 + 8) * KSTR + col + 8);
+#pragma unroll
+      for (int nt = 0; nt < 3; ++nt) {
+        const int nrow = 8 * nt + g8;  // rows 16,17 = q_hi, q_lo; >= 18 zero
+        const uint32_t b0 = nrow < 18 ? *reinterpret_cast<const uint32_t*>(k16 + nrow * KSTR + col) : 0u;
+        const uint32_t b1 = nrow < 18 ? *reinterpret_cast<const uint32_t*>(k16 + nrow * KSTR + col + 8) : 0u;
+        mma16816(gacc[nt], a, b0, b1);
+      }
+    }
+    const float gs = INV_KPOW * INV_KPOW;
+#pragma unroll
+    for (int nt = 0; nt < 3; ++nt) {
+      gram[g8 * 24 + 8 * nt + 2 * t4] = gacc[nt][0] * gs;
+      gram[g8 * 24 + 8 * nt + 2 * t4 + 1] = gacc[nt][1] * gs;
+      gram[(g8 + 8) * 24 + 8 * nt + 2 * t4] = gacc[nt][2] * gs;
+      gram[(g8 + 8) * 24 + 8 * nt + 2 * t4 + 1] = gacc[nt][3] * gs;
+    }
+    __syncwarp();
+    if (lane < 16) {
+      const int j = lane;
+      float pa = 1.0f, pd = 1.0f;
+      for (int m = 0; m <= j && m < n; ++m) pa *= gam_s[m];
+      for (int m = j + 1; m < n; ++m) pd *= gam_s[m];
+      av[j] = j < n ? pa : 0.0f;
+      dv[j] = j < n ? pd : 0.0f;
+      kqv[j] = j < n ? gram[j * 24 + 16] + gram[j * 24 + 17] : 0.0f;
+      float pm = 1.0f;
+      for (int t = 0; t < 16; ++t) {
+        float mm = 0.0f;
+        if (t > j && t < n) {
+          pm *= gam_s[t];
+          mm = pm * gram[j * 24 + t];
+        }
+        mg[j * 16 + t] = mm;
+      }
+    }
+  }
+  sync();
+  // per m-tile: E, recurrence, W (A fragments of the S_L product)
+  const float alast = n > 0 ? av[n - 1] : 1.0f;
+  const float asc = alast * sc;
+  uint32_t ahi[2][4], alo[2][4];
+  float wpow[2];
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt) {
+    float e[3][4];
+#pragma unroll
+    for (int nt = 0; nt < 3; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) e[nt][i] = 0.0f;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      uint32_t a[4];
+      s0_afrag_f16(s0, rw0 + 16 * mt, ks, g8, t4, a);
+      const int col = 16 * ks + 2 * t4;
+#pragma unroll
+      for (int nt = 0; nt < 3; ++nt) {
+        const int nrow = 8 * nt + g8;
+        const uint32_t b0 = nrow < 18 ? *reinterpret_cast<const uint32_t*>(k16 + nrow * KSTR + col) : 0u;
+        const uint32_t b1 = nrow < 18 ? *reinterpret_cast<const uint32_t*>(k16 + nrow * KSTR + col + 8) : 0u;
+        mma16816(e[nt], a, b0, b1);
+      }
+    }
+    // lane (g8, t4) holds rows rw0+16mt+g8 (+8) and tokens slot s -> t = 8(s>>1) + 2t4 + (s&1)
+    float u[2][4], racc[2][4];
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+      for (int s = 0; s < 4; ++s) {
+        u[hf][s] = 0.0f;
+        racc[hf][s] = 0.0f;
+      }
+    const int quad = lane & ~3;
+    const float esc = sc * INV_KPOW;
+#pragma unroll
+    for (int t = 0; t < 16; ++t) {
+      if (t < n) {
+        const int owner = (t & 7) >> 1, slot = (t >> 3) * 2 + (t & 1);
+        const float at = av[t] * esc, bt = T.br[t];
+        const float2 m01 = *reinterpret_cast<const float2*>(mg + t * 16 + 2 * t4);
+        const float2 m23 = *reinterpret_cast<const float2*>(mg + t * 16 + 8 + 2 * t4);
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const int r = rw0 + 16 * mt + g8 + 8 * hf;
+          const float et = e[t >> 3][2 * hf + (t & 1)];
+          const float mine = bt * (bf16_to_f(vr_s[t * VSTR + r]) - fmaf(at, et, racc[hf][slot]));
+          u[hf][slot] = (t4 == owner) ? mine : u[hf][slot];
+          const float ut = __shfl_sync(0xffffffffu, mine, quad | owner);
+          racc[hf][0] = fmaf(ut, m01.x, racc[hf][0]);
+          racc[hf][1] = fmaf(ut, m01.y, racc[hf][1]);
+          racc[hf][2] = fmaf(ut, m23.x, racc[hf][2]);
+          racc[hf][3] = fmaf(ut, m23.y, racc[hf][3]);
+        }
+      }
+    }
+    // W = u d; output o = asc (S0 q) + sum_t W_t kq_t
+    float wv[2][4];
+    float wmax = 0.0f;
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      float o = 0.0f;
+#pragma unroll
+      for (int s = 0; s < 4; ++s) {
+        const int ts = 8 * (s >> 1) + 2 * t4 + (s & 1);
+        const float w = ts < n ? u[hf][s] * dv[ts] : 0.0f;
+        wv[hf][s] = w;
+        wmax = fmaxf(wmax, fabsf(w));
+        o = fmaf(w, ts < n ? kqv[ts] : 0.0f, o);
+      }
+      // S0 q: n-tile 2, columns 16 (q_hi) and 17 (q_lo) -> lane t4 == 0, c0 + c1 / c2 + c3
+      if (t4 == 0) o = fmaf(asc * INV_KPOW, e[2][2 * hf] + e[2][2 * hf + 1], o);
+      o += __shfl_xor_sync(0xffffffffu, o, 1);
+      o += __shfl_xor_sync(0xffffffffu, o, 2);
+      if (t4 == 0) ow[16 * mt + g8 + 8 * hf] = o * KSCALE_H;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) wmax = fmaxf(wmax, __shfl_xor_sync(0xffffffffu, wmax, o));
+    const float wp = pow2_scale_for(wmax);
+    wpow[mt] = wp;
+    float hi[2][4];
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+      for (int s = 0; s < 4; ++s) hi[hf][s] = __half2float(__float2half_rn(wv[hf][s] * wp));
+    ahi[mt][0] = pack_f16x2(hi[0][0], hi[0][1]);
+    ahi[mt][1] = pack_f16x2(hi[1][0], hi[1][1]);
+    ahi[mt][2] = pack_f16x2(hi[0][2], hi[0][3]);
+    ahi[mt][3] = pack_f16x2(hi[1][2], hi[1][3]);
+    alo[mt][0] = pack_f16x2(wv[0][0] * wp - hi[0][0], wv[0][1] * wp - hi[0][1]);
+    alo[mt][1] = pack_f16x2(wv[1][0] * wp - hi[1][0], wv[1][1] * wp - hi[1][1]);
+    alo[mt][2] = pack_f16x2(wv[0][2] * wp - hi[0][2], wv[0][3] * wp - hi[0][3]);
+    alo[mt][3] = pack_f16x2(wv[1][2] * wp - hi[1][2], wv[1][3] * wp - hi[1][3]);
+  }
+  // K^T * 256 as f16 (B operand of S_L), reusing the k16 region
+  sync();
+  uint16_t* kt = k16;
+  for (int i = gtid; i < 128 * 8; i += nthreads) {
+    const int col = i >> 3, t = 2 * (i & 7);
+    const float k0 = t < n ? bf16_to_f(kr_s[t * KSTR + col]) : 0.0f;
+    const float k1 = t + 1 < n ? bf16_to_f(kr_s[(t + 1) * KSTR + col]) : 0.0f;
+    *reinterpret_cast<uint32_t*>(kt + col * KTSTR + t) = pack_f16x2(k0 * KPOW, k1 * KPOW);
+  }
+  sync();
+  // S_L = asc S0 + (W K); pass 0 = amax, pass 1 = quantise into the tile
+  float amax = 0.0f, rcp = 1.0f;
+  VScale vs;
+  vs.divisor = 1.0f;
+  vs.stored = __float2half_rn(1.0f);
+  bool fast = false;
+  const float dsc0 = INV_KPOW / wpow[0], dsc1 = INV_KPOW / wpow[1];
+#pragma unroll 1
+  for (int pass = 0; pass < 2; ++pass) {
+    if (pass == 1) {
+      amax = warp_max_nan(amax);
+      vs = vblock_scale(amax, quant_rounded);
+      rcp = __fdiv_rn(1.0f, vs.divisor);
+      fast = quant_fast_ok(vs.divisor, rcp);
+    }
+#pragma unroll 2
+    for (int nt = 0; nt < 16; ++nt) {
+      const int col = 8 * nt + g8;
+      const uint32_t b0 = *reinterpret_cast<const uint32_t*>(kt + col * KTSTR + 2 * t4);
+      const uint32_t b1 = *reinterpret_cast<const uint32_t*>(kt + col * KTSTR + 8 + 2 * t4);
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        mma16816(acc, ahi[mt], b0, b1);
+        mma16816(acc, alo[mt], b0, b1);
+        const float dsc = mt == 0 ? dsc0 : dsc1;
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const int r = rw0 + 16 * mt + g8 + 8 * hf;
+          const int cc = 8 * nt + 2 * t4;  // even column pair (cc, cc+1)
+          uint8_t* sp = s0 + s0_off(r, cc >> 4) + (cc & 15);
+          const uint32_t h2 = e4m3x2_to_f16x2(*reinterpret_cast<const uint16_t*>(sp));
+          const float2 sf = __half22float2(*reinterpret_cast<const __half2*>(&h2));
+          const float x0 = fmaf(acc[2 * hf], dsc, asc * sf.x);
+          const float x1 = fmaf(acc[2 * hf + 1], dsc, asc * sf.y);
+          if (pass == 0) {
+            amax = fmax_nan(amax, fmax_nan(fabsf(x0), fabsf(x1)));
+          } else {
+            const float y0 = quant_quotient(x0, vs.divisor, rcp, fast);
+            const float y1 = quant_quotient(x1, vs.divisor, rcp, fast);
+            *reinterpret_cast<uint16_t*>(sp) = static_cast<uint16_t>(e4m3x2_sat(y0, y1));
+          }
+        }
+      }
+    }
+  }
+  __syncwarp();
+  // new checkpoint rows (coalesced 16-byte stores) and scale
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    const int r = rw0 + 4 * it + (lane >> 3);
+    *reinterpret_cast<uint4*>(ck_tile_global + r * 128 + c8 * 16) = *reinterpret_cast<const uint4*>(s0 + s0_off(r, c8));
+  }
+  if (lane == 0) {
+    if (sc_dt == GDNR_F16)
+      static_cast<__half*>(scale_ptr)[sc_index] = vs.stored;
+    else
+      static_cast<float*>(scale_ptr)[sc_index] = __half2float(vs.stored);
+  }
+  __syncwarp();
+}
+
+}  // namespace gdnr

@@ -101,6 +101,13 @@ __host__ __device__ inline SmemLayout step_smem_layout(int G, int L, int rows, i
 constexpr uint32_t MAX_DYN_SMEM = 227u * 1024u;
 
 cudaError_t launch_step(const StepParams& p, bool fused, bool f32ck, int group, cudaStream_t stream);
+// B200 path for E4M3 checkpoints and rings of L <= 16 (one CTA per value head)
+cudaError_t launch_step2(const StepParams& p, bool fused, cudaStream_t stream);
+constexpr int STEP2_MAX_L = 16;
+// persistent pipelined path (one CTA per SM): E4M3, L <= 16, whole heads,
+// f32 gates, 16-byte aligned rows; otherwise launch_step2 / launch_step
+bool step3_eligible(const StepParams& p, bool fused, bool f32ck);
+cudaError_t launch_step3(const StepParams& p, bool fused, cudaStream_t stream);
 
 // ---------------------------------------------------------------- codec kernel
 struct CodecParams {
