@@ -225,6 +225,16 @@ int validate_out(const gdnr_tensor& out, StepParams& p) {
   return GDNR_OK;
 }
 
+int check_launch_opts(int32_t hint, int32_t flags, StepParams& p) {
+  if (hint != GDNR_FLUSH_AUTO && hint != GDNR_FLUSH_NONE && hint != GDNR_FLUSH_ALL)
+    return set_error(GDNR_ERR_ARG, "flush_hint must be GDNR_FLUSH_AUTO, _NONE or _ALL (got %d)", hint);
+  if (flags & ~GDNR_LAUNCH_PDL) return set_error(GDNR_ERR_ARG, "unknown launch_flags bits 0x%x", flags);
+  p.flush_hint = hint;
+  p.pdl = (flags & GDNR_LAUNCH_PDL) ? 1 : 0;
+  p.head_filter = 0;
+  return GDNR_OK;
+}
+
 // Picks the row tile: the requested one, shrunk until the CTA's shared
 // memory fits (only the float32 checkpoint variant ever needs that).
 int pick_rows(int requested, int group, int L, bool f32ck, int& rows) {
@@ -289,6 +299,7 @@ int gdnr_replay(const gdnr_replay_args* a, void* stream) {
   p.quant_rounded = a->quant_divisor;
   p.err = a->error_flag ? a->error_flag : default_error_word();
   if (!p.err) return set_error(GDNR_ERR_CUDA, "no device error word available");
+  CHECK(check_launch_opts(a->flush_hint, a->launch_flags, p));
   if (p.B == 0) return GDNR_OK;
   return cuda_status(launch_step(p, false, f32ck, group, static_cast<cudaStream_t>(stream)), "gdnr_replay launch");
 }
@@ -353,6 +364,7 @@ int gdnr_fused_step(const gdnr_step_args* a, void* stream) {
   p.quant_rounded = a->quant_divisor;
   p.err = a->error_flag ? a->error_flag : default_error_word();
   if (!p.err) return set_error(GDNR_ERR_CUDA, "no device error word available");
+  CHECK(check_launch_opts(a->flush_hint, a->launch_flags, p));
   if (p.B == 0) return GDNR_OK;
   return cuda_status(launch_step(p, true, f32ck, group, static_cast<cudaStream_t>(stream)), "gdnr_fused_step launch");
 }

@@ -81,6 +81,11 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   return false;
 }
 
+// Programmatic dependent launch: wait for the preceding grid's memory /
+// allow the next grid to start its pre-wait prologue.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Global -> shared bulk copy (untiled TMA).  dst/src 16-byte aligned,
 // bytes a multiple of 16.  Completion is signalled on `bar` as tx bytes.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {

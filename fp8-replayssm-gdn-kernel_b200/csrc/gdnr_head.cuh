@@ -1,6 +1,6 @@
-// Per-head compute of the FP8 replay step on sm_100a (rings of L <= 16), shared
-// by the one-CTA-per-head kernel (gdnr_step2.cu) and the persistent pipelined
-// kernel (gdnr_step3.cu).  Everything here works on one value head whose
+// Per-head compute of the FP8 replay step on sm_100a (rings of L <= 16) used
+// by the one-CTA-per-head kernel (gdnr_step2.cu; constants shared with the
+// persistent kernel gdnr_step5.cu).  Everything here works on one value head whose
 // checkpoint tile, ring and query already sit in shared memory; `Sync` is
 // the barrier of the 4 warps that own the head (a CTA barrier or a named
 // barrier of one pipeline).
@@ -82,184 +82,211 @@ __device__ __forceinline__ void s0_afrag_f16(const uint8_t* s0, int rbase, int k
 }
 
 // ============================================================== non-flush
+// Backward chain of one head in Gram form (one warp).  n: ring slots replayed.
+// Leaves in X: t8 (T as five e4m3 terms), cb (c as three bf16), misc[0] = 1/sigma.
+__device__ __forceinline__ void head_chain(const HeadTile& T, const HeadScratch& X, int n, int lane) {
+  const int g8 = lane >> 2, t4 = lane & 3;
+  const uint16_t* kr_s = T.kr;
+  float* gam_s = X.ad;
+  float* mgT = X.mg;  // mgT[t][i] = M[i][t], i < t
+  // q split into three bf16 rows (exact for bf16 q, ~24 bits for f32 q)
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float q = X.qs[lane * 4 + i];
+    const uint16_t q0 = f_to_bf16(q);
+    const float r1 = q - bf16_to_f(q0);
+    const uint16_t q1 = f_to_bf16(r1);
+    const uint16_t q2 = f_to_bf16(r1 - bf16_to_f(q1));
+    X.qb[lane * 4 + i] = q0;
+    X.qb[128 + lane * 4 + i] = q1;
+    X.qb[256 + lane * 4 + i] = q2;
+  }
+  if (lane < 16) gam_s[lane] = lane < n ? expf(T.gr[lane]) : 0.0f;
+  __syncwarp();
+  // G = K [K; q]^T by bf16 MMA from the ring (tokens >= n masked to zero)
+  float gacc[3][4];
+#pragma unroll
+  for (int nt = 0; nt < 3; ++nt)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) gacc[nt][i] = 0.0f;
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+    const int col = 16 * ks + 2 * t4;
+    uint32_t a[4];
+    a[0] = g8 < n ? *reinterpret_cast<const uint32_t*>(kr_s + g8 * KSTR + col) : 0u;
+    a[1] = g8 + 8 < n ? *reinterpret_cast<const uint32_t*>(kr_s + (g8 + 8) * KSTR + col) : 0u;
+    a[2] = g8 < n ? *reinterpret_cast<const uint32_t*>(kr_s + g8 * KSTR + col + 8) : 0u;
+    a[3] = g8 + 8 < n ? *reinterpret_cast<const uint32_t*>(kr_s + (g8 + 8) * KSTR + col + 8) : 0u;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const int tok = 8 * nt + g8;
+      const uint32_t b0 = tok < n ? *reinterpret_cast<const uint32_t*>(kr_s + tok * KSTR + col) : 0u;
+      const uint32_t b1 = tok < n ? *reinterpret_cast<const uint32_t*>(kr_s + tok * KSTR + col + 8) : 0u;
+      mma16816_bf16(gacc[nt], a, b0, b1);
+    }
+    const uint32_t b0 = g8 < 3 ? *reinterpret_cast<const uint32_t*>(X.qb + g8 * 128 + col) : 0u;
+    const uint32_t b1 = g8 < 3 ? *reinterpret_cast<const uint32_t*>(X.qb + g8 * 128 + col + 8) : 0u;
+    mma16816_bf16(gacc[2], a, b0, b1);
+  }
+#pragma unroll
+  for (int nt = 0; nt < 3; ++nt) {
+    X.gram[g8 * 24 + 8 * nt + 2 * t4] = gacc[nt][0];
+    X.gram[g8 * 24 + 8 * nt + 2 * t4 + 1] = gacc[nt][1];
+    X.gram[(g8 + 8) * 24 + 8 * nt + 2 * t4] = gacc[nt][2];
+    X.gram[(g8 + 8) * 24 + 8 * nt + 2 * t4 + 1] = gacc[nt][3];
+  }
+  __syncwarp();
+  float a_j = 1.0f, d_j = 1.0f, kq_j = 0.0f;
+  if (lane < n) {
+    const int j = lane;
+    for (int m = 0; m <= j; ++m) a_j *= gam_s[m];
+    float pm = 1.0f;
+    for (int t = j + 1; t < n; ++t) {
+      pm *= gam_s[t];
+      mgT[t * 16 + j] = pm * X.gram[j * 24 + t];
+    }
+    d_j = pm;
+    kq_j = X.gram[j * 24 + 16] + X.gram[j * 24 + 17] + X.gram[j * 24 + 18];
+  }
+  __syncwarp();
+  // triangular solve, t = n-1 .. 0: c_t = beta_t (d_t kq_t - sum_{j>t} c_j M[t][j])
+  float acc = d_j * kq_j, cval = 0.0f;
+  for (int t = n - 1; t >= 0; --t) {
+    const float ct = __shfl_sync(0xffffffffu, T.br[t] * acc, t);
+    if (lane == t) cval = ct;
+    if (lane < t) acc = fmaf(-ct, mgT[t * 16 + lane], acc);
+  }
+  // T_0 = a_{n-1} q - sum_j c_j a_j k_j  (lane: elements 4 lane .. 4 lane + 3)
+  const float alast = n > 0 ? __shfl_sync(0xffffffffu, a_j, n - 1) : 1.0f;
+  float Tq[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) Tq[i] = alast * X.qs[lane * 4 + i];
+  const float wj = cval * a_j;
+  for (int j = 0; j < n; ++j) {
+    const float w = __shfl_sync(0xffffffffu, wj, j);
+    const uint2 kw = *reinterpret_cast<const uint2*>(kr_s + j * KSTR + lane * 4);
+    const float2 k01 = bf16x2_to_f2(kw.x), k23 = bf16x2_to_f2(kw.y);
+    Tq[0] = fmaf(-w, k01.x, Tq[0]);
+    Tq[1] = fmaf(-w, k01.y, Tq[1]);
+    Tq[2] = fmaf(-w, k23.x, Tq[2]);
+    Tq[3] = fmaf(-w, k23.y, Tq[3]);
+  }
+  // c -> [c_hi; c_mid; c_lo] bf16
+  if (lane < 16) {
+    const float c = lane < n ? cval : 0.0f;
+    const uint16_t chi = f_to_bf16(c);
+    const float r1 = c - bf16_to_f(chi);
+    const uint16_t cmid = f_to_bf16(r1);
+    const uint16_t clo = f_to_bf16(r1 - bf16_to_f(cmid));
+    X.cb[lane] = chi;
+    X.cb[16 + lane] = cmid;
+    X.cb[32 + lane] = clo;
+  }
+  // T -> 5 e4m3 terms: T sigma = sum_i term_i 16^-i, max |T sigma| in [128, 256)
+  float m = fmaxf(fmaxf(fabsf(Tq[0]), fabsf(Tq[1])), fmaxf(fabsf(Tq[2]), fabsf(Tq[3])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const float sig = pow2_scale_for(m) * (1.0f / 64.0f);
+  float x[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) x[i] = Tq[i] * sig;
+#pragma unroll
+  for (int j = 0; j < 5; ++j) {
+    const uint32_t p01 = e4m3x2_sat(x[0], x[1]);
+    const uint32_t p23 = e4m3x2_sat(x[2], x[3]);
+    *reinterpret_cast<uint32_t*>(X.t8 + j * T8STR + lane * 4) = p01 | (p23 << 16);
+    const uint32_t h01 = e4m3x2_to_f16x2(p01), h23 = e4m3x2_to_f16x2(p23);
+    const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&h01));
+    const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&h23));
+    x[0] = (x[0] - f01.x) * 16.0f;
+    x[1] = (x[1] - f01.y) * 16.0f;
+    x[2] = (x[2] - f23.x) * 16.0f;
+    x[3] = (x[3] - f23.y) * 16.0f;
+  }
+#pragma unroll
+  for (int j = 5; j < 8; ++j) *reinterpret_cast<uint32_t*>(X.t8 + j * T8STR + lane * 4) = 0u;
+  if (lane == 0) X.misc[0] = 1.0f / sig;
+}
+
+// Readout of tile rows rbase..rbase+15 (one m-tile) from the chain results:
+// returns, in lanes with t4 == 0, o(row rbase+g8) in o0 and o(row rbase+g8+8)
+// in o1 (already * K^-1/2).  Columns 0..4: S_fp8 . term_j (e4m3 MMA);
+// 5..7: V^T . c (bf16 MMA).  bt/rb are the lane's B fragments (head_readout_frags).
+struct ReadoutFrags {
+  uint32_t bt[4][2];
+  uint32_t rb0, rb1;
+};
+
+__device__ __forceinline__ ReadoutFrags head_readout_frags(const HeadScratch& X, int lane) {
+  const int g8 = lane >> 2, t4 = lane & 3;
+  ReadoutFrags f;
+#pragma unroll
+  for (int ks = 0; ks < 4; ++ks) {
+    f.bt[ks][0] = g8 < 5 ? *reinterpret_cast<const uint32_t*>(X.t8 + g8 * T8STR + 32 * ks + 4 * t4) : 0u;
+    f.bt[ks][1] = g8 < 5 ? *reinterpret_cast<const uint32_t*>(X.t8 + g8 * T8STR + 32 * ks + 16 + 4 * t4) : 0u;
+  }
+  const bool rcol = g8 >= 5;
+  f.rb0 = rcol ? *reinterpret_cast<const uint32_t*>(X.cb + (g8 - 5) * 16 + 2 * t4) : 0u;
+  f.rb1 = rcol ? *reinterpret_cast<const uint32_t*>(X.cb + (g8 - 5) * 16 + 8 + 2 * t4) : 0u;
+  return f;
+}
+
+__device__ __forceinline__ void head_readout_mtile(const HeadTile& T, const ReadoutFrags& f, int n, float wsc,
+                                                   int rbase, int lane, float& o0, float& o1) {
+  const int g8 = lane >> 2, t4 = lane & 3;
+  const int VSTR = T.vstr;
+  const uint16_t* vr_s = T.vr;
+  // column weights: t4 = 0 -> terms 0,1; 1 -> terms 2,3; 2 -> term 4, ring; 3 -> ring, ring
+  const float w0 = t4 == 0 ? wsc : (t4 == 1 ? wsc * (1.0f / 256.0f) : (t4 == 2 ? wsc * (1.0f / 65536.0f) : 1.0f));
+  const float w1 = t4 == 0 ? wsc * (1.0f / 16.0f) : (t4 == 1 ? wsc * (1.0f / 4096.0f) : 1.0f);
+  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  const int r0 = rbase + g8, r1 = r0 + 8;
+#pragma unroll
+  for (int ks = 0; ks < 4; ++ks) {
+    uint32_t a[4];
+    a[0] = *reinterpret_cast<const uint32_t*>(T.s0 + s0_off(r0, 2 * ks) + 4 * t4);
+    a[1] = *reinterpret_cast<const uint32_t*>(T.s0 + s0_off(r1, 2 * ks) + 4 * t4);
+    a[2] = *reinterpret_cast<const uint32_t*>(T.s0 + s0_off(r0, 2 * ks + 1) + 4 * t4);
+    a[3] = *reinterpret_cast<const uint32_t*>(T.s0 + s0_off(r1, 2 * ks + 1) + 4 * t4);
+    mma16832_e4m3(acc, a, f.bt[ks][0], f.bt[ks][1]);
+  }
+  {
+    const int t0 = 2 * t4, t1 = 2 * t4 + 8;
+    uint32_t a[4];
+    a[0] = (t0 < n ? uint32_t(vr_s[t0 * VSTR + r0]) : 0u) | (t0 + 1 < n ? uint32_t(vr_s[(t0 + 1) * VSTR + r0]) << 16 : 0u);
+    a[1] = (t0 < n ? uint32_t(vr_s[t0 * VSTR + r1]) : 0u) | (t0 + 1 < n ? uint32_t(vr_s[(t0 + 1) * VSTR + r1]) << 16 : 0u);
+    a[2] = (t1 < n ? uint32_t(vr_s[t1 * VSTR + r0]) : 0u) | (t1 + 1 < n ? uint32_t(vr_s[(t1 + 1) * VSTR + r0]) << 16 : 0u);
+    a[3] = (t1 < n ? uint32_t(vr_s[t1 * VSTR + r1]) : 0u) | (t1 + 1 < n ? uint32_t(vr_s[(t1 + 1) * VSTR + r1]) << 16 : 0u);
+    mma16816_bf16(acc, a, f.rb0, f.rb1);
+  }
+  o0 = fmaf(acc[1], w1, acc[0] * w0);
+  o1 = fmaf(acc[3], w1, acc[2] * w0);
+  o0 += __shfl_xor_sync(0xffffffffu, o0, 1);
+  o1 += __shfl_xor_sync(0xffffffffu, o1, 1);
+  o0 += __shfl_xor_sync(0xffffffffu, o0, 2);
+  o1 += __shfl_xor_sync(0xffffffffu, o1, 2);
+  o0 *= KSCALE_H;
+  o1 *= KSCALE_H;
+}
+
 // n: ring slots replayed (0..16); sc: the vblock scale of this warp's rows.
 // Writes X.ow[32 warp + i] = output row i of the warp's vblock (already * K^-1/2).
 template <class Sync>
 __device__ __forceinline__ void head_nonflush(const HeadTile& T, const HeadScratch& X, int n, float sc, int warp,
                                               int lane, Sync sync) {
-  const int g8 = lane >> 2, t4 = lane & 3;
-  const int VSTR = T.vstr;
-  const uint16_t* kr_s = T.kr;
-  const uint16_t* vr_s = T.vr;
-  float* gam_s = X.ad;
-  float* mgT = X.mg;  // mgT[t][i] = M[i][t], i < t
-  if (warp == 0) {
-    // q split into three bf16 rows (exact for bf16 q, ~24 bits for f32 q)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float q = X.qs[lane * 4 + i];
-      const uint16_t q0 = f_to_bf16(q);
-      const float r1 = q - bf16_to_f(q0);
-      const uint16_t q1 = f_to_bf16(r1);
-      const uint16_t q2 = f_to_bf16(r1 - bf16_to_f(q1));
-      X.qb[lane * 4 + i] = q0;
-      X.qb[128 + lane * 4 + i] = q1;
-      X.qb[256 + lane * 4 + i] = q2;
-    }
-    if (lane < 16) gam_s[lane] = lane < n ? expf(T.gr[lane]) : 0.0f;
-    __syncwarp();
-    // G = K [K; q]^T by bf16 MMA from the ring (tokens >= n masked to zero)
-    float gacc[3][4];
-#pragma unroll
-    for (int nt = 0; nt < 3; ++nt)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) gacc[nt][i] = 0.0f;
-#pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      const int col = 16 * ks + 2 * t4;
-      uint32_t a[4];
-      a[0] = g8 < n ? *reinterpret_cast<const uint32_t*>(kr_s + g8 * KSTR + col) : 0u;
-      a[1] = g8 + 8 < n ? *reinterpret_cast<const uint32_t*>(kr_s + (g8 + 8) * KSTR + col) : 0u;
-      a[2] = g8 < n ? *reinterpret_cast<const uint32_t*>(kr_s + g8 * KSTR + col + 8) : 0u;
-      a[3] = g8 + 8 < n ? *reinterpret_cast<const uint32_t*>(kr_s + (g8 + 8) * KSTR + col + 8) : 0u;
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        const int tok = 8 * nt + g8;
-        const uint32_t b0 = tok < n ? *reinterpret_cast<const uint32_t*>(kr_s + tok * KSTR + col) : 0u;
-        const uint32_t b1 = tok < n ? *reinterpret_cast<const uint32_t*>(kr_s + tok * KSTR + col + 8) : 0u;
-        mma16816_bf16(gacc[nt], a, b0, b1);
-      }
-      const uint32_t b0 = g8 < 3 ? *reinterpret_cast<const uint32_t*>(X.qb + g8 * 128 + col) : 0u;
-      const uint32_t b1 = g8 < 3 ? *reinterpret_cast<const uint32_t*>(X.qb + g8 * 128 + col + 8) : 0u;
-      mma16816_bf16(gacc[2], a, b0, b1);
-    }
-#pragma unroll
-    for (int nt = 0; nt < 3; ++nt) {
-      X.gram[g8 * 24 + 8 * nt + 2 * t4] = gacc[nt][0];
-      X.gram[g8 * 24 + 8 * nt + 2 * t4 + 1] = gacc[nt][1];
-      X.gram[(g8 + 8) * 24 + 8 * nt + 2 * t4] = gacc[nt][2];
-      X.gram[(g8 + 8) * 24 + 8 * nt + 2 * t4 + 1] = gacc[nt][3];
-    }
-    __syncwarp();
-    float a_j = 1.0f, d_j = 1.0f, kq_j = 0.0f;
-    if (lane < n) {
-      const int j = lane;
-      for (int m = 0; m <= j; ++m) a_j *= gam_s[m];
-      float pm = 1.0f;
-      for (int t = j + 1; t < n; ++t) {
-        pm *= gam_s[t];
-        mgT[t * 16 + j] = pm * X.gram[j * 24 + t];
-      }
-      d_j = pm;
-      kq_j = X.gram[j * 24 + 16] + X.gram[j * 24 + 17] + X.gram[j * 24 + 18];
-    }
-    __syncwarp();
-    // triangular solve, t = n-1 .. 0: c_t = beta_t (d_t kq_t - sum_{j>t} c_j M[t][j])
-    float acc = d_j * kq_j, cval = 0.0f;
-    for (int t = n - 1; t >= 0; --t) {
-      const float ct = __shfl_sync(0xffffffffu, T.br[t] * acc, t);
-      if (lane == t) cval = ct;
-      if (lane < t) acc = fmaf(-ct, mgT[t * 16 + lane], acc);
-    }
-    // T_0 = a_{n-1} q - sum_j c_j a_j k_j  (lane: elements 4 lane .. 4 lane + 3)
-    const float alast = n > 0 ? __shfl_sync(0xffffffffu, a_j, n - 1) : 1.0f;
-    float Tq[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) Tq[i] = alast * X.qs[lane * 4 + i];
-    const float wj = cval * a_j;
-    for (int j = 0; j < n; ++j) {
-      const float w = __shfl_sync(0xffffffffu, wj, j);
-      const uint2 kw = *reinterpret_cast<const uint2*>(kr_s + j * KSTR + lane * 4);
-      const float2 k01 = bf16x2_to_f2(kw.x), k23 = bf16x2_to_f2(kw.y);
-      Tq[0] = fmaf(-w, k01.x, Tq[0]);
-      Tq[1] = fmaf(-w, k01.y, Tq[1]);
-      Tq[2] = fmaf(-w, k23.x, Tq[2]);
-      Tq[3] = fmaf(-w, k23.y, Tq[3]);
-    }
-    // c -> [c_hi; c_mid; c_lo] bf16
-    if (lane < 16) {
-      const float c = lane < n ? cval : 0.0f;
-      const uint16_t chi = f_to_bf16(c);
-      const float r1 = c - bf16_to_f(chi);
-      const uint16_t cmid = f_to_bf16(r1);
-      const uint16_t clo = f_to_bf16(r1 - bf16_to_f(cmid));
-      X.cb[lane] = chi;
-      X.cb[16 + lane] = cmid;
-      X.cb[32 + lane] = clo;
-    }
-    // T -> 5 e4m3 terms: T sigma = sum_i term_i 16^-i, max |T sigma| in [128, 256)
-    float m = fmaxf(fmaxf(fabsf(Tq[0]), fabsf(Tq[1])), fmaxf(fabsf(Tq[2]), fabsf(Tq[3])));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    const float sig = pow2_scale_for(m) * (1.0f / 64.0f);
-    float x[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) x[i] = Tq[i] * sig;
-#pragma unroll
-    for (int j = 0; j < 5; ++j) {
-      const uint32_t p01 = e4m3x2_sat(x[0], x[1]);
-      const uint32_t p23 = e4m3x2_sat(x[2], x[3]);
-      *reinterpret_cast<uint32_t*>(X.t8 + j * T8STR + lane * 4) = p01 | (p23 << 16);
-      const uint32_t h01 = e4m3x2_to_f16x2(p01), h23 = e4m3x2_to_f16x2(p23);
-      const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&h01));
-      const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&h23));
-      x[0] = (x[0] - f01.x) * 16.0f;
-      x[1] = (x[1] - f01.y) * 16.0f;
-      x[2] = (x[2] - f23.x) * 16.0f;
-      x[3] = (x[3] - f23.y) * 16.0f;
-    }
-#pragma unroll
-    for (int j = 5; j < 8; ++j) *reinterpret_cast<uint32_t*>(X.t8 + j * T8STR + lane * 4) = 0u;
-    if (lane == 0) X.misc[0] = 1.0f / sig;
-  }
+  if (warp == 0) head_chain(T, X, n, lane);
   sync();
-  // readout on tensor cores.  Columns 0..4: S_fp8 . term_j (e4m3 MMA); 5..7: V^T . c (bf16 MMA)
-  uint32_t bt[4][2];
-#pragma unroll
-  for (int ks = 0; ks < 4; ++ks) {
-    bt[ks][0] = *reinterpret_cast<const uint32_t*>(X.t8 + g8 * T8STR + 32 * ks + 4 * t4);
-    bt[ks][1] = *reinterpret_cast<const uint32_t*>(X.t8 + g8 * T8STR + 32 * ks + 16 + 4 * t4);
-  }
-  const bool rcol = g8 >= 5;
-  const uint32_t rb0 = rcol ? *reinterpret_cast<const uint32_t*>(X.cb + (g8 - 5) * 16 + 2 * t4) : 0u;
-  const uint32_t rb1 = rcol ? *reinterpret_cast<const uint32_t*>(X.cb + (g8 - 5) * 16 + 8 + 2 * t4) : 0u;
-  // column weights: t4 = 0 -> terms 0,1; 1 -> terms 2,3; 2 -> term 4, ring; 3 -> ring, ring
-  const float wbase = X.misc[0] * sc;
-  const float w0 = t4 == 0 ? wbase : (t4 == 1 ? wbase * (1.0f / 256.0f) : (t4 == 2 ? wbase * (1.0f / 65536.0f) : 1.0f));
-  const float w1 = t4 == 0 ? wbase * (1.0f / 16.0f) : (t4 == 1 ? wbase * (1.0f / 4096.0f) : 1.0f);
-  const int rw0 = 32 * warp;
+  const int g8 = lane >> 2, t4 = lane & 3;
+  const ReadoutFrags f = head_readout_frags(X, lane);
+  const float wsc = X.misc[0] * sc;
   float* ow = X.ow + 32 * warp;
 #pragma unroll
   for (int mt = 0; mt < 2; ++mt) {
-    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    const int r0 = rw0 + 16 * mt + g8, r1 = r0 + 8;
-#pragma unroll
-    for (int ks = 0; ks < 4; ++ks) {
-      uint32_t a[4];
-      a[0] = *reinterpret_cast<const uint32_t*>(T.s0 + s0_off(r0, 2 * ks) + 4 * t4);
-      a[1] = *reinterpret_cast<const uint32_t*>(T.s0 + s0_off(r1, 2 * ks) + 4 * t4);
-      a[2] = *reinterpret_cast<const uint32_t*>(T.s0 + s0_off(r0, 2 * ks + 1) + 4 * t4);
-      a[3] = *reinterpret_cast<const uint32_t*>(T.s0 + s0_off(r1, 2 * ks + 1) + 4 * t4);
-      mma16832_e4m3(acc, a, bt[ks][0], bt[ks][1]);
-    }
-    {
-      const int t0 = 2 * t4, t1 = 2 * t4 + 8;
-      uint32_t a[4];
-      a[0] = (t0 < n ? uint32_t(vr_s[t0 * VSTR + r0]) : 0u) | (t0 + 1 < n ? uint32_t(vr_s[(t0 + 1) * VSTR + r0]) << 16 : 0u);
-      a[1] = (t0 < n ? uint32_t(vr_s[t0 * VSTR + r1]) : 0u) | (t0 + 1 < n ? uint32_t(vr_s[(t0 + 1) * VSTR + r1]) << 16 : 0u);
-      a[2] = (t1 < n ? uint32_t(vr_s[t1 * VSTR + r0]) : 0u) | (t1 + 1 < n ? uint32_t(vr_s[(t1 + 1) * VSTR + r0]) << 16 : 0u);
-      a[3] = (t1 < n ? uint32_t(vr_s[t1 * VSTR + r1]) : 0u) | (t1 + 1 < n ? uint32_t(vr_s[(t1 + 1) * VSTR + r1]) << 16 : 0u);
-      mma16816_bf16(acc, a, rb0, rb1);
-    }
-    float o0 = fmaf(acc[1], w1, acc[0] * w0);
-    float o1 = fmaf(acc[3], w1, acc[2] * w0);
-    o0 += __shfl_xor_sync(0xffffffffu, o0, 1);
-    o1 += __shfl_xor_sync(0xffffffffu, o1, 1);
-    o0 += __shfl_xor_sync(0xffffffffu, o0, 2);
-    o1 += __shfl_xor_sync(0xffffffffu, o1, 2);
+    float o0, o1;
+    head_readout_mtile(T, f, n, wsc, 32 * warp + 16 * mt, lane, o0, o1);
     if (t4 == 0) {
-      ow[16 * mt + g8] = o0 * KSCALE_H;
-      ow[16 * mt + g8 + 8] = o1 * KSCALE_H;
+      ow[16 * mt + g8] = o0;
+      ow[16 * mt + g8 + 8] = o1;
     }
   }
   __syncwarp();

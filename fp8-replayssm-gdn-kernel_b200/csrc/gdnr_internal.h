@@ -66,6 +66,9 @@ struct StepParams {
   int32_t rows;  // value rows per CTA (32/64/128)
   int32_t quant_rounded;
   uint32_t* err;
+  int32_t flush_hint;   // GDNR_FLUSH_*
+  int32_t head_filter;  // 0: every head; 2: only heads that flush
+  int32_t pdl;          // launch with programmatic stream serialization
 };
 
 struct SmemLayout {
@@ -104,10 +107,9 @@ cudaError_t launch_step(const StepParams& p, bool fused, bool f32ck, int group, 
 // B200 path for E4M3 checkpoints and rings of L <= 16 (one CTA per value head)
 cudaError_t launch_step2(const StepParams& p, bool fused, cudaStream_t stream);
 constexpr int STEP2_MAX_L = 16;
-// persistent pipelined path (one CTA per SM): E4M3, L <= 16, whole heads,
-// f32 gates, 16-byte aligned rows; otherwise launch_step2 / launch_step
-bool step3_eligible(const StepParams& p, bool fused, bool f32ck);
-cudaError_t launch_step3(const StepParams& p, bool fused, cudaStream_t stream);
+// persistent warp-specialised path for the heads that do not flush (gdnr_step5.cu)
+bool step5_eligible(const StepParams& p, bool fused, bool f32ck);
+cudaError_t launch_step5(const StepParams& p, bool fused, bool pdl, cudaStream_t stream);
 
 // ---------------------------------------------------------------- codec kernel
 struct CodecParams {

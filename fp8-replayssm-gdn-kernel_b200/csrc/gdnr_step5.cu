@@ -1,0 +1,931 @@
+// Persistent warp-specialised GDN decode step (sm_100a) for E4M3 checkpoints
+// with rings of 4 <= L <= 16: every head whose ring is not full.
+//
+// Work unit: the (up to) two value heads of one key head that share the key
+// ring and the query (G = HV/H value heads per key head; a unit holds
+// hpu = min(G, 2) of them).  One CTA per SM owns units blockIdx.x,
+// blockIdx.x + gridDim.x, ...  Three warp roles run concurrently:
+//
+//  * producer (warp 0): streams each unit's checkpoint tiles (ONE tensor-map
+//    TMA request of 128 x 128 x hpu bytes, 128-byte swizzle = the layout the
+//    tensor-core fragments read conflict-free) and value-ring rows (boxes of
+//    8 slots) through S5_STAGES shared-memory stages, in unit order.
+//  * chain warps (S5_NCW): one warp per unit runs everything that does not
+//    touch the checkpoint -- prep of this token (q/k L2 norm, gates, ring
+//    append; kern.py:453-576), the Gram matrix of the key ring on tensor
+//    cores, the triangular solve for the replay coefficients c and the
+//    transformed query T of the backward chain (kern.py:121-176 in Gram
+//    form) -- for both heads of the unit at once.  A unit's chain needs only
+//    its key ring (4 KB, loaded by the chain warp's own TMA), so all chains of
+//    the SM run while the checkpoints are still streaming in.
+//  * readout team (S5_NRW warps): consumes the stages in order; each warp
+//    reads out 32 * hpu / 2 rows of the unit on tensor cores: S_fp8 . T as an
+//    e4m3 MMA against T split into five e4m3 terms, V^T c as a bf16 MMA into
+//    the spare accumulator columns, plus this token's value row (rank one).
+//
+// Units whose ring is full (flush) are skipped; the caller runs the flush
+// path for them (gdnr_step2.cu in flush-only mode).
+#include <cuda.h>
+
+#include "gdnr_device.cuh"
+#include "gdnr_head.cuh"
+#include "gdnr_internal.h"
+
+namespace gdnr {
+
+constexpr int S5_NS = 4;    // checkpoint / value-ring stages
+constexpr int S5_NPRO = 2;  // stages requested before the first dependent load
+constexpr int S5_NCW = 7;   // chain warps
+constexpr int S5_NRW = 8;   // readout warps
+constexpr int S5_THREADS = 32 * (1 + S5_NCW + S5_NRW);
+constexpr int S5_GSTR = 20;  // Gram scratch row (floats): 16 key columns + 3 query terms + pad
+constexpr float S5_LOG2E = 1.4426950408889634f;
+
+struct S5Geo {
+  int hpu;  // value heads per unit (1 or 2)
+  int upk;  // units per key head (G / hpu)
+  int rb;   // ring slots per TMA request (8, or 4 when L < 8)
+};
+
+__host__ __device__ inline S5Geo s5_geo(int H, int HV, int L) {
+  S5Geo g;
+  const int G = HV / H;
+  g.hpu = G >= 2 ? 2 : 1;
+  g.upk = G / g.hpu;
+  g.rb = L >= 8 ? 8 : 4;
+  return g;
+}
+
+// Shared memory.  Ring regions hold 16 slots of 256 bytes (the fragment loads
+// always cover 16 slots; slots >= n are masked).
+//   [barriers | table] [stages: ck (hpu x 16 KB) | vr (hpu x 4 KB)] x S5_NS
+//   [kbuf: key ring (4 KB)] x S5_NCW
+//   [res: t8 x hpu | cb x hpu | misc x hpu | vnew x hpu] x S5_NCW  (the t8 area
+//        doubles as the chain's q-split / Gram scratch before T is written)
+//   [ost: 32 floats] x S5_NRW
+struct S5Layout {
+  uint32_t full, empty, kfull, cdone, rfree, abort, table;
+  uint32_t stage0, stage_bytes, ck, vr;
+  uint32_t kbuf0;
+  uint32_t res0, res_bytes, t8, cb, misc, vnew;
+  uint32_t qb, gram;  // chain scratch inside res (aliases t8)
+  uint32_t ost0;
+  uint32_t total;
+};
+
+__host__ __device__ inline S5Layout s5_layout(const S5Geo& g, int max_units) {
+  S5Layout s;
+  uint32_t o = 0;
+  s.full = smem_take(o, S5_NS * 8);
+  s.empty = smem_take(o, S5_NS * 8);
+  s.kfull = smem_take(o, S5_NCW * 8);
+  s.cdone = smem_take(o, S5_NCW * 8);
+  s.rfree = smem_take(o, S5_NCW * 8);
+  s.abort = smem_take(o, 16);
+  s.table = smem_take(o, uint32_t(max_units) * 4u);
+  o = (o + 1023u) & ~1023u;
+  s.stage0 = o;
+  s.ck = 0;
+  s.vr = uint32_t(g.hpu) * 16384u;
+  s.stage_bytes = s.vr + uint32_t(g.hpu) * 4096u;
+  o += S5_NS * s.stage_bytes;
+  s.kbuf0 = o;
+  o += S5_NCW * 4096u;
+  uint32_t r = 0;
+  s.t8 = smem_take(r, 2u * 8u * T8STR);
+  s.cb = smem_take(r, 2u * 3u * 16u * 2u);
+  s.misc = smem_take(r, 2u * 16u);
+  s.vnew = smem_take(r, 2u * 128u * 2u);
+  s.res_bytes = r;
+  r = 0;
+  s.qb = smem_take(r, 3u * 128u * 2u);
+  s.gram = smem_take(r, 16u * S5_GSTR * 4u);  // qb + gram fit in the t8 area
+  s.res0 = o;
+  o += S5_NCW * s.res_bytes;
+  s.ost0 = o;
+  o += S5_NRW * 128u;
+  s.total = o;
+  return s;
+}
+
+// ---------------------------------------------------------------- device helpers
+__device__ __forceinline__ void s5_ldsm_x4(uint32_t addr, uint32_t* r) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr)
+               : "memory");
+}
+
+__device__ __forceinline__ void s5_ldsm_x4_t(uint32_t addr, uint32_t* r) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr)
+               : "memory");
+}
+
+__device__ __forceinline__ void s5_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void s5_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ void s5_tma4(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                        uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
+      "%5}], [%6];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void s5_tma5(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3, int c4,
+                                        uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, "
+      "%6}], [%7];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(smem_addr(bar))
+      : "memory");
+}
+
+
+// Bounded mbarrier wait that also gives up once another warp has recorded a
+// failure in *abort (then every later wait returns at once).
+__device__ __forceinline__ bool s5_wait(uint64_t* bar, uint32_t parity, uint32_t* err, volatile int* abort) {
+  const uint32_t a = smem_addr(bar);
+  if (mbar_try_wait(a, parity)) return true;
+  if (*abort) return false;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1; it < WAIT_LIMIT_ITERS; ++it) {
+    if (mbar_try_wait(a, parity)) return true;
+    if ((it & 63u) == 0) {
+      if (*abort) return false;
+      if (globaltimer_ns() - t0 > WAIT_LIMIT_NS) break;
+    }
+  }
+  *abort = 1;
+  atomicOr(err, GDNR_DEVERR_WAIT_TIMEOUT);
+  return false;
+}
+
+__device__ __forceinline__ bool s5_warp_wait(uint64_t* bar, uint32_t parity, uint32_t* err, volatile int* abort,
+                                             int lane) {
+  int ok = 1;
+  if (lane == 0) ok = s5_wait(bar, parity, err, abort) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+// Byte offset of element (slot t, column col) in a ring region written by the
+// 128-byte-swizzled ring boxes: slot t is two 128-byte lines R = 2t + col/64,
+// and 16-byte chunk c of line R sits at chunk c ^ (R & 7).
+__device__ __forceinline__ uint32_t s5_ring_off(int t, int col) {
+  const int R = 2 * t + (col >> 6);
+  const int c = (col & 63) >> 3;
+  return uint32_t(R) * 128u + (uint32_t(c ^ (R & 7)) << 4) + uint32_t(col & 7) * 2u;
+}
+
+// four consecutive elements of a bf16 or f32 row, kept raw until used
+__device__ __forceinline__ uint4 s5_load4(const void* base, int64_t idx, bool bf16) {
+  if (bf16) {
+    const uint2 w = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(base) + idx);
+    return make_uint4(w.x, w.y, 0u, 0u);
+  }
+  return *reinterpret_cast<const uint4*>(static_cast<const float*>(base) + idx);
+}
+
+__device__ __forceinline__ void s5_unpack4(uint4 w, bool bf16, float* x) {
+  if (bf16) {
+    const float2 a = bf16x2_to_f2(w.x), b = bf16x2_to_f2(w.y);
+    x[0] = a.x;
+    x[1] = a.y;
+    x[2] = b.x;
+    x[3] = b.y;
+  } else {
+    x[0] = __uint_as_float(w.x);
+    x[1] = __uint_as_float(w.y);
+    x[2] = __uint_as_float(w.z);
+    x[3] = __uint_as_float(w.w);
+  }
+}
+
+// Unit descriptor in the table: bits 0-7 slots replayed (this token included),
+// 8-15 slots read from memory, bit 16 skip (flush elsewhere, or a bad position).
+__device__ __forceinline__ int s5_n(int code) { return code & 0xff; }
+__device__ __forceinline__ int s5_nmem(int code) { return (code >> 8) & 0xff; }
+__device__ __forceinline__ bool s5_skip(int code) { return (code >> 16) & 1; }
+
+struct S5Unit {
+  int b, h, pp, hv0;
+};
+
+__device__ __forceinline__ S5Unit s5_unit(int u, int H, int G, const S5Geo& g) {
+  S5Unit x;
+  const int per_b = H * g.upk;
+  x.b = u / per_b;
+  const int r = u - x.b * per_b;
+  x.h = r / g.upk;
+  x.pp = r - x.h * g.upk;
+  x.hv0 = x.h * G + x.pp * g.hpu;
+  return x;
+}
+
+__device__ __forceinline__ float s5_ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// 2^(14 - e) for m in [2^(e-1), 2^e), clamped to 2^[-124, 124]; 1 for m not
+// finite-positive (so that max |x| * scale lies in [2^13, 2^14))
+__device__ __forceinline__ float s5_pow2_scale(float m) {
+  if (!(m > 0.0f) || !(m <= 3.402823466e38f)) return 1.0f;
+  const int e = int((__float_as_uint(m) >> 23) & 0xffu) - 126;
+  int k = 14 - e;
+  k = k > 124 ? 124 : (k < -124 ? -124 : k);
+  return __uint_as_float(uint32_t(k + 127) << 23);
+}
+
+// Two heads' T (4 elements per lane each: 4 lane .. 4 lane + 3) -> five e4m3
+// terms per head in t8 rows 0..4 (rows 5..7 zero):
+// T sigma = sum_i term_i 16^-i, max |T sigma| in [128, 256); misc[0] = 1/sigma.
+template <int HPU>
+__device__ __forceinline__ void s5_tsplit(const float (*Tq)[4], uint8_t* t8, float* misc, int lane) {
+  float m[HPU];
+#pragma unroll
+  for (int h = 0; h < HPU; ++h)
+    m[h] = fmaxf(fmaxf(fabsf(Tq[h][0]), fabsf(Tq[h][1])), fmaxf(fabsf(Tq[h][2]), fabsf(Tq[h][3])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int h = 0; h < HPU; ++h) m[h] = fmaxf(m[h], __shfl_xor_sync(0xffffffffu, m[h], o));
+  float x[HPU][4], sig[HPU];
+#pragma unroll
+  for (int h = 0; h < HPU; ++h) {
+    sig[h] = s5_pow2_scale(m[h]) * (1.0f / 64.0f);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) x[h][i] = Tq[h][i] * sig[h];
+  }
+#pragma unroll
+  for (int j = 0; j < 5; ++j) {
+#pragma unroll
+    for (int h = 0; h < HPU; ++h) {
+      const uint32_t p01 = e4m3x2_sat(x[h][0], x[h][1]);
+      const uint32_t p23 = e4m3x2_sat(x[h][2], x[h][3]);
+      *reinterpret_cast<uint32_t*>(t8 + (h * 8 + j) * T8STR + lane * 4) = p01 | (p23 << 16);
+      if (j < 4) {
+        const uint32_t h01 = e4m3x2_to_f16x2(p01), h23 = e4m3x2_to_f16x2(p23);
+        const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&h01));
+        const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&h23));
+        x[h][0] = (x[h][0] - f01.x) * 16.0f;
+        x[h][1] = (x[h][1] - f01.y) * 16.0f;
+        x[h][2] = (x[h][2] - f23.x) * 16.0f;
+        x[h][3] = (x[h][3] - f23.y) * 16.0f;
+      }
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < HPU; ++h) {
+#pragma unroll
+    for (int j = 5; j < 8; ++j) *reinterpret_cast<uint32_t*>(t8 + (h * 8 + j) * T8STR + lane * 4) = 0u;
+    if (lane == 0) misc[h * 4] = 1.0f / sig[h];
+  }
+}
+
+// Per-lane raw inputs of one unit for its chain warp (lane 16 e + t: head e,
+// ring slot t), loaded as soon as the unit is known.
+struct S5In {
+  uint4 q, k;              // query / key rows, 4 elements per lane
+  uint4 v0, v1;            // this token's value rows of heads 0 and 1 (fused)
+  float g, beta;           // gates of (head e, slot t) for slots read from memory
+  float a, bb, alog, dtb;  // this token's gate inputs of head e (fused)
+};
+
+template <bool FUSED, int HPU>
+__device__ __forceinline__ S5In s5_fetch(const StepParams& p, const S5Unit& U, int code, int lane) {
+  S5In in;
+  in.q = in.k = in.v0 = in.v1 = make_uint4(0u, 0u, 0u, 0u);
+  in.g = in.beta = in.a = in.bb = in.alog = in.dtb = 0.0f;
+  if (s5_skip(code)) return in;
+  const int e = lane >> 4, t = lane & 15;
+  const int hv = U.hv0 + (e < HPU ? e : 0);
+  if (e < HPU && t < s5_nmem(code)) {
+    in.g = load_scalar(p.gr, int64_t(U.b) * p.gr_sb + int64_t(t) * p.gr_st + int64_t(hv) * p.gr_sh, p.gr_dt);
+    in.beta = load_scalar(p.br, int64_t(U.b) * p.br_sb + int64_t(t) * p.br_st + int64_t(hv) * p.br_sh, p.br_dt);
+  }
+  if constexpr (FUSED) {
+    const bool bf = p.mx_dt == GDNR_BF16;
+    const int64_t row = int64_t(U.b) * p.mx_sb;
+    in.q = s5_load4(p.mixed, row + int64_t(U.h) * KD + 4 * lane, bf);
+    in.k = s5_load4(p.mixed, row + int64_t(p.H + U.h) * KD + 4 * lane, bf);
+    const int64_t vrow = row + 2 * int64_t(p.H) * KD + int64_t(U.hv0) * VD + 4 * lane;
+    in.v0 = s5_load4(p.mixed, vrow, bf);
+    if (HPU == 2) in.v1 = s5_load4(p.mixed, vrow + VD, bf);
+    in.a = load_scalar(p.a, int64_t(U.b) * p.a_sb + int64_t(hv) * p.a_sh, p.a_dt);
+    in.bb = load_scalar(p.bb, int64_t(U.b) * p.b_sb + int64_t(hv) * p.b_sh, p.b_dt);
+    in.alog = p.a_log[int64_t(hv) * p.al_s];
+    in.dtb = p.dt_bias[int64_t(hv) * p.db_s];
+  } else {
+    in.q = s5_load4(p.q, int64_t(U.b) * p.q_sb + int64_t(U.h) * p.q_sh + 4 * lane, p.q_dt == GDNR_BF16);
+  }
+  return in;
+}
+
+// The chain of one unit (one warp, both heads).  kbuf: the unit's key ring
+// (swizzled, slots < nmem loaded); res: this warp's result block.
+template <bool FUSED, int HPU>
+__device__ __forceinline__ void s5_chain(const StepParams& p, const S5Unit& U, int code, const S5In& in,
+                                         uint8_t* kbuf, uint8_t* res, const S5Layout& lay, int lane) {
+  const int g8 = lane >> 2, t4 = lane & 3;
+  const int e = lane >> 4, t = lane & 15;
+  const int n = s5_n(code), nmem = s5_nmem(code);
+  uint16_t* qb = reinterpret_cast<uint16_t*>(res + lay.t8 + lay.qb);
+  float* gram = reinterpret_cast<float*>(res + lay.t8 + lay.gram);
+  float* misc = reinterpret_cast<float*>(res + lay.misc);
+  float g_own = in.g, beta_own = in.beta;  // gates of (head e, slot t)
+  float qv[4];
+  if constexpr (FUSED) {
+    const int L = p.L;
+    const int pos = nmem;
+    const bool bf = p.mx_dt == GDNR_BF16;
+    // this token's gates for head e (every lane; slot pos keeps them)
+    {
+      const float xg = in.a + in.dtb;
+      const float sp = (xg <= SOFTPLUS_THRESHOLD) ? logf(1.0f + expf(xg)) : xg;
+      const float gn = round_to(-expf(in.alog) * sp, p.gr_dt);
+      const float bn = round_to(1.0f / (1.0f + expf(-in.bb)), p.br_dt);
+      if (t == pos) {
+        g_own = gn;
+        beta_own = bn;
+      }
+    }
+    float x[4], y[4];
+    s5_unpack4(in.q, bf, x);
+    s5_unpack4(in.k, bf, y);
+    // q, k <- x / sqrt(sum x^2 + eps)  (kern.py:514-515): one correctly rounded
+    // reciprocal of the norm, then products
+    const float qs2 = warp_sum(x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3]);
+    const float ks2 = warp_sum(y[0] * y[0] + y[1] * y[1] + y[2] * y[2] + y[3] * y[3]);
+    const float qi = __frcp_rn(sqrtf(qs2 + L2_EPS)), ki = __frcp_rn(sqrtf(ks2 + L2_EPS));
+    const int qdt = p.q_out ? p.qo_dt : GDNR_BF16;
+    const bool owner = U.pp == 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) qv[i] = round_to(x[i] * qi, qdt);
+    if (owner && p.q_out) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        store_scalar(p.q_out, int64_t(U.b) * p.qo_sb + int64_t(U.h) * p.qo_sh + 4 * lane + i, qdt, qv[i]);
+    }
+    const uint2 kw = make_uint2(pack_bf16x2(y[0] * ki, y[1] * ki), pack_bf16x2(y[2] * ki, y[3] * ki));
+    *reinterpret_cast<uint2*>(kbuf + s5_ring_off(pos, 4 * lane)) = kw;
+    if (owner)
+      *reinterpret_cast<uint2*>(p.kr + int64_t(U.b) * p.kr_sb + int64_t(pos) * p.kr_st + int64_t(U.h) * p.kr_sh +
+                                4 * lane) = kw;
+    // this token's value rows: ring slot pos in HBM, and the readout's rank-one term
+#pragma unroll
+    for (int h = 0; h < HPU; ++h) {
+      float vv[4];
+      s5_unpack4(h == 0 ? in.v0 : in.v1, bf, vv);
+      const uint2 vw = make_uint2(pack_bf16x2(vv[0], vv[1]), pack_bf16x2(vv[2], vv[3]));
+      *reinterpret_cast<uint2*>(res + lay.vnew + h * 256 + 8 * lane) = vw;
+      *reinterpret_cast<uint2*>(p.vr + int64_t(U.b) * p.vr_sb + int64_t(pos) * p.vr_st +
+                                int64_t(U.hv0 + h) * p.vr_sh + 4 * lane) = vw;
+    }
+    if (t == pos && e < HPU) {
+      const int hv = U.hv0 + e;
+      store_scalar(p.gr, int64_t(U.b) * p.gr_sb + int64_t(pos) * p.gr_st + int64_t(hv) * p.gr_sh, p.gr_dt, g_own);
+      store_scalar(p.br, int64_t(U.b) * p.br_sb + int64_t(pos) * p.br_st + int64_t(hv) * p.br_sh, p.br_dt, beta_own);
+      if (p.pos_out && hv == 0) p.pos_out[int64_t(U.b) * p.po_s] = (pos + 1) % L;
+    }
+  } else {
+    s5_unpack4(in.q, p.q_dt == GDNR_BF16, qv);
+  }
+  // q split into three bf16 rows (the Gram's query columns)
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float q = qv[i];
+    const uint16_t q0 = f_to_bf16(q);
+    const float r1 = q - bf16_to_f(q0);
+    const uint16_t q1 = f_to_bf16(r1);
+    const uint16_t q2 = f_to_bf16(r1 - bf16_to_f(q1));
+    qb[4 * lane + i] = q0;
+    qb[128 + 4 * lane + i] = q1;
+    qb[256 + 4 * lane + i] = q2;
+  }
+  __syncwarp();
+
+  // ---- Gram G = K [K; q]^T on tensor cores (slots >= n masked to zero)
+  {
+    const uint32_t kr_addr = smem_addr(kbuf);
+    const uint32_t m_lo = g8 < n ? 0xffffffffu : 0u, m_hi = g8 + 8 < n ? 0xffffffffu : 0u;
+    float gacc[3][4];
+#pragma unroll
+    for (int nt = 0; nt < 3; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) gacc[nt][i] = 0.0f;
+    const int mi = lane >> 3;
+    const int trow = (lane & 7) + 8 * (mi & 1);
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      uint32_t a[4];
+      s5_ldsm_x4(kr_addr + s5_ring_off(trow, 16 * ks + 8 * (mi >> 1)), a);
+      a[0] &= m_lo;
+      a[2] &= m_lo;
+      a[1] &= m_hi;
+      a[3] &= m_hi;
+      mma16816_bf16(gacc[0], a, a[0], a[2]);
+      mma16816_bf16(gacc[1], a, a[1], a[3]);
+      const int col = 16 * ks + 2 * t4;
+      const uint32_t b0 = g8 < 3 ? *reinterpret_cast<const uint32_t*>(qb + g8 * 128 + col) : 0u;
+      const uint32_t b1 = g8 < 3 ? *reinterpret_cast<const uint32_t*>(qb + g8 * 128 + col + 8) : 0u;
+      mma16816_bf16(gacc[2], a, b0, b1);
+    }
+#pragma unroll
+    for (int nt = 0; nt < 3; ++nt) {
+      if (nt < 2 || t4 < 2) {
+        const int col = 8 * nt + 2 * t4;
+        *reinterpret_cast<float2*>(gram + g8 * S5_GSTR + col) = make_float2(gacc[nt][0], gacc[nt][1]);
+        *reinterpret_cast<float2*>(gram + (g8 + 8) * S5_GSTR + col) = make_float2(gacc[nt][2], gacc[nt][3]);
+      }
+    }
+  }
+  __syncwarp();
+  // lane (e, t) holds row t of G (the same rows in both half-warps)
+  float grow[16];
+  float kq;
+  {
+    const float4* gr4 = reinterpret_cast<const float4*>(gram + t * S5_GSTR);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float4 v = gr4[i];
+      grow[4 * i] = v.x;
+      grow[4 * i + 1] = v.y;
+      grow[4 * i + 2] = v.z;
+      grow[4 * i + 3] = v.w;
+    }
+    const float4 v = gr4[4];
+    kq = v.x + v.y + v.z;
+  }
+  // ---- decays in log2 space per head (16-lane segment): Lg_t = sum_{m<=t} g_m log2(e),
+  // a_t = 2^Lg_t, d_t = 2^(Lg_{n-1} - Lg_t), M[t][j] = 2^(Lg_j - Lg_t) G[t][j]  (t < j)
+  float Lg = t < n ? g_own * S5_LOG2E : 0.0f;
+#pragma unroll
+  for (int o = 1; o < 16; o <<= 1) {
+    const float up = __shfl_up_sync(0xffffffffu, Lg, o, 16);
+    if (t >= o) Lg += up;
+  }
+  const float Llast = __shfl_sync(0xffffffffu, Lg, 15, 16);  // slots >= n add nothing
+  const float a_own = s5_ex2(Lg);
+  const float bsel = t < n ? beta_own : 0.0f;
+  float acc = t < n ? s5_ex2(Llast - Lg) * kq : 0.0f;
+  float cval = 0.0f;
+  // ---- triangular solve, j = n-1 .. 0: c_j = beta_j (d_j kq_j - sum_{m>j} c_m M[j][m]).
+  // Slots j >= n carry c_j = 0 (beta masked), so the steps run unconditionally.
+  const int jtop = n > 8 ? 15 : 7;
+#pragma unroll
+  for (int j = 15; j >= 0; --j) {
+    if (j <= jtop) {
+      const float Lj = __shfl_sync(0xffffffffu, Lg, j, 16);
+      const float cj = __shfl_sync(0xffffffffu, bsel * acc, j, 16);
+      if (t == j) cval = cj;
+      if (t < j) acc = fmaf(-cj, s5_ex2(Lj - Lg) * grow[j], acc);
+    }
+  }
+  // ---- c -> [c_hi; c_mid; c_lo] bf16 over the slots read from memory (ring
+  // columns of the readout); this token's own slot is a rank-one term
+  if (e < HPU) {
+    uint16_t* cb = reinterpret_cast<uint16_t*>(res + lay.cb + e * 96);
+    const float cc = t < nmem ? cval : 0.0f;
+    const uint16_t chi = f_to_bf16(cc);
+    const float r1 = cc - bf16_to_f(chi);
+    const uint16_t cmid = f_to_bf16(r1);
+    const uint16_t clo = f_to_bf16(r1 - bf16_to_f(cmid));
+    cb[t] = chi;
+    cb[16 + t] = cmid;
+    cb[32 + t] = clo;
+  }
+  {
+    // coefficient of this token's own slot (fused): one writer per head
+    const float cp = __shfl_sync(0xffffffffu, cval, (lane & 16) + (nmem & 15));
+    if (t == 0 && e < HPU) misc[e * 4 + 1] = FUSED ? cp : 0.0f;
+  }
+  // ---- T_e = a_{n-1} q - sum_j c_j a_j k_j  (lane: elements 4 lane .. 4 lane + 3)
+  const float wj = cval * a_own;  // 0 for slots >= n
+  float T[HPU][4];
+#pragma unroll
+  for (int h = 0; h < HPU; ++h) {
+    const float al = s5_ex2(__shfl_sync(0xffffffffu, Llast, 16 * h));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) T[h][i] = al * qv[i];
+  }
+  {
+    const int half = lane >> 4, c16 = (lane & 15) >> 1;
+    const uint8_t* kbase = kbuf + half * 128 + (lane & 1) * 8;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (j <= jtop) {
+        const int R = 2 * j + half;
+        uint2 kw = *reinterpret_cast<const uint2*>(kbase + j * 256 + ((c16 ^ (R & 7)) << 4));
+        if (j >= n) kw = make_uint2(0u, 0u);  // stale or unloaded slot
+        const float2 k01 = bf16x2_to_f2(kw.x), k23 = bf16x2_to_f2(kw.y);
+#pragma unroll
+        for (int h = 0; h < HPU; ++h) {
+          const float w = __shfl_sync(0xffffffffu, wj, 16 * h + j);
+          T[h][0] = fmaf(-w, k01.x, T[h][0]);
+          T[h][1] = fmaf(-w, k01.y, T[h][1]);
+          T[h][2] = fmaf(-w, k23.x, T[h][2]);
+          T[h][3] = fmaf(-w, k23.y, T[h][3]);
+        }
+      }
+    }
+  }
+  __syncwarp();  // q-split / Gram scratch (aliases t8) is dead from here on
+  s5_tsplit<HPU>(T, res + lay.t8, misc, lane);
+}
+
+// Readout of MW m-tiles (rows rbase .. rbase + 16 MW - 1, one vblock) of one
+// head by one warp.  Leaves o(row) in ost[0 .. 16 MW).
+template <int MW, bool FUSED>
+__device__ __forceinline__ void s5_readout(const uint8_t* ck_s, const uint8_t* vr_s, const uint8_t* t8,
+                                           const uint16_t* cb, float wsc, float cpos, const uint16_t* vnew,
+                                           int rbase, int nmem, float* ost, int lane) {
+  const int g8 = lane >> 2, t4 = lane & 3;
+  uint32_t bt[4][2];
+#pragma unroll
+  for (int ks = 0; ks < 4; ++ks) {
+    bt[ks][0] = g8 < 5 ? *reinterpret_cast<const uint32_t*>(t8 + g8 * T8STR + 32 * ks + 4 * t4) : 0u;
+    bt[ks][1] = g8 < 5 ? *reinterpret_cast<const uint32_t*>(t8 + g8 * T8STR + 32 * ks + 16 + 4 * t4) : 0u;
+  }
+  const bool rcol = g8 >= 5;
+  const uint32_t rb0 = rcol ? *reinterpret_cast<const uint32_t*>(cb + (g8 - 5) * 16 + 2 * t4) : 0u;
+  const uint32_t rb1 = rcol ? *reinterpret_cast<const uint32_t*>(cb + (g8 - 5) * 16 + 8 + 2 * t4) : 0u;
+  // value-ring slots >= nmem hold stale or unloaded data: mask them in the A fragments
+  const int t0 = 2 * t4, t1 = 2 * t4 + 8;
+  const uint32_t mk0 = (t0 < nmem ? 0x0000ffffu : 0u) | (t0 + 1 < nmem ? 0xffff0000u : 0u);
+  const uint32_t mk1 = (t1 < nmem ? 0x0000ffffu : 0u) | (t1 + 1 < nmem ? 0xffff0000u : 0u);
+  const uint32_t ck_addr = smem_addr(ck_s), vr_addr = smem_addr(vr_s);
+  const int mi = lane >> 3, r8 = lane & 7;
+  float acc[MW][4];
+#pragma unroll
+  for (int m = 0; m < MW; ++m)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[m][i] = 0.0f;
+#pragma unroll
+  for (int ks = 0; ks < 4; ++ks) {
+#pragma unroll
+    for (int m = 0; m < MW; ++m) {
+      uint32_t a[4];
+      const int row = rbase + 16 * m + r8 + 8 * (mi & 1);
+      s5_ldsm_x4(ck_addr + s0_off(row, 2 * ks + (mi >> 1)), a);
+      mma16832_e4m3(acc[m], a, bt[ks][0], bt[ks][1]);
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < MW; ++m) {
+    uint32_t a[4];
+    s5_ldsm_x4_t(vr_addr + s5_ring_off(r8 + 8 * (mi >> 1), rbase + 16 * m + 8 * (mi & 1)), a);
+    a[0] &= mk0;
+    a[1] &= mk0;
+    a[2] &= mk1;
+    a[3] &= mk1;
+    mma16816_bf16(acc[m], a, rb0, rb1);
+  }
+  // column weights: t4 = 0 -> terms 0,1; 1 -> terms 2,3; 2 -> term 4, ring; 3 -> ring, ring
+  const float w0 = t4 == 0 ? wsc : (t4 == 1 ? wsc * (1.0f / 256.0f) : (t4 == 2 ? wsc * (1.0f / 65536.0f) : 1.0f));
+  const float w1 = t4 == 0 ? wsc * (1.0f / 16.0f) : (t4 == 1 ? wsc * (1.0f / 4096.0f) : 1.0f);
+  float o[MW][2];
+#pragma unroll
+  for (int m = 0; m < MW; ++m) {
+    o[m][0] = fmaf(acc[m][1], w1, acc[m][0] * w0);
+    o[m][1] = fmaf(acc[m][3], w1, acc[m][2] * w0);
+  }
+  // quad sums, spread so that lane t4 ends with value t4 & (2 MW - 1) of the list
+  // (m0 row g8, m0 row g8+8, m1 row g8, m1 row g8+8)
+  const bool odd = t4 & 1;
+  if constexpr (MW == 2) {
+    float x0 = odd ? o[1][0] : o[0][0], x1 = odd ? o[1][1] : o[0][1];
+    const float y0 = odd ? o[0][0] : o[1][0], y1 = odd ? o[0][1] : o[1][1];
+    x0 += __shfl_xor_sync(0xffffffffu, y0, 1);
+    x1 += __shfl_xor_sync(0xffffffffu, y1, 1);
+    x0 += __shfl_xor_sync(0xffffffffu, x0, 2);
+    x1 += __shfl_xor_sync(0xffffffffu, x1, 2);
+    // lanes t4 = 0 (m-tile 0) and 1 (m-tile 1) write rows g8 and g8 + 8
+    if (t4 < 2) {
+      const int r0 = 16 * t4 + g8;
+      if (FUSED) {
+        x0 = fmaf(cpos, bf16_to_f(vnew[rbase + r0]), x0);
+        x1 = fmaf(cpos, bf16_to_f(vnew[rbase + r0 + 8]), x1);
+      }
+      ost[r0] = x0 * KSCALE_H;
+      ost[r0 + 8] = x1 * KSCALE_H;
+    }
+  } else {
+    float x = odd ? o[0][1] : o[0][0];
+    const float y = odd ? o[0][0] : o[0][1];
+    x += __shfl_xor_sync(0xffffffffu, y, 1);
+    x += __shfl_xor_sync(0xffffffffu, x, 2);
+    if (t4 < 2) {
+      const int r = g8 + 8 * t4;
+      if (FUSED) x = fmaf(cpos, bf16_to_f(vnew[rbase + r]), x);
+      ost[r] = x * KSCALE_H;
+    }
+  }
+}
+
+template <bool FUSED, int HPU>
+__global__ void __launch_bounds__(S5_THREADS, 1)
+    step5_kernel(const __grid_constant__ StepParams p, const __grid_constant__ CUtensorMap ck_map,
+                 const __grid_constant__ CUtensorMap kr_map, const __grid_constant__ CUtensorMap vr_map) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int L = p.L, G = p.HV / p.H;
+  const S5Geo geo = s5_geo(p.H, p.HV, L);
+  const int total = p.B * p.H * geo.upk;
+  const int grid = int(gridDim.x), bid = int(blockIdx.x);
+  const int nu = total > bid ? (total - bid + grid - 1) / grid : 0;
+  const int max_units = (total + grid - 1) / grid;
+  const S5Layout lay = s5_layout(geo, max_units);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + lay.full);
+  uint64_t* empty = reinterpret_cast<uint64_t*>(smem + lay.empty);
+  uint64_t* kfull = reinterpret_cast<uint64_t*>(smem + lay.kfull);
+  uint64_t* cdone = reinterpret_cast<uint64_t*>(smem + lay.cdone);
+  uint64_t* rfree = reinterpret_cast<uint64_t*>(smem + lay.rfree);
+  volatile int* abort = reinterpret_cast<volatile int*>(smem + lay.abort);
+  int* table = reinterpret_cast<int*>(smem + lay.table);
+  const bool aligned = (smem_addr(smem) & 1023u) == 0;  // swizzled TMA boxes need 1024-byte alignment
+  const uint32_t box_bytes = uint32_t(geo.rb) * 256u;
+
+  if (tid == 0) {
+    for (int s = 0; s < S5_NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], S5_NRW);
+    }
+    for (int c = 0; c < S5_NCW; ++c) {
+      mbar_init(&kfull[c], 1);
+      mbar_init(&cdone[c], 1);
+      mbar_init(&rfree[c], S5_NRW);
+    }
+    *abort = aligned ? 0 : 1;
+    fence_mbar_init();
+    if (!aligned) atomicOr(p.err, GDNR_DEVERR_WAIT_TIMEOUT);
+  }
+  __syncthreads();
+  if (!aligned) return;
+
+  // ---- prologue: checkpoint tiles of the first units (decode state, not
+  // output of the preceding kernel; see GDNR_LAUNCH_PDL)
+  const int npro = nu < S5_NPRO ? nu : S5_NPRO;
+  if (warp == 0 && lane == 0) {
+    for (int i = 0; i < npro; ++i) {
+      const S5Unit U = s5_unit(bid + i * grid, p.H, G, geo);
+      s5_expect_tx(&full[i], uint32_t(HPU) * 16384u);
+      s5_tma4(smem + lay.stage0 + i * lay.stage_bytes + lay.ck, &ck_map, 0, 0, U.hv0, U.b, &full[i]);
+    }
+  }
+  griddep_wait();
+  for (int i = tid; i < nu; i += blockDim.x) {
+    const S5Unit U = s5_unit(bid + i * grid, p.H, G, geo);
+    int n, nmem, skip = 0;
+    bool flush = false;
+    if constexpr (FUSED) {
+      const int pv = p.pos[int64_t(U.b) * p.pos_s];
+      if (pv < 0 || pv >= L) {
+        n = nmem = 0;
+        skip = 1;
+        if (U.h == 0 && U.pp == 0) atomicOr(p.err, GDNR_DEVERR_BAD_POS);
+      } else {
+        n = pv + 1;
+        nmem = pv;
+        flush = pv == L - 1;
+      }
+    } else {
+      const int v = p.valid_len[int64_t(U.b) * p.vl_s];
+      n = nmem = v < 0 ? 0 : (v > L ? L : v);
+      flush = (p.fl_dt == GDNR_I32) ? (static_cast<const int32_t*>(p.flush)[int64_t(U.b) * p.fl_s] != 0)
+                                    : (static_cast<const uint8_t*>(p.flush)[int64_t(U.b) * p.fl_s] != 0);
+    }
+    if (flush) {
+      skip = 1;
+      if (p.flush_hint == GDNR_FLUSH_NONE && U.h == 0 && U.pp == 0) atomicOr(p.err, GDNR_DEVERR_BAD_HINT);
+    }
+    table[i] = n | (nmem << 8) | (skip << 16);
+  }
+  __syncthreads();
+  if (tid == 0) griddep_launch();
+
+  if (warp == 0) {
+    // =================== producer ===================
+    if (lane != 0) return;
+    for (int i = 0; i < nu; ++i) {
+      const int s = i % S5_NS;
+      if (i >= S5_NS && !s5_wait(&empty[s], ((i / S5_NS) - 1) & 1, p.err, abort)) return;
+      const int code = table[i];
+      const S5Unit U = s5_unit(bid + i * grid, p.H, G, geo);
+      uint8_t* sb = smem + lay.stage0 + s * lay.stage_bytes;
+      const bool skip = s5_skip(code);
+      const int nreq = skip ? 0 : (s5_nmem(code) + geo.rb - 1) / geo.rb;
+      const bool ck = i >= S5_NPRO && !skip;
+      mbar_arrive_expect_tx(&full[s], (ck ? uint32_t(HPU) * 16384u : 0u) + uint32_t(nreq * HPU) * box_bytes);
+      if (ck) s5_tma4(sb + lay.ck, &ck_map, 0, 0, U.hv0, U.b, &full[s]);
+      for (int j = 0; j < nreq; ++j)
+#pragma unroll
+        for (int e = 0; e < HPU; ++e)
+          s5_tma5(sb + lay.vr + e * 4096 + j * box_bytes, &vr_map, 0, 0, U.hv0 + e, j * geo.rb, U.b, &full[s]);
+    }
+    return;
+  }
+
+  if (warp <= S5_NCW) {
+    // =================== chain warps ===================
+    const int cw = warp - 1;
+    uint8_t* kbuf = smem + lay.kbuf0 + cw * 4096;
+    uint8_t* res = smem + lay.res0 + cw * lay.res_bytes;
+    for (int i = cw, k = 0; i < nu; i += S5_NCW, ++k) {
+      const int code = table[i];
+      const S5Unit U = s5_unit(bid + i * grid, p.H, G, geo);
+      const bool skip = s5_skip(code);
+      // the result block is free once the readout of this warp's previous unit is done
+      bool ok = k == 0 || s5_warp_wait(&rfree[cw], (k - 1) & 1, p.err, abort, lane);
+      const int nreq = (ok && !skip) ? (s5_nmem(code) + geo.rb - 1) / geo.rb : 0;
+      // every lane's earlier generic accesses to kbuf, ordered before the copy
+      // engine overwrites it
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&kfull[cw], uint32_t(nreq) * box_bytes);
+        for (int j = 0; j < nreq; ++j)
+          s5_tma5(kbuf + j * box_bytes, &kr_map, 0, 0, U.h, j * geo.rb, U.b, &kfull[cw]);
+      }
+      const S5In in = s5_fetch<FUSED, HPU>(p, U, ok ? code : (1 << 16), lane);
+      ok = s5_warp_wait(&kfull[cw], k & 1, p.err, abort, lane) && ok;
+      if (ok && !skip) s5_chain<FUSED, HPU>(p, U, code, in, kbuf, res, lay, lane);
+      __syncwarp();
+      if (lane == 0) s5_arrive(&cdone[cw]);
+    }
+    return;
+  }
+
+  // =================== readout team ===================
+  const int rw = warp - 1 - S5_NCW;
+  constexpr int MW = HPU;  // m-tiles per readout warp: 16 * HPU * 8 rows / (16 * 8 warps)
+  const int head_r = (rw * 16 * MW) >> 7;
+  const int rbase = (rw * 16 * MW) & 127;
+  float* ost = reinterpret_cast<float*>(smem + lay.ost0 + rw * 128);
+  for (int i = 0; i < nu; ++i) {
+    const int s = i % S5_NS;
+    const int cw = i % S5_NCW, k = i / S5_NCW;
+    const int code = table[i];
+    const S5Unit U = s5_unit(bid + i * grid, p.H, G, geo);
+    const bool skip = s5_skip(code);
+    float sc = 1.0f;
+    if (!skip && lane == 0)
+      sc = load_scalar(p.sc, int64_t(U.b) * p.sc_sb + int64_t(U.hv0 + head_r) * p.sc_sh +
+                                 int64_t(rbase / VBLOCK) * p.sc_sv,
+                       p.sc_dt);
+    bool ok = s5_warp_wait(&full[s], (i / S5_NS) & 1, p.err, abort, lane);
+    ok = s5_warp_wait(&cdone[cw], k & 1, p.err, abort, lane) && ok;
+    if (ok && !skip) {
+      const uint8_t* sb = smem + lay.stage0 + s * lay.stage_bytes;
+      const uint8_t* res = smem + lay.res0 + cw * lay.res_bytes;
+      const float* misc = reinterpret_cast<const float*>(res + lay.misc) + head_r * 4;
+      const float wsc = misc[0] * __shfl_sync(0xffffffffu, sc, 0);
+      s5_readout<MW, FUSED>(sb + lay.ck + head_r * 16384, sb + lay.vr + head_r * 4096,
+                            res + lay.t8 + head_r * 8 * T8STR,
+                            reinterpret_cast<const uint16_t*>(res + lay.cb + head_r * 96), wsc, misc[1],
+                            reinterpret_cast<const uint16_t*>(res + lay.vnew + head_r * 256), rbase,
+                            s5_nmem(code), ost, lane);
+      __syncwarp();
+      if (lane < 16 * MW) {
+        const int64_t oi = int64_t(U.b) * p.o_sb + int64_t(U.hv0 + head_r) * p.o_sh + int64_t(rbase + lane) * p.o_sv;
+        store_scalar(p.out, oi, p.o_dt, ost[lane]);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) {
+      s5_arrive(&empty[s]);
+      s5_arrive(&rfree[cw]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- host side
+static int s5_sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+  return n;
+}
+
+static bool s5_grid(const StepParams& p, int& grid, S5Layout& lay) {
+  const int nsm = s5_sm_count();
+  if (nsm <= 0) return false;
+  const S5Geo g = s5_geo(p.H, p.HV, p.L);
+  const int64_t total = int64_t(p.B) * p.H * g.upk;
+  if (total <= 0 || total > (int64_t(1) << 30)) return false;
+  grid = int(total < nsm ? total : nsm);
+  const int max_units = int((total + grid - 1) / grid);
+  lay = s5_layout(g, max_units);
+  return true;
+}
+
+bool step5_eligible(const StepParams& p, bool fused, bool f32ck) {
+  if (f32ck || p.L < 4 || p.L > STEP2_MAX_L) return false;
+  const int G = p.HV / p.H;
+  if (G != 1 && G % 2 != 0) return false;
+  if (p.ck_sb % 16 || p.ck_sh % 16 || reinterpret_cast<uintptr_t>(p.ck) % 16) return false;
+  // ring tensor maps: 16-byte aligned base and strides
+  if (reinterpret_cast<uintptr_t>(p.kr) % 16 || (p.kr_sb * 2) % 16 || (p.kr_st * 2) % 16 || (p.kr_sh * 2) % 16)
+    return false;
+  if (reinterpret_cast<uintptr_t>(p.vr) % 16 || (p.vr_sb * 2) % 16 || (p.vr_st * 2) % 16 || (p.vr_sh * 2) % 16)
+    return false;
+  if (fused) {
+    const int esz = p.mx_dt == GDNR_BF16 ? 2 : 4;
+    if (reinterpret_cast<uintptr_t>(p.mixed) % 16 || (p.mx_sb * esz) % 16) return false;
+  } else {
+    const int esz = p.q_dt == GDNR_BF16 ? 2 : 4;
+    if (reinterpret_cast<uintptr_t>(p.q) % 16 || (p.q_sb * esz) % 16 || (p.q_sh * esz) % 16) return false;
+  }
+  int grid;
+  S5Layout lay;
+  if (!s5_grid(p, grid, lay)) return false;
+  return lay.total <= MAX_DYN_SMEM;
+}
+
+using S5EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static S5EncodeFn s5_encode_fn() {
+  static S5EncodeFn fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<S5EncodeFn>(ptr);
+  }
+  return fn;
+}
+
+template <bool FUSED, int HPU>
+static cudaError_t s5_launch(const StepParams& p, const CUtensorMap& ck, const CUtensorMap& kr,
+                             const CUtensorMap& vr, int grid, uint32_t smem, bool pdl, cudaStream_t stream) {
+  auto kern = step5_kernel<FUSED, HPU>;
+  static int configured = 0;
+  if (int(smem) > configured) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return e;
+    configured = int(smem);
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(S5_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, p, ck, kr, vr);
+}
+
+cudaError_t launch_step5(const StepParams& p, bool fused, bool pdl, cudaStream_t stream) {
+  S5EncodeFn enc = s5_encode_fn();
+  if (!enc) return cudaErrorNotSupported;
+  const S5Geo g = s5_geo(p.H, p.HV, p.L);
+  int grid;
+  S5Layout lay;
+  if (!s5_grid(p, grid, lay)) return cudaErrorInvalidValue;
+  CUtensorMap ck, kr, vr;
+  {
+    // checkpoint [B][HV][V][K] e4m3: box = hpu whole 128 x 128 head tiles
+    const cuuint64_t dims[4] = {128, 128, cuuint64_t(p.HV), cuuint64_t(p.B)};
+    const cuuint64_t strides[3] = {128, cuuint64_t(p.ck_sh), cuuint64_t(p.ck_sb)};
+    const cuuint32_t box[4] = {128, 128, cuuint32_t(g.hpu), 1};
+    const cuuint32_t es[4] = {1, 1, 1, 1};
+    if (enc(&ck, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, p.ck, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
+  // rings [B][L][heads][128] bf16 viewed as [B][L][heads][2][64]: a box of rb
+  // slots lands as rb x 256-byte rows, each 128-byte half swizzled
+  auto ring_map = [&](CUtensorMap* m, void* base, int heads, int64_t s_head, int64_t s_slot, int64_t s_b) {
+    const cuuint64_t dims[5] = {64, 2, cuuint64_t(heads), cuuint64_t(p.L), cuuint64_t(p.B)};
+    const cuuint64_t strides[4] = {128, cuuint64_t(s_head * 2), cuuint64_t(s_slot * 2), cuuint64_t(s_b * 2)};
+    const cuuint32_t box[5] = {64, 2, 1, cuuint32_t(g.rb), 1};
+    const cuuint32_t es[5] = {1, 1, 1, 1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 5, base, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  };
+  if (ring_map(&kr, p.kr, p.H, p.kr_sh, p.kr_st, p.kr_sb) != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  if (ring_map(&vr, p.vr, p.HV, p.vr_sh, p.vr_st, p.vr_sb) != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  if (fused)
+    return g.hpu == 2 ? s5_launch<true, 2>(p, ck, kr, vr, grid, lay.total, pdl, stream)
+                      : s5_launch<true, 1>(p, ck, kr, vr, grid, lay.total, pdl, stream);
+  return g.hpu == 2 ? s5_launch<false, 2>(p, ck, kr, vr, grid, lay.total, pdl, stream)
+                    : s5_launch<false, 1>(p, ck, kr, vr, grid, lay.total, pdl, stream);
+}
+
+}  // namespace gdnr

@@ -41,6 +41,7 @@ STATUS_NAMES = {
 
 DEVERR_WAIT_TIMEOUT = 0x1
 DEVERR_BAD_POS = 0x2
+DEVERR_BAD_HINT = 0x4
 
 
 class Tensor(ctypes.Structure):
@@ -62,6 +63,8 @@ class ReplayArgs(ctypes.Structure):
         ("block_v", ctypes.c_int32),
         ("quant_divisor", ctypes.c_int32),
         ("error_flag", ctypes.c_void_p),
+        ("flush_hint", ctypes.c_int32),
+        ("launch_flags", ctypes.c_int32),
     ]
 
 
@@ -85,6 +88,8 @@ class StepArgs(ctypes.Structure):
                                       "scale", "k_ring", "v_ring", "g_ring", "beta_ring", "out", "q_out")] + [
         ("quant_divisor", ctypes.c_int32),
         ("error_flag", ctypes.c_void_p),
+        ("flush_hint", ctypes.c_int32),
+        ("launch_flags", ctypes.c_int32),
     ]
 
 

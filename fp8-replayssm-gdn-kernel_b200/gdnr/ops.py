@@ -41,6 +41,17 @@ def _divisor(mode: str | int) -> int:
         raise ValueError(f"quant_divisor must be one of {sorted(_DIVISOR)}") from None
 
 
+_FLUSH_HINT = {"auto": 0, "none": 1, "all": 2}
+LAUNCH_PDL = 0x1
+
+
+def _flush_hint(hint: str) -> int:
+    try:
+        return _FLUSH_HINT[hint]
+    except KeyError:
+        raise ValueError(f"flush_hint must be one of {sorted(_FLUSH_HINT)}") from None
+
+
 def _as_bhv(out: torch.Tensor) -> torch.Tensor:
     # accept the production layout [B,1,HV,V] as well as [B,HV,V]
     if out.dim() == 4 and out.shape[1] == 1:
@@ -71,6 +82,8 @@ def gdn_replay_fp8(
     out: torch.Tensor | None = None,
     quant_divisor: str = "oracle",
     error_flag: torch.Tensor | None = None,
+    flush_hint: str = "auto",
+    pdl: bool = False,
 ) -> torch.Tensor:
     """Replay (and, where ``flush[b]``, rebuild + re-quantise in place).
 
@@ -78,6 +91,13 @@ def gdn_replay_fp8(
     checkpoint_scale [B,HV,V/32] float16|float32, q [B,H,K], rings
     k [B,L,H,K] / v [B,L,HV,V] bf16, g/beta [B,L,HV], valid_len [B] int32,
     flush [B] bool.  Returns out [B,HV,V] in q's dtype unless ``out`` given.
+
+    ``flush_hint`` -- what the caller knows about ``flush``: "auto" (nothing),
+    "none" (no sequence flushes: one launch; a set flag is reported in the
+    device error word as ``GDNR_DEVERR_BAD_HINT`` and that sequence is left
+    unprocessed) or "all".  ``pdl`` launches with programmatic dependent
+    launch; only valid when the preceding kernel on the stream does not write
+    this call's checkpoint or scales.
     """
     del num_warps
     batch, _, _, _ = k_cache.shape
@@ -98,6 +118,8 @@ def gdn_replay_fp8(
     args.block_v = int(block_v)
     args.quant_divisor = _divisor(quant_divisor)
     args.error_flag = _err_ptr(error_flag)
+    args.flush_hint = _flush_hint(flush_hint)
+    args.launch_flags = LAUNCH_PDL if pdl else 0
     _lib.check(_lib.load().gdnr_replay(ctypes.byref(args), _lib.stream_handle(q.device)))
     return out
 
@@ -192,14 +214,23 @@ def gdn_fused_step(
     pos_out: torch.Tensor | None = None,
     quant_divisor: str = "oracle",
     error_flag: torch.Tensor | None = None,
+    flush_hint: str = "auto",
+    pdl: bool = False,
 ) -> torch.Tensor:
-    """One full-contract decode step in one launch.
+    """One full-contract decode step.
 
     Appends this token (prep of ``mixed_qkv``/``a``/``b``) to ring slot
     ``pos[b]``, replays slots ``0..pos[b]`` against the FP8 checkpoint, writes
     ``out`` [B,HV,V] (or [B,1,HV,V]), and when ``pos[b] == L-1`` rebuilds the
     state and re-quantises the checkpoint in place.  ``pos_out`` (optional,
     distinct from ``pos``) receives ``(pos+1) % L``.
+
+    ``flush_hint``: "auto" (some sequences may be at ``L-1``: the
+    non-flushing heads and the flushing heads run as two launches), "none"
+    (no ``pos[b] == L-1``: one launch; a violation is reported in the device
+    error word as ``GDNR_DEVERR_BAD_HINT`` and that sequence is left
+    unprocessed) or "all" (one launch of the flush-capable kernel).  ``pdl``
+    as in :func:`gdn_replay_fp8`.
     """
     batch = mixed_qkv.shape[0]
     value_heads = v_ring.shape[2]
@@ -223,6 +254,8 @@ def gdn_fused_step(
     args.q_out = _lib.tensor_desc(q_out)
     args.quant_divisor = _divisor(quant_divisor)
     args.error_flag = _err_ptr(error_flag)
+    args.flush_hint = _flush_hint(flush_hint)
+    args.launch_flags = LAUNCH_PDL if pdl else 0
     _lib.check(_lib.load().gdnr_fused_step(ctypes.byref(args), _lib.stream_handle(mixed_qkv.device)))
     return out
 

@@ -89,8 +89,10 @@ class ReplayState:
             if t is not None)
 
     def step(self, mixed_qkv, a, b, a_log, dt_bias, out=None, pos_out=None, q_out=None,
-             quant_divisor: str = "oracle", error_flag=None) -> torch.Tensor:
+             quant_divisor: str = "oracle", error_flag=None, flush_hint: str = "auto",
+             pdl: bool = False) -> torch.Tensor:
         """One fused decode step on this state (see :func:`gdnr.ops.gdn_fused_step`)."""
         return ops.gdn_fused_step(mixed_qkv, a, b, a_log, dt_bias, self.pos, self.checkpoint, self.scale,
                                   self.k_ring, self.v_ring, self.g_ring, self.beta_ring, out=out, q_out=q_out,
-                                  pos_out=pos_out, quant_divisor=quant_divisor, error_flag=error_flag)
+                                  pos_out=pos_out, quant_divisor=quant_divisor, error_flag=error_flag,
+                                  flush_hint=flush_hint, pdl=pdl)

@@ -57,6 +57,18 @@ typedef enum {
 /* Bits of the device error word (see error_flag below). */
 #define GDNR_DEVERR_WAIT_TIMEOUT 0x1u /* a bounded mbarrier wait gave up */
 #define GDNR_DEVERR_BAD_POS 0x2u      /* fused step: pos[b] outside [0, L) */
+#define GDNR_DEVERR_BAD_HINT 0x4u     /* flush_hint NONE but a sequence's ring was full */
+
+/* flush_hint: what the caller knows about which sequences flush in this call */
+#define GDNR_FLUSH_AUTO 0 /* unknown: every head is checked on the device */
+#define GDNR_FLUSH_NONE 1 /* no sequence flushes (a full ring is reported as GDNR_DEVERR_BAD_HINT) */
+#define GDNR_FLUSH_ALL 2  /* every sequence may flush */
+
+/* launch_flags */
+#define GDNR_LAUNCH_PDL 0x1 /* programmatic dependent launch: the kernel may start while the
+                               preceding kernel on the stream drains and read this call's
+                               checkpoint before that kernel completes.  Only valid when the
+                               preceding kernel does not write this call's checkpoint. */
 
 /* Strided view of a device (or, for validation only, any) buffer. */
 typedef struct {
@@ -82,6 +94,8 @@ typedef struct {
   int32_t block_v;        /* value rows per CTA: 32, 64 or 128 (0 -> 128) */
   int32_t quant_divisor;  /* 0: x/(amax/448) like ref.py:94; 1: x/fp16(amax/448) like kern.py:234 */
   uint32_t* error_flag;   /* optional device word, OR-ed with GDNR_DEVERR_* */
+  int32_t flush_hint;     /* GDNR_FLUSH_* */
+  int32_t launch_flags;   /* GDNR_LAUNCH_* */
 } gdnr_replay_args;
 
 int gdnr_replay(const gdnr_replay_args* args, void* stream);
@@ -124,6 +138,8 @@ typedef struct {
   gdnr_tensor q_out;      /* optional [B,H,K]: normalised q as the reference's prep writes it */
   int32_t quant_divisor;
   uint32_t* error_flag;
+  int32_t flush_hint;     /* GDNR_FLUSH_* */
+  int32_t launch_flags;   /* GDNR_LAUNCH_* */
 } gdnr_step_args;
 
 int gdnr_fused_step(const gdnr_step_args* args, void* stream);
