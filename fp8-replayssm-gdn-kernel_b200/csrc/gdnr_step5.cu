@@ -34,9 +34,9 @@
 namespace gdnr {
 
 constexpr int S5_NS = 4;    // checkpoint / value-ring stages
-constexpr int S5_NPRO = 2;  // stages requested before the first dependent load
 constexpr int S5_NCW = 7;   // chain warps
 constexpr int S5_NRW = 8;   // readout warps
+constexpr int S5_TEAM = S5_NRW / S5_NS;  // readout warps per stage
 constexpr int S5_THREADS = 32 * (1 + S5_NCW + S5_NRW);
 constexpr int S5_GSTR = 20;  // Gram scratch row (floats): 16 key columns + 3 query terms + pad
 constexpr float S5_LOG2E = 1.4426950408889634f;
@@ -62,9 +62,9 @@ __host__ __device__ inline S5Geo s5_geo(int H, int HV, int L) {
 //   [kbuf: key ring (4 KB)] x S5_NCW
 //   [res: t8 x hpu | cb x hpu | misc x hpu | vnew x hpu] x S5_NCW  (the t8 area
 //        doubles as the chain's q-split / Gram scratch before T is written)
-//   [ost: 32 floats] x S5_NRW
+//   [ost: 128 floats] x S5_NRW
 struct S5Layout {
-  uint32_t full, empty, kfull, cdone, rfree, abort, table;
+  uint32_t full, empty, kfull, cseq, rcnt, abort, table;
   uint32_t stage0, stage_bytes, ck, vr;
   uint32_t kbuf0;
   uint32_t res0, res_bytes, t8, cb, misc, vnew;
@@ -79,8 +79,8 @@ __host__ __device__ inline S5Layout s5_layout(const S5Geo& g, int max_units) {
   s.full = smem_take(o, S5_NS * 8);
   s.empty = smem_take(o, S5_NS * 8);
   s.kfull = smem_take(o, S5_NCW * 8);
-  s.cdone = smem_take(o, S5_NCW * 8);
-  s.rfree = smem_take(o, S5_NCW * 8);
+  s.cseq = smem_take(o, S5_NCW * 4);
+  s.rcnt = smem_take(o, S5_NCW * 4);
   s.abort = smem_take(o, 16);
   s.table = smem_take(o, uint32_t(max_units) * 4u);
   o = (o + 1023u) & ~1023u;
@@ -103,7 +103,7 @@ __host__ __device__ inline S5Layout s5_layout(const S5Geo& g, int max_units) {
   s.res0 = o;
   o += S5_NCW * s.res_bytes;
   s.ost0 = o;
-  o += S5_NRW * 128u;
+  o += S5_NRW * 512u;
   s.total = o;
   return s;
 }
@@ -266,14 +266,14 @@ __device__ __forceinline__ void s5_tsplit(const float (*Tq)[4], uint8_t* t8, flo
 #pragma unroll
     for (int i = 0; i < 4; ++i) x[h][i] = Tq[h][i] * sig[h];
   }
-#pragma unroll
+#pragma unroll 1
   for (int j = 0; j < 5; ++j) {
 #pragma unroll
     for (int h = 0; h < HPU; ++h) {
       const uint32_t p01 = e4m3x2_sat(x[h][0], x[h][1]);
       const uint32_t p23 = e4m3x2_sat(x[h][2], x[h][3]);
       *reinterpret_cast<uint32_t*>(t8 + (h * 8 + j) * T8STR + lane * 4) = p01 | (p23 << 16);
-      if (j < 4) {
+      {
         const uint32_t h01 = e4m3x2_to_f16x2(p01), h23 = e4m3x2_to_f16x2(p23);
         const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&h01));
         const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&h23));
@@ -292,27 +292,38 @@ __device__ __forceinline__ void s5_tsplit(const float (*Tq)[4], uint8_t* t8, flo
   }
 }
 
+// Raw bits of one element of a F32 / BF16 / F16 tensor: the load completes
+// in the background; s5_cvt turns it into a float where it is first needed.
+__device__ __forceinline__ uint32_t s5_ld_raw(const void* p, int64_t i, int dtype) {
+  return dtype == GDNR_F32 ? static_cast<const uint32_t*>(p)[i] : uint32_t(static_cast<const uint16_t*>(p)[i]);
+}
+
+__device__ __forceinline__ float s5_cvt(uint32_t raw, int dtype) {
+  if (dtype == GDNR_F32) return __uint_as_float(raw);
+  if (dtype == GDNR_BF16) return bf16_to_f(uint16_t(raw));
+  return __half2float(__ushort_as_half(uint16_t(raw)));
+}
+
 // Per-lane raw inputs of one unit for its chain warp (lane 16 e + t: head e,
-// ring slot t), loaded as soon as the unit is known.
+// ring slot t), issued as soon as the unit is known and consumed only inside
+// the chain, so that no warp stalls on them early.
 struct S5In {
-  uint4 q, k;              // query / key rows, 4 elements per lane
-  uint4 v0, v1;            // this token's value rows of heads 0 and 1 (fused)
-  float g, beta;           // gates of (head e, slot t) for slots read from memory
-  float a, bb, alog, dtb;  // this token's gate inputs of head e (fused)
+  uint4 q, k;         // query / key rows, 4 elements per lane
+  uint4 v0, v1;       // this token's value rows of heads 0 and 1 (fused)
+  uint32_t g, beta;   // gates of (head e, slot min(t, L-1))
+  uint32_t a, bb;     // this token's gate inputs of head e (fused)
+  float alog, dtb;
+  int pos, flag;      // ring position (fused) / valid_len and flush (replay)
 };
 
 template <bool FUSED, int HPU>
-__device__ __forceinline__ S5In s5_fetch(const StepParams& p, const S5Unit& U, int code, int lane) {
+__device__ __forceinline__ S5In s5_fetch(const StepParams& p, const S5Unit& U, int lane) {
   S5In in;
-  in.q = in.k = in.v0 = in.v1 = make_uint4(0u, 0u, 0u, 0u);
-  in.g = in.beta = in.a = in.bb = in.alog = in.dtb = 0.0f;
-  if (s5_skip(code)) return in;
   const int e = lane >> 4, t = lane & 15;
   const int hv = U.hv0 + (e < HPU ? e : 0);
-  if (e < HPU && t < s5_nmem(code)) {
-    in.g = load_scalar(p.gr, int64_t(U.b) * p.gr_sb + int64_t(t) * p.gr_st + int64_t(hv) * p.gr_sh, p.gr_dt);
-    in.beta = load_scalar(p.br, int64_t(U.b) * p.br_sb + int64_t(t) * p.br_st + int64_t(hv) * p.br_sh, p.br_dt);
-  }
+  const int ts = t < p.L ? t : p.L - 1;
+  in.g = s5_ld_raw(p.gr, int64_t(U.b) * p.gr_sb + int64_t(ts) * p.gr_st + int64_t(hv) * p.gr_sh, p.gr_dt);
+  in.beta = s5_ld_raw(p.br, int64_t(U.b) * p.br_sb + int64_t(ts) * p.br_st + int64_t(hv) * p.br_sh, p.br_dt);
   if constexpr (FUSED) {
     const bool bf = p.mx_dt == GDNR_BF16;
     const int64_t row = int64_t(U.b) * p.mx_sb;
@@ -320,29 +331,131 @@ __device__ __forceinline__ S5In s5_fetch(const StepParams& p, const S5Unit& U, i
     in.k = s5_load4(p.mixed, row + int64_t(p.H + U.h) * KD + 4 * lane, bf);
     const int64_t vrow = row + 2 * int64_t(p.H) * KD + int64_t(U.hv0) * VD + 4 * lane;
     in.v0 = s5_load4(p.mixed, vrow, bf);
-    if (HPU == 2) in.v1 = s5_load4(p.mixed, vrow + VD, bf);
-    in.a = load_scalar(p.a, int64_t(U.b) * p.a_sb + int64_t(hv) * p.a_sh, p.a_dt);
-    in.bb = load_scalar(p.bb, int64_t(U.b) * p.b_sb + int64_t(hv) * p.b_sh, p.b_dt);
+    in.v1 = s5_load4(p.mixed, vrow + (HPU == 2 ? VD : 0), bf);
+    in.a = s5_ld_raw(p.a, int64_t(U.b) * p.a_sb + int64_t(hv) * p.a_sh, p.a_dt);
+    in.bb = s5_ld_raw(p.bb, int64_t(U.b) * p.b_sb + int64_t(hv) * p.b_sh, p.b_dt);
     in.alog = p.a_log[int64_t(hv) * p.al_s];
     in.dtb = p.dt_bias[int64_t(hv) * p.db_s];
+    in.pos = p.pos[int64_t(U.b) * p.pos_s];
+    in.flag = 0;
   } else {
     in.q = s5_load4(p.q, int64_t(U.b) * p.q_sb + int64_t(U.h) * p.q_sh + 4 * lane, p.q_dt == GDNR_BF16);
+    in.k = in.v0 = in.v1 = make_uint4(0u, 0u, 0u, 0u);
+    in.a = in.bb = 0u;
+    in.alog = in.dtb = 0.0f;
+    in.pos = p.valid_len[int64_t(U.b) * p.vl_s];
+    in.flag = (p.fl_dt == GDNR_I32) ? static_cast<const int32_t*>(p.flush)[int64_t(U.b) * p.fl_s]
+                                    : int(static_cast<const uint8_t*>(p.flush)[int64_t(U.b) * p.fl_s]);
   }
   return in;
+}
+
+// Unit descriptor (see s5_n / s5_nmem / s5_skip) from its raw position inputs.
+template <bool FUSED>
+__device__ __forceinline__ int s5_code(int raw, int flag, int L) {
+  if constexpr (FUSED) {
+    if (raw < 0 || raw >= L) return 1 << 16;
+    return (raw + 1) | (raw << 8) | ((raw == L - 1 ? 1 : 0) << 16);
+  } else {
+    const int v = raw < 0 ? 0 : (raw > L ? L : raw);
+    return v | (v << 8) | ((flag != 0 ? 1 : 0) << 16);
+  }
+}
+
+// This token's ring append and query output (fused), written to HBM after
+// the chain has handed its results to the readout.
+struct S5Append {
+  uint2 kw;        // normalised key (bf16), 4 elements per lane
+  uint2 vw[2];     // value rows of heads 0 and 1 (bf16)
+  float g, beta;   // gates of (head lane/16, slot pos) on lane pos
+  float qv[4];     // normalised query
+};
+
+template <bool FUSED, int HPU>
+__device__ __forceinline__ void s5_append(const StepParams& p, const S5Unit& U, int code, const S5Append& a,
+                                          int lane) {
+  if constexpr (FUSED) {
+    const int pos = s5_nmem(code);
+    const int e = lane >> 4, t = lane & 15;
+    const bool owner = U.pp == 0;
+    if (owner) {
+      *reinterpret_cast<uint2*>(p.kr + int64_t(U.b) * p.kr_sb + int64_t(pos) * p.kr_st + int64_t(U.h) * p.kr_sh +
+                                4 * lane) = a.kw;
+      if (p.q_out) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          store_scalar(p.q_out, int64_t(U.b) * p.qo_sb + int64_t(U.h) * p.qo_sh + 4 * lane + i, p.qo_dt, a.qv[i]);
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < HPU; ++h)
+      *reinterpret_cast<uint2*>(p.vr + int64_t(U.b) * p.vr_sb + int64_t(pos) * p.vr_st +
+                                int64_t(U.hv0 + h) * p.vr_sh + 4 * lane) = a.vw[h];
+    if (t == pos && e < HPU) {
+      const int hv = U.hv0 + e;
+      store_scalar(p.gr, int64_t(U.b) * p.gr_sb + int64_t(pos) * p.gr_st + int64_t(hv) * p.gr_sh, p.gr_dt, a.g);
+      store_scalar(p.br, int64_t(U.b) * p.br_sb + int64_t(pos) * p.br_st + int64_t(hv) * p.br_sh, p.br_dt, a.beta);
+      if (p.pos_out && hv == 0) p.pos_out[int64_t(U.b) * p.po_s] = (pos + 1) % p.L;
+    }
+  }
+}
+
+// Triangular solve and transformed query of both heads (lane 16 e + t), with
+// NSTEP = 8 or 16 ring slots (slots >= n carry zero gates and keys, so the
+// steps run unconditionally).  em[j] = M[t][j] for the lane's row t.
+__device__ __forceinline__ void s5_solve(const float* em, float bsel, float& acc, float& cval, int t) {
+#pragma unroll
+  for (int j = 15; j >= 0; --j) {
+    const float cj = __shfl_sync(0xffffffffu, bsel * acc, j, 16);
+    if (t == j) cval = cj;
+    if (t < j) acc = fmaf(-cj, em[j], acc);
+  }
+}
+
+template <int HPU>
+__device__ __forceinline__ void s5_tloop(const uint8_t* kbuf, float wj, int n, float (*T)[4], int lane) {
+  const int half = lane >> 4, c16 = (lane & 15) >> 1;
+  const uint8_t* kbase = kbuf + half * 128 + (lane & 1) * 8;
+#pragma unroll 1
+  for (int j0 = 0; j0 < n; j0 += 4) {
+    float w[HPU][4];
+    uint2 kw[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int j = j0 + q;
+#pragma unroll
+      for (int h = 0; h < HPU; ++h) w[h][q] = __shfl_sync(0xffffffffu, wj, 16 * h + (j & 15));
+      const int R = 2 * j + half;
+      kw[q] = *reinterpret_cast<const uint2*>(kbase + (j & 15) * 256 + ((c16 ^ (R & 7)) << 4));
+      if (j >= n) kw[q] = make_uint2(0u, 0u);  // stale slot (its weight is zero too)
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 k01 = bf16x2_to_f2(kw[q].x), k23 = bf16x2_to_f2(kw[q].y);
+#pragma unroll
+      for (int h = 0; h < HPU; ++h) {
+        T[h][0] = fmaf(-w[h][q], k01.x, T[h][0]);
+        T[h][1] = fmaf(-w[h][q], k01.y, T[h][1]);
+        T[h][2] = fmaf(-w[h][q], k23.x, T[h][2]);
+        T[h][3] = fmaf(-w[h][q], k23.y, T[h][3]);
+      }
+    }
+  }
 }
 
 // The chain of one unit (one warp, both heads).  kbuf: the unit's key ring
 // (swizzled, slots < nmem loaded); res: this warp's result block.
 template <bool FUSED, int HPU>
-__device__ __forceinline__ void s5_chain(const StepParams& p, const S5Unit& U, int code, const S5In& in,
-                                         uint8_t* kbuf, uint8_t* res, const S5Layout& lay, int lane) {
+__device__ __forceinline__ S5Append s5_chain(const StepParams& p, const S5Unit& U, int code, const S5In& in,
+                                             uint8_t* kbuf, uint8_t* res, const S5Layout& lay, int lane) {
+  S5Append ap;
   const int g8 = lane >> 2, t4 = lane & 3;
   const int e = lane >> 4, t = lane & 15;
   const int n = s5_n(code), nmem = s5_nmem(code);
   uint16_t* qb = reinterpret_cast<uint16_t*>(res + lay.t8 + lay.qb);
   float* gram = reinterpret_cast<float*>(res + lay.t8 + lay.gram);
   float* misc = reinterpret_cast<float*>(res + lay.misc);
-  float g_own = in.g, beta_own = in.beta;  // gates of (head e, slot t)
+  float g_own = s5_cvt(in.g, p.gr_dt), beta_own = s5_cvt(in.beta, p.br_dt);  // gates of (head e, slot t)
   float qv[4];
   if constexpr (FUSED) {
     const int L = p.L;
@@ -350,10 +463,10 @@ __device__ __forceinline__ void s5_chain(const StepParams& p, const S5Unit& U, i
     const bool bf = p.mx_dt == GDNR_BF16;
     // this token's gates for head e (every lane; slot pos keeps them)
     {
-      const float xg = in.a + in.dtb;
+      const float xg = s5_cvt(in.a, p.a_dt) + in.dtb;
       const float sp = (xg <= SOFTPLUS_THRESHOLD) ? logf(1.0f + expf(xg)) : xg;
       const float gn = round_to(-expf(in.alog) * sp, p.gr_dt);
-      const float bn = round_to(1.0f / (1.0f + expf(-in.bb)), p.br_dt);
+      const float bn = round_to(1.0f / (1.0f + expf(-s5_cvt(in.bb, p.b_dt))), p.br_dt);
       if (t == pos) {
         g_own = gn;
         beta_own = bn;
@@ -368,35 +481,24 @@ __device__ __forceinline__ void s5_chain(const StepParams& p, const S5Unit& U, i
     const float ks2 = warp_sum(y[0] * y[0] + y[1] * y[1] + y[2] * y[2] + y[3] * y[3]);
     const float qi = __frcp_rn(sqrtf(qs2 + L2_EPS)), ki = __frcp_rn(sqrtf(ks2 + L2_EPS));
     const int qdt = p.q_out ? p.qo_dt : GDNR_BF16;
-    const bool owner = U.pp == 0;
 #pragma unroll
     for (int i = 0; i < 4; ++i) qv[i] = round_to(x[i] * qi, qdt);
-    if (owner && p.q_out) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        store_scalar(p.q_out, int64_t(U.b) * p.qo_sb + int64_t(U.h) * p.qo_sh + 4 * lane + i, qdt, qv[i]);
-    }
     const uint2 kw = make_uint2(pack_bf16x2(y[0] * ki, y[1] * ki), pack_bf16x2(y[2] * ki, y[3] * ki));
     *reinterpret_cast<uint2*>(kbuf + s5_ring_off(pos, 4 * lane)) = kw;
-    if (owner)
-      *reinterpret_cast<uint2*>(p.kr + int64_t(U.b) * p.kr_sb + int64_t(pos) * p.kr_st + int64_t(U.h) * p.kr_sh +
-                                4 * lane) = kw;
-    // this token's value rows: ring slot pos in HBM, and the readout's rank-one term
+    ap.kw = kw;
+    // this token's value rows: the readout's rank-one term (HBM ring slot later)
 #pragma unroll
     for (int h = 0; h < HPU; ++h) {
       float vv[4];
       s5_unpack4(h == 0 ? in.v0 : in.v1, bf, vv);
       const uint2 vw = make_uint2(pack_bf16x2(vv[0], vv[1]), pack_bf16x2(vv[2], vv[3]));
       *reinterpret_cast<uint2*>(res + lay.vnew + h * 256 + 8 * lane) = vw;
-      *reinterpret_cast<uint2*>(p.vr + int64_t(U.b) * p.vr_sb + int64_t(pos) * p.vr_st +
-                                int64_t(U.hv0 + h) * p.vr_sh + 4 * lane) = vw;
+      ap.vw[h] = vw;
     }
-    if (t == pos && e < HPU) {
-      const int hv = U.hv0 + e;
-      store_scalar(p.gr, int64_t(U.b) * p.gr_sb + int64_t(pos) * p.gr_st + int64_t(hv) * p.gr_sh, p.gr_dt, g_own);
-      store_scalar(p.br, int64_t(U.b) * p.br_sb + int64_t(pos) * p.br_st + int64_t(hv) * p.br_sh, p.br_dt, beta_own);
-      if (p.pos_out && hv == 0) p.pos_out[int64_t(U.b) * p.po_s] = (pos + 1) % L;
-    }
+    ap.g = g_own;
+    ap.beta = beta_own;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) ap.qv[i] = qv[i];
   } else {
     s5_unpack4(in.q, p.q_dt == GDNR_BF16, qv);
   }
@@ -425,7 +527,7 @@ __device__ __forceinline__ void s5_chain(const StepParams& p, const S5Unit& U, i
       for (int i = 0; i < 4; ++i) gacc[nt][i] = 0.0f;
     const int mi = lane >> 3;
     const int trow = (lane & 7) + 8 * (mi & 1);
-#pragma unroll
+#pragma unroll 2
     for (int ks = 0; ks < 8; ++ks) {
       uint32_t a[4];
       s5_ldsm_x4(kr_addr + s5_ring_off(trow, 16 * ks + 8 * (mi >> 1)), a);
@@ -479,18 +581,11 @@ __device__ __forceinline__ void s5_chain(const StepParams& p, const S5Unit& U, i
   const float bsel = t < n ? beta_own : 0.0f;
   float acc = t < n ? s5_ex2(Llast - Lg) * kq : 0.0f;
   float cval = 0.0f;
-  // ---- triangular solve, j = n-1 .. 0: c_j = beta_j (d_j kq_j - sum_{m>j} c_m M[j][m]).
-  // Slots j >= n carry c_j = 0 (beta masked), so the steps run unconditionally.
-  const int jtop = n > 8 ? 15 : 7;
+  // ---- triangular solve, j = n-1 .. 0: c_j = beta_j (d_j kq_j - sum_{m>j} c_m M[j][m])
+  float em[16];
 #pragma unroll
-  for (int j = 15; j >= 0; --j) {
-    if (j <= jtop) {
-      const float Lj = __shfl_sync(0xffffffffu, Lg, j, 16);
-      const float cj = __shfl_sync(0xffffffffu, bsel * acc, j, 16);
-      if (t == j) cval = cj;
-      if (t < j) acc = fmaf(-cj, s5_ex2(Lj - Lg) * grow[j], acc);
-    }
-  }
+  for (int j = 0; j < 16; ++j) em[j] = s5_ex2(__shfl_sync(0xffffffffu, Lg, j, 16) - Lg) * grow[j];
+  s5_solve(em, bsel, acc, cval, t);
   // ---- c -> [c_hi; c_mid; c_lo] bf16 over the slots read from memory (ring
   // columns of the readout); this token's own slot is a rank-one term
   if (e < HPU) {
@@ -518,37 +613,19 @@ __device__ __forceinline__ void s5_chain(const StepParams& p, const S5Unit& U, i
 #pragma unroll
     for (int i = 0; i < 4; ++i) T[h][i] = al * qv[i];
   }
-  {
-    const int half = lane >> 4, c16 = (lane & 15) >> 1;
-    const uint8_t* kbase = kbuf + half * 128 + (lane & 1) * 8;
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      if (j <= jtop) {
-        const int R = 2 * j + half;
-        uint2 kw = *reinterpret_cast<const uint2*>(kbase + j * 256 + ((c16 ^ (R & 7)) << 4));
-        if (j >= n) kw = make_uint2(0u, 0u);  // stale or unloaded slot
-        const float2 k01 = bf16x2_to_f2(kw.x), k23 = bf16x2_to_f2(kw.y);
-#pragma unroll
-        for (int h = 0; h < HPU; ++h) {
-          const float w = __shfl_sync(0xffffffffu, wj, 16 * h + j);
-          T[h][0] = fmaf(-w, k01.x, T[h][0]);
-          T[h][1] = fmaf(-w, k01.y, T[h][1]);
-          T[h][2] = fmaf(-w, k23.x, T[h][2]);
-          T[h][3] = fmaf(-w, k23.y, T[h][3]);
-        }
-      }
-    }
-  }
+  s5_tloop<HPU>(kbuf, wj, n, T, lane);
   __syncwarp();  // q-split / Gram scratch (aliases t8) is dead from here on
   s5_tsplit<HPU>(T, res + lay.t8, misc, lane);
+  return ap;
 }
 
-// Readout of MW m-tiles (rows rbase .. rbase + 16 MW - 1, one vblock) of one
-// head by one warp.  Leaves o(row) in ost[0 .. 16 MW).
-template <int MW, bool FUSED>
+// Readout of MW m-tiles (rows rbase .. rbase + 16 MW - 1) of one head by one
+// warp: pre-scale o(row) = (S_fp8 . T) / sigma * scale(row) + V^T c into ost[row].
+// Lane sc_base + v of sc holds the scale of vblock v of these rows.
+template <int MW>
 __device__ __forceinline__ void s5_readout(const uint8_t* ck_s, const uint8_t* vr_s, const uint8_t* t8,
-                                           const uint16_t* cb, float wsc, float cpos, const uint16_t* vnew,
-                                           int rbase, int nmem, float* ost, int lane) {
+                                           const uint16_t* cb, float inv_sig, float sc, int sc_base, int rbase,
+                                           int nmem, float* ost, int lane) {
   const int g8 = lane >> 2, t4 = lane & 3;
   uint32_t bt[4][2];
 #pragma unroll
@@ -565,71 +642,93 @@ __device__ __forceinline__ void s5_readout(const uint8_t* ck_s, const uint8_t* v
   const uint32_t mk1 = (t1 < nmem ? 0x0000ffffu : 0u) | (t1 + 1 < nmem ? 0xffff0000u : 0u);
   const uint32_t ck_addr = smem_addr(ck_s), vr_addr = smem_addr(vr_s);
   const int mi = lane >> 3, r8 = lane & 7;
-  float acc[MW][4];
+  // m-tiles in pairs (one vblock of 32 rows per pair)
+#pragma unroll 1
+  for (int pr = 0; pr < MW / 2; ++pr) {
+    const int rp = rbase + 32 * pr;
+    float acc[2][4];
 #pragma unroll
-  for (int m = 0; m < MW; ++m)
+    for (int m = 0; m < 2; ++m)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) acc[m][i] = 0.0f;
+      for (int i = 0; i < 4; ++i) acc[m][i] = 0.0f;
 #pragma unroll
-  for (int ks = 0; ks < 4; ++ks) {
+    for (int ks = 0; ks < 4; ++ks) {
 #pragma unroll
-    for (int m = 0; m < MW; ++m) {
-      uint32_t a[4];
-      const int row = rbase + 16 * m + r8 + 8 * (mi & 1);
-      s5_ldsm_x4(ck_addr + s0_off(row, 2 * ks + (mi >> 1)), a);
-      mma16832_e4m3(acc[m], a, bt[ks][0], bt[ks][1]);
-    }
-  }
-#pragma unroll
-  for (int m = 0; m < MW; ++m) {
-    uint32_t a[4];
-    s5_ldsm_x4_t(vr_addr + s5_ring_off(r8 + 8 * (mi >> 1), rbase + 16 * m + 8 * (mi & 1)), a);
-    a[0] &= mk0;
-    a[1] &= mk0;
-    a[2] &= mk1;
-    a[3] &= mk1;
-    mma16816_bf16(acc[m], a, rb0, rb1);
-  }
-  // column weights: t4 = 0 -> terms 0,1; 1 -> terms 2,3; 2 -> term 4, ring; 3 -> ring, ring
-  const float w0 = t4 == 0 ? wsc : (t4 == 1 ? wsc * (1.0f / 256.0f) : (t4 == 2 ? wsc * (1.0f / 65536.0f) : 1.0f));
-  const float w1 = t4 == 0 ? wsc * (1.0f / 16.0f) : (t4 == 1 ? wsc * (1.0f / 4096.0f) : 1.0f);
-  float o[MW][2];
-#pragma unroll
-  for (int m = 0; m < MW; ++m) {
-    o[m][0] = fmaf(acc[m][1], w1, acc[m][0] * w0);
-    o[m][1] = fmaf(acc[m][3], w1, acc[m][2] * w0);
-  }
-  // quad sums, spread so that lane t4 ends with value t4 & (2 MW - 1) of the list
-  // (m0 row g8, m0 row g8+8, m1 row g8, m1 row g8+8)
-  const bool odd = t4 & 1;
-  if constexpr (MW == 2) {
-    float x0 = odd ? o[1][0] : o[0][0], x1 = odd ? o[1][1] : o[0][1];
-    const float y0 = odd ? o[0][0] : o[1][0], y1 = odd ? o[0][1] : o[1][1];
-    x0 += __shfl_xor_sync(0xffffffffu, y0, 1);
-    x1 += __shfl_xor_sync(0xffffffffu, y1, 1);
-    x0 += __shfl_xor_sync(0xffffffffu, x0, 2);
-    x1 += __shfl_xor_sync(0xffffffffu, x1, 2);
-    // lanes t4 = 0 (m-tile 0) and 1 (m-tile 1) write rows g8 and g8 + 8
-    if (t4 < 2) {
-      const int r0 = 16 * t4 + g8;
-      if (FUSED) {
-        x0 = fmaf(cpos, bf16_to_f(vnew[rbase + r0]), x0);
-        x1 = fmaf(cpos, bf16_to_f(vnew[rbase + r0 + 8]), x1);
+      for (int m = 0; m < 2; ++m) {
+        uint32_t a[4];
+        s5_ldsm_x4(ck_addr + s0_off(rp + 16 * m + r8 + 8 * (mi & 1), 2 * ks + (mi >> 1)), a);
+        mma16832_e4m3(acc[m], a, bt[ks][0], bt[ks][1]);
       }
-      ost[r0] = x0 * KSCALE_H;
-      ost[r0 + 8] = x1 * KSCALE_H;
     }
-  } else {
-    float x = odd ? o[0][1] : o[0][0];
-    const float y = odd ? o[0][0] : o[0][1];
-    x += __shfl_xor_sync(0xffffffffu, y, 1);
-    x += __shfl_xor_sync(0xffffffffu, x, 2);
-    if (t4 < 2) {
-      const int r = g8 + 8 * t4;
-      if (FUSED) x = fmaf(cpos, bf16_to_f(vnew[rbase + r]), x);
-      ost[r] = x * KSCALE_H;
+#pragma unroll
+    for (int m = 0; m < 2; ++m) {
+      uint32_t a[4];
+      s5_ldsm_x4_t(vr_addr + s5_ring_off(r8 + 8 * (mi >> 1), rp + 16 * m + 8 * (mi & 1)), a);
+      a[0] &= mk0;
+      a[1] &= mk0;
+      a[2] &= mk1;
+      a[3] &= mk1;
+      mma16816_bf16(acc[m], a, rb0, rb1);
+    }
+    // column weights: t4 = 0 -> terms 0,1; 1 -> terms 2,3; 2 -> term 4, ring; 3 -> ring, ring
+    const float wsc = inv_sig * __shfl_sync(0xffffffffu, sc, sc_base + pr);
+    const float w0 = t4 == 0 ? wsc : (t4 == 1 ? wsc * (1.0f / 256.0f) : (t4 == 2 ? wsc * (1.0f / 65536.0f) : 1.0f));
+    const float w1 = t4 == 0 ? wsc * (1.0f / 16.0f) : (t4 == 1 ? wsc * (1.0f / 4096.0f) : 1.0f);
+    // v = (m0 row g8, m0 row g8+8, m1 row g8, m1 row g8+8), summed over the quad as a
+    // transpose-reduce: lane t4 ends with m-tile t4 & 1, row half t4 >> 1
+    const float v0 = fmaf(acc[0][1], w1, acc[0][0] * w0), v1 = fmaf(acc[0][3], w1, acc[0][2] * w0);
+    const float v2 = fmaf(acc[1][1], w1, acc[1][0] * w0), v3 = fmaf(acc[1][3], w1, acc[1][2] * w0);
+    const bool odd = t4 & 1;
+    float x0 = odd ? v2 : v0, x1 = odd ? v3 : v1;
+    x0 += __shfl_xor_sync(0xffffffffu, odd ? v0 : v2, 1);
+    x1 += __shfl_xor_sync(0xffffffffu, odd ? v1 : v3, 1);
+    const bool hi = t4 & 2;
+    float r = hi ? x1 : x0;
+    r += __shfl_xor_sync(0xffffffffu, hi ? x0 : x1, 2);
+    ost[32 * pr + 16 * (t4 & 1) + g8 + 8 * (t4 >> 1)] = r;
+  }
+}
+
+__device__ __forceinline__ uint32_t s5_ld_acquire(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_addr(p)) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void s5_st_release(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_addr(p)), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void s5_add_release(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.cta.shared::cta.add.u32 [%0], %1;" ::"r"(smem_addr(p)), "r"(v) : "memory");
+}
+
+// Bounded wait (by lane 0, broadcast) for a shared counter to reach `target`.
+__device__ __forceinline__ bool s5_warp_wait_count(const uint32_t* c, uint32_t target, uint32_t* err,
+                                                   volatile int* abort, int lane) {
+  int ok = 1;
+  if (lane == 0 && s5_ld_acquire(c) < target) {
+    ok = 0;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 1; it < WAIT_LIMIT_ITERS; ++it) {
+      __nanosleep(32);
+      if (s5_ld_acquire(c) >= target) {
+        ok = 1;
+        break;
+      }
+      if ((it & 63u) == 0) {
+        if (*abort) break;
+        if (globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
+          *abort = 1;
+          atomicOr(err, GDNR_DEVERR_WAIT_TIMEOUT);
+          break;
+        }
+      }
     }
   }
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  __syncwarp();
+  return ok != 0;
 }
 
 template <bool FUSED, int HPU>
@@ -648,22 +747,23 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + lay.full);
   uint64_t* empty = reinterpret_cast<uint64_t*>(smem + lay.empty);
   uint64_t* kfull = reinterpret_cast<uint64_t*>(smem + lay.kfull);
-  uint64_t* cdone = reinterpret_cast<uint64_t*>(smem + lay.cdone);
-  uint64_t* rfree = reinterpret_cast<uint64_t*>(smem + lay.rfree);
+  uint32_t* cseq = reinterpret_cast<uint32_t*>(smem + lay.cseq);  // chains finished, per chain warp
+  uint32_t* rcnt = reinterpret_cast<uint32_t*>(smem + lay.rcnt);  // readout parts finished, per chain warp
   volatile int* abort = reinterpret_cast<volatile int*>(smem + lay.abort);
   int* table = reinterpret_cast<int*>(smem + lay.table);
   const bool aligned = (smem_addr(smem) & 1023u) == 0;  // swizzled TMA boxes need 1024-byte alignment
   const uint32_t box_bytes = uint32_t(geo.rb) * 256u;
+  const uint32_t ck_bytes = uint32_t(HPU) * 16384u;
 
   if (tid == 0) {
     for (int s = 0; s < S5_NS; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], S5_NRW);
+      mbar_init(&empty[s], S5_TEAM);
     }
     for (int c = 0; c < S5_NCW; ++c) {
       mbar_init(&kfull[c], 1);
-      mbar_init(&cdone[c], 1);
-      mbar_init(&rfree[c], S5_NRW);
+      cseq[c] = 0;
+      rcnt[c] = 0;
     }
     *abort = aligned ? 0 : 1;
     fence_mbar_init();
@@ -672,46 +772,91 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
   __syncthreads();
   if (!aligned) return;
 
-  // ---- prologue: checkpoint tiles of the first units (decode state, not
-  // output of the preceding kernel; see GDNR_LAUNCH_PDL)
-  const int npro = nu < S5_NPRO ? nu : S5_NPRO;
-  if (warp == 0 && lane == 0) {
+  // Checkpoint tiles of the first stages: decode state, not output of the
+  // preceding kernel (see GDNR_LAUNCH_PDL), so under programmatic dependent
+  // launch they stream while that kernel drains.
+  const int npro = nu < S5_NS ? nu : S5_NS;
+  auto prologue = [&]() {
     for (int i = 0; i < npro; ++i) {
       const S5Unit U = s5_unit(bid + i * grid, p.H, G, geo);
-      s5_expect_tx(&full[i], uint32_t(HPU) * 16384u);
+      s5_expect_tx(&full[i], ck_bytes);
       s5_tma4(smem + lay.stage0 + i * lay.stage_bytes + lay.ck, &ck_map, 0, 0, U.hv0, U.b, &full[i]);
     }
-  }
+  };
+  if (p.pdl && warp == 0 && lane == 0) prologue();
   griddep_wait();
-  for (int i = tid; i < nu; i += blockDim.x) {
+  // Chain warps: the first unit's inputs and whole key ring (small, on the
+  // critical path) go out before the checkpoint stream.
+  const int cw = warp - 1;
+  const bool chain_warp = warp >= 1 && warp <= S5_NCW;
+  const int nreq_k = (L + geo.rb - 1) / geo.rb;
+  uint8_t* kbuf = smem + lay.kbuf0 + (chain_warp ? cw : 0) * 4096;
+  S5In in0;
+  if (chain_warp) {
+    const int i0 = cw < nu ? cw : 0;
+    const S5Unit U = s5_unit(bid + i0 * grid, p.H, G, geo);
+    if (lane == 0) {
+      const int nr = cw < nu ? nreq_k : 0;
+      mbar_arrive_expect_tx(&kfull[cw], uint32_t(nr) * box_bytes);
+      for (int j = 0; j < nr; ++j) s5_tma5(kbuf + j * box_bytes, &kr_map, 0, 0, U.h, j * geo.rb, U.b, &kfull[cw]);
+    }
+    in0 = s5_fetch<FUSED, HPU>(p, U, lane);
+  }
+  // readout warps: vblock scales of their first units (lane l: team unit
+  // l / (2 HPU), vblock l % (2 HPU) of the warp's rows), raw until used
+  constexpr int VBW = 2 * HPU;  // vblocks per readout warp and unit
+  constexpr int SC_UNITS = 32 / VBW;
+  uint32_t scl_raw = 0u;
+  const int rw = warp - 1 - S5_NCW;
+  const int team = rw / S5_TEAM, mem = rw % S5_TEAM;
+  const int head_r = HPU == 2 ? mem : 0;
+  const int rbase = HPU == 2 ? 0 : 64 * mem;
+  if (warp > S5_NCW) {
+    int i = team + S5_NS * (lane / VBW);
+    i = i < nu ? i : 0;
     const S5Unit U = s5_unit(bid + i * grid, p.H, G, geo);
-    int n, nmem, skip = 0;
-    bool flush = false;
+    scl_raw = s5_ld_raw(p.sc, int64_t(U.b) * p.sc_sb + int64_t(U.hv0 + head_r) * p.sc_sh +
+                                  int64_t(rbase / VBLOCK + lane % VBW) * p.sc_sv,
+                        p.sc_dt);
+  }
+  // ring positions of this CTA's units for the producer and the readout, read
+  // by the threads from the top of the block down
+  const int ti = S5_THREADS - 1 - tid;
+  int raw0 = 0, raw1 = 0;
+  if (ti < nu) {
+    const S5Unit U = s5_unit(bid + ti * grid, p.H, G, geo);
     if constexpr (FUSED) {
-      const int pv = p.pos[int64_t(U.b) * p.pos_s];
-      if (pv < 0 || pv >= L) {
-        n = nmem = 0;
-        skip = 1;
-        if (U.h == 0 && U.pp == 0) atomicOr(p.err, GDNR_DEVERR_BAD_POS);
-      } else {
-        n = pv + 1;
-        nmem = pv;
-        flush = pv == L - 1;
-      }
+      raw0 = p.pos[int64_t(U.b) * p.pos_s];
     } else {
-      const int v = p.valid_len[int64_t(U.b) * p.vl_s];
-      n = nmem = v < 0 ? 0 : (v > L ? L : v);
-      flush = (p.fl_dt == GDNR_I32) ? (static_cast<const int32_t*>(p.flush)[int64_t(U.b) * p.fl_s] != 0)
-                                    : (static_cast<const uint8_t*>(p.flush)[int64_t(U.b) * p.fl_s] != 0);
+      raw0 = p.valid_len[int64_t(U.b) * p.vl_s];
+      raw1 = (p.fl_dt == GDNR_I32) ? static_cast<const int32_t*>(p.flush)[int64_t(U.b) * p.fl_s]
+                                   : int(static_cast<const uint8_t*>(p.flush)[int64_t(U.b) * p.fl_s]);
     }
-    if (flush) {
-      skip = 1;
-      if (p.flush_hint == GDNR_FLUSH_NONE && U.h == 0 && U.pp == 0) atomicOr(p.err, GDNR_DEVERR_BAD_HINT);
-    }
-    table[i] = n | (nmem << 8) | (skip << 16);
   }
   __syncthreads();
+  // the checkpoint stream starts behind the small loads above
+  if (!p.pdl && warp == 0 && lane == 0) prologue();
   if (tid == 0) griddep_launch();
+  if (ti < nu) {
+    const S5Unit U = s5_unit(bid + ti * grid, p.H, G, geo);
+    const int code = s5_code<FUSED>(raw0, raw1, L);
+    if (FUSED && s5_n(code) == 0 && U.h == 0 && U.pp == 0) atomicOr(p.err, GDNR_DEVERR_BAD_POS);
+    if (s5_n(code) > 0 && s5_skip(code) && p.flush_hint == GDNR_FLUSH_NONE && U.h == 0 && U.pp == 0)
+      atomicOr(p.err, GDNR_DEVERR_BAD_HINT);
+    if (!FUSED && s5_skip(code) && p.flush_hint == GDNR_FLUSH_NONE && U.h == 0 && U.pp == 0)
+      atomicOr(p.err, GDNR_DEVERR_BAD_HINT);
+    table[ti] = code;
+  }
+  // The table is for the producer and the readout warps: the readout warps
+  // sync on it (barrier 1) and signal it to the producer (barrier 2), which
+  // joins once it has issued the checkpoint stream.  Chain warps decode their
+  // own units.
+  if (warp > S5_NCW) {
+    asm volatile("bar.arrive 2, %0;" ::"n"(32 * (1 + S5_NRW)) : "memory");
+    asm volatile("bar.sync 1, %0;" ::"n"(32 * S5_NRW) : "memory");
+  } else if (warp == 0) {
+    asm volatile("bar.sync 2, %0;" ::"n"(32 * (1 + S5_NRW)) : "memory");
+  }
 
   if (warp == 0) {
     // =================== producer ===================
@@ -724,8 +869,8 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       uint8_t* sb = smem + lay.stage0 + s * lay.stage_bytes;
       const bool skip = s5_skip(code);
       const int nreq = skip ? 0 : (s5_nmem(code) + geo.rb - 1) / geo.rb;
-      const bool ck = i >= S5_NPRO && !skip;
-      mbar_arrive_expect_tx(&full[s], (ck ? uint32_t(HPU) * 16384u : 0u) + uint32_t(nreq * HPU) * box_bytes);
+      const bool ck = i >= npro && !skip;
+      mbar_arrive_expect_tx(&full[s], (ck ? ck_bytes : 0u) + uint32_t(nreq * HPU) * box_bytes);
       if (ck) s5_tma4(sb + lay.ck, &ck_map, 0, 0, U.hv0, U.b, &full[s]);
       for (int j = 0; j < nreq; ++j)
 #pragma unroll
@@ -735,75 +880,117 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
     return;
   }
 
-  if (warp <= S5_NCW) {
+  if (chain_warp) {
     // =================== chain warps ===================
-    const int cw = warp - 1;
-    uint8_t* kbuf = smem + lay.kbuf0 + cw * 4096;
     uint8_t* res = smem + lay.res0 + cw * lay.res_bytes;
     for (int i = cw, k = 0; i < nu; i += S5_NCW, ++k) {
-      const int code = table[i];
       const S5Unit U = s5_unit(bid + i * grid, p.H, G, geo);
-      const bool skip = s5_skip(code);
-      // the result block is free once the readout of this warp's previous unit is done
-      bool ok = k == 0 || s5_warp_wait(&rfree[cw], (k - 1) & 1, p.err, abort, lane);
-      const int nreq = (ok && !skip) ? (s5_nmem(code) + geo.rb - 1) / geo.rb : 0;
-      // every lane's earlier generic accesses to kbuf, ordered before the copy
-      // engine overwrites it
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&kfull[cw], uint32_t(nreq) * box_bytes);
-        for (int j = 0; j < nreq; ++j)
-          s5_tma5(kbuf + j * box_bytes, &kr_map, 0, 0, U.h, j * geo.rb, U.b, &kfull[cw]);
+      bool ok = true;
+      S5In in = in0;
+      if (k > 0) {
+        // the key ring and result block are free once both readout warps of
+        // this warp's previous unit are done with them
+        ok = s5_warp_wait_count(&rcnt[cw], uint32_t(S5_TEAM * k), p.err, abort, lane);
+        // every lane's earlier generic accesses to kbuf, ordered before the
+        // copy engine overwrites it
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) {
+          const int nr = ok ? nreq_k : 0;
+          mbar_arrive_expect_tx(&kfull[cw], uint32_t(nr) * box_bytes);
+          for (int j = 0; j < nr; ++j)
+            s5_tma5(kbuf + j * box_bytes, &kr_map, 0, 0, U.h, j * geo.rb, U.b, &kfull[cw]);
+        }
+        in = s5_fetch<FUSED, HPU>(p, U, lane);
       }
-      const S5In in = s5_fetch<FUSED, HPU>(p, U, ok ? code : (1 << 16), lane);
       ok = s5_warp_wait(&kfull[cw], k & 1, p.err, abort, lane) && ok;
-      if (ok && !skip) s5_chain<FUSED, HPU>(p, U, code, in, kbuf, res, lay, lane);
+      const int code = s5_code<FUSED>(in.pos, in.flag, L);
+      const bool work = ok && !s5_skip(code);
+      S5Append ap{};
+      if (work) ap = s5_chain<FUSED, HPU>(p, U, code, in, kbuf, res, lay, lane);
       __syncwarp();
-      if (lane == 0) s5_arrive(&cdone[cw]);
+      if (lane == 0) s5_st_release(&cseq[cw], uint32_t(k + 1));
+      if (work) s5_append<FUSED, HPU>(p, U, code, ap, lane);
     }
     return;
   }
 
-  // =================== readout team ===================
-  const int rw = warp - 1 - S5_NCW;
-  constexpr int MW = HPU;  // m-tiles per readout warp: 16 * HPU * 8 rows / (16 * 8 warps)
-  const int head_r = (rw * 16 * MW) >> 7;
-  const int rbase = (rw * 16 * MW) & 127;
-  float* ost = reinterpret_cast<float*>(smem + lay.ost0 + rw * 128);
-  for (int i = 0; i < nu; ++i) {
-    const int s = i % S5_NS;
-    const int cw = i % S5_NCW, k = i / S5_NCW;
+  // =================== readout teams ===================
+  // Team j (2 warps) reads out the units of stage j in order; with two heads
+  // per unit each warp takes one head (8 m-tiles), with one head each warp
+  // takes 64 of its rows.
+  constexpr int MW = 4 * HPU;
+  constexpr int ROWS = 16 * MW;
+  float* ost = reinterpret_cast<float*>(smem + lay.ost0 + rw * 512);
+  const int esz_o = p.o_dt == GDNR_BF16 ? 2 : 4;
+  const bool vec_out = p.o_sv == 1 && (reinterpret_cast<uintptr_t>(p.out) % 16) == 0 &&
+                       ((p.o_sb * esz_o) % 16) == 0 && ((p.o_sh * esz_o) % 16) == 0;
+  for (int i = team, ul = 0; i < nu; i += S5_NS, ++ul) {
+    const int s = i % S5_NS;  // == team
+    const int ccw = i % S5_NCW, k = i / S5_NCW;
     const int code = table[i];
-    const S5Unit U = s5_unit(bid + i * grid, p.H, G, geo);
-    const bool skip = s5_skip(code);
-    float sc = 1.0f;
-    if (!skip && lane == 0)
-      sc = load_scalar(p.sc, int64_t(U.b) * p.sc_sb + int64_t(U.hv0 + head_r) * p.sc_sh +
-                                 int64_t(rbase / VBLOCK) * p.sc_sv,
-                       p.sc_dt);
+    float sc = s5_cvt(scl_raw, p.sc_dt);
+    int sc_base = ul * VBW;
+    if (ul >= SC_UNITS) {  // beyond the prefetched units
+      sc = 1.0f;
+      sc_base = 0;
+      if (lane < VBW && !s5_skip(code)) {
+        const S5Unit U = s5_unit(bid + i * grid, p.H, G, geo);
+        sc = load_scalar(p.sc, int64_t(U.b) * p.sc_sb + int64_t(U.hv0 + head_r) * p.sc_sh +
+                                   int64_t(rbase / VBLOCK + lane) * p.sc_sv,
+                         p.sc_dt);
+      }
+    }
     bool ok = s5_warp_wait(&full[s], (i / S5_NS) & 1, p.err, abort, lane);
-    ok = s5_warp_wait(&cdone[cw], k & 1, p.err, abort, lane) && ok;
-    if (ok && !skip) {
+    ok = s5_warp_wait_count(&cseq[ccw], uint32_t(k + 1), p.err, abort, lane) && ok;
+    if (ok && !s5_skip(code)) {
+      const S5Unit U = s5_unit(bid + i * grid, p.H, G, geo);
       const uint8_t* sb = smem + lay.stage0 + s * lay.stage_bytes;
-      const uint8_t* res = smem + lay.res0 + cw * lay.res_bytes;
+      const uint8_t* res = smem + lay.res0 + ccw * lay.res_bytes;
       const float* misc = reinterpret_cast<const float*>(res + lay.misc) + head_r * 4;
-      const float wsc = misc[0] * __shfl_sync(0xffffffffu, sc, 0);
-      s5_readout<MW, FUSED>(sb + lay.ck + head_r * 16384, sb + lay.vr + head_r * 4096,
-                            res + lay.t8 + head_r * 8 * T8STR,
-                            reinterpret_cast<const uint16_t*>(res + lay.cb + head_r * 96), wsc, misc[1],
-                            reinterpret_cast<const uint16_t*>(res + lay.vnew + head_r * 256), rbase,
-                            s5_nmem(code), ost, lane);
+      s5_readout<MW>(sb + lay.ck + head_r * 16384, sb + lay.vr + head_r * 4096, res + lay.t8 + head_r * 8 * T8STR,
+                     reinterpret_cast<const uint16_t*>(res + lay.cb + head_r * 96), misc[0], sc, sc_base,
+                     rbase, s5_nmem(code), ost, lane);
       __syncwarp();
-      if (lane < 16 * MW) {
-        const int64_t oi = int64_t(U.b) * p.o_sb + int64_t(U.hv0 + head_r) * p.o_sh + int64_t(rbase + lane) * p.o_sv;
-        store_scalar(p.out, oi, p.o_dt, ost[lane]);
+      // this token's own slot (fused) as a rank-one term, K^-1/2, coalesced store
+      constexpr int RPL = ROWS / 32;  // rows per lane: 4 or 2
+      const int r0 = RPL * lane;
+      float o[RPL];
+#pragma unroll
+      for (int q = 0; q < RPL; ++q) o[q] = ost[r0 + q];
+      if constexpr (FUSED) {
+        const float cpos = misc[1];
+        const uint16_t* vnew = reinterpret_cast<const uint16_t*>(res + lay.vnew + head_r * 256) + rbase;
+#pragma unroll
+        for (int q = 0; q < RPL; ++q) o[q] = fmaf(cpos, bf16_to_f(vnew[r0 + q]), o[q]);
+      }
+      const int64_t obase = int64_t(U.b) * p.o_sb + int64_t(U.hv0 + head_r) * p.o_sh;
+      if (vec_out) {
+        if (esz_o == 2) {
+          if constexpr (RPL == 4)
+            *reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.out) + obase + rbase + r0) =
+                make_uint2(pack_bf16x2(o[0] * KSCALE_H, o[1] * KSCALE_H), pack_bf16x2(o[2] * KSCALE_H, o[3] * KSCALE_H));
+          else
+            *reinterpret_cast<uint32_t*>(static_cast<uint16_t*>(p.out) + obase + rbase + r0) =
+                pack_bf16x2(o[0] * KSCALE_H, o[1] * KSCALE_H);
+        } else {
+          if constexpr (RPL == 4)
+            *reinterpret_cast<float4*>(static_cast<float*>(p.out) + obase + rbase + r0) =
+                make_float4(o[0] * KSCALE_H, o[1] * KSCALE_H, o[2] * KSCALE_H, o[3] * KSCALE_H);
+          else
+            *reinterpret_cast<float2*>(static_cast<float*>(p.out) + obase + rbase + r0) =
+                make_float2(o[0] * KSCALE_H, o[1] * KSCALE_H);
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < RPL; ++q)
+          store_scalar(p.out, obase + int64_t(rbase + r0 + q) * p.o_sv, p.o_dt, o[q] * KSCALE_H);
       }
     }
     __syncwarp();
     if (lane == 0) {
       s5_arrive(&empty[s]);
-      s5_arrive(&rfree[cw]);
+      s5_add_release(&rcnt[ccw], 1u);
     }
   }
 }
@@ -824,6 +1011,7 @@ static bool s5_grid(const StepParams& p, int& grid, S5Layout& lay) {
   if (total <= 0 || total > (int64_t(1) << 30)) return false;
   grid = int(total < nsm ? total : nsm);
   const int max_units = int((total + grid - 1) / grid);
+  if (max_units > 32 * S5_NRW) return false;  // the unit table is filled in one pass by the readout warps
   lay = s5_layout(g, max_units);
   return true;
 }
