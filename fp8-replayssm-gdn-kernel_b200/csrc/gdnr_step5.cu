@@ -185,13 +185,20 @@ __device__ __forceinline__ uint32_t s5_ring_off(int t, int col) {
   return uint32_t(R) * 128u + (uint32_t(c ^ (R & 7)) << 4) + uint32_t(col & 7) * 2u;
 }
 
-// four consecutive elements of a bf16 or f32 row, kept raw until used
+// Four consecutive elements of a bf16 or f32 row, kept raw until used.  Both
+// widths load into the same registers under a predicate, so nothing waits for
+// the data before it is unpacked.
 __device__ __forceinline__ uint4 s5_load4(const void* base, int64_t idx, bool bf16) {
-  if (bf16) {
-    const uint2 w = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(base) + idx);
-    return make_uint4(w.x, w.y, 0u, 0u);
-  }
-  return *reinterpret_cast<const uint4*>(static_cast<const float*>(base) + idx);
+  uint4 r;
+  const char* pb = static_cast<const char*>(base) + idx * (bf16 ? 2 : 4);
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.u32 p, %4, 0;\n\t"
+      "@p ld.global.v2.u32 {%0, %1}, [%5];\n\t"
+      "@!p ld.global.v4.u32 {%0, %1, %2, %3}, [%5];\n\t}"
+      : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+      : "r"(bf16 ? 1u : 0u), "l"(pb));
+  return r;
 }
 
 __device__ __forceinline__ void s5_unpack4(uint4 w, bool bf16, float* x) {
@@ -295,7 +302,32 @@ __device__ __forceinline__ void s5_tsplit(const float (*Tq)[4], uint8_t* t8, flo
 // Raw bits of one element of a F32 / BF16 / F16 tensor: the load completes
 // in the background; s5_cvt turns it into a float where it is first needed.
 __device__ __forceinline__ uint32_t s5_ld_raw(const void* p, int64_t i, int dtype) {
-  return dtype == GDNR_F32 ? static_cast<const uint32_t*>(p)[i] : uint32_t(static_cast<const uint16_t*>(p)[i]);
+  uint32_t r;
+  const bool w32 = dtype == GDNR_F32;
+  const char* pb = static_cast<const char*>(p) + i * (w32 ? 4 : 2);
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "@p ld.global.u32 %0, [%2];\n\t"
+      "@!p ld.global.u16 %0, [%2];\n\t}"
+      : "=r"(r)
+      : "r"(w32 ? 1u : 0u), "l"(pb));
+  return r;
+}
+
+// an I32 or U8 flag, raw
+__device__ __forceinline__ int s5_ld_flag(const void* p, int64_t i, int dtype) {
+  uint32_t r;
+  const bool w32 = dtype == GDNR_I32;
+  const char* pb = static_cast<const char*>(p) + i * (w32 ? 4 : 1);
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "@p ld.global.u32 %0, [%2];\n\t"
+      "@!p ld.global.u8 %0, [%2];\n\t}"
+      : "=r"(r)
+      : "r"(w32 ? 1u : 0u), "l"(pb));
+  return int(r);
 }
 
 __device__ __forceinline__ float s5_cvt(uint32_t raw, int dtype) {
@@ -344,8 +376,7 @@ __device__ __forceinline__ S5In s5_fetch(const StepParams& p, const S5Unit& U, i
     in.a = in.bb = 0u;
     in.alog = in.dtb = 0.0f;
     in.pos = p.valid_len[int64_t(U.b) * p.vl_s];
-    in.flag = (p.fl_dt == GDNR_I32) ? static_cast<const int32_t*>(p.flush)[int64_t(U.b) * p.fl_s]
-                                    : int(static_cast<const uint8_t*>(p.flush)[int64_t(U.b) * p.fl_s]);
+    in.flag = s5_ld_flag(p.flush, int64_t(U.b) * p.fl_s, p.fl_dt);
   }
   return in;
 }
@@ -786,7 +817,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
   if (p.pdl && warp == 0 && lane == 0) prologue();
   griddep_wait();
   // Chain warps: the first unit's inputs and whole key ring (small, on the
-  // critical path) go out before the checkpoint stream.
+  // critical path), alongside the checkpoint stream.
   const int cw = warp - 1;
   const bool chain_warp = warp >= 1 && warp <= S5_NCW;
   const int nreq_k = (L + geo.rb - 1) / geo.rb;
@@ -801,6 +832,12 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       for (int j = 0; j < nr; ++j) s5_tma5(kbuf + j * box_bytes, &kr_map, 0, 0, U.h, j * geo.rb, U.b, &kfull[cw]);
     }
     in0 = s5_fetch<FUSED, HPU>(p, U, lane);
+    // the key rings and these loads go out first; the producer starts the
+    // checkpoint stream once the ring positions (issued alongside) are back
+    // (barriers 3 and 2): DRAM serves a running stream before scattered loads
+    asm volatile("bar.arrive 3, %0;" ::"n"(32 * (1 + S5_NCW)) : "memory");
+  } else if (warp == 0) {
+    asm volatile("bar.sync 3, %0;" ::"n"(32 * (1 + S5_NCW)) : "memory");
   }
   // readout warps: vblock scales of their first units (lane l: team unit
   // l / (2 HPU), vblock l % (2 HPU) of the warp's rows), raw until used
@@ -820,7 +857,8 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
                         p.sc_dt);
   }
   // ring positions of this CTA's units for the producer and the readout, read
-  // by the threads from the top of the block down
+  // by the threads from the top of the block down (the producer is busy
+  // issuing the checkpoint stream, which blocks at the SM's share of HBM)
   const int ti = S5_THREADS - 1 - tid;
   int raw0 = 0, raw1 = 0;
   if (ti < nu) {
@@ -829,14 +867,10 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       raw0 = p.pos[int64_t(U.b) * p.pos_s];
     } else {
       raw0 = p.valid_len[int64_t(U.b) * p.vl_s];
-      raw1 = (p.fl_dt == GDNR_I32) ? static_cast<const int32_t*>(p.flush)[int64_t(U.b) * p.fl_s]
-                                   : int(static_cast<const uint8_t*>(p.flush)[int64_t(U.b) * p.fl_s]);
+      raw1 = s5_ld_flag(p.flush, int64_t(U.b) * p.fl_s, p.fl_dt);
     }
   }
-  __syncthreads();
-  // the checkpoint stream starts behind the small loads above
-  if (!p.pdl && warp == 0 && lane == 0) prologue();
-  if (tid == 0) griddep_launch();
+  if (tid == S5_THREADS - 1) griddep_launch();
   if (ti < nu) {
     const S5Unit U = s5_unit(bid + ti * grid, p.H, G, geo);
     const int code = s5_code<FUSED>(raw0, raw1, L);
@@ -869,7 +903,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       uint8_t* sb = smem + lay.stage0 + s * lay.stage_bytes;
       const bool skip = s5_skip(code);
       const int nreq = skip ? 0 : (s5_nmem(code) + geo.rb - 1) / geo.rb;
-      const bool ck = i >= npro && !skip;
+      const bool ck = i >= (p.pdl ? npro : 0) && !skip;  // not already requested before griddepcontrol.wait
       mbar_arrive_expect_tx(&full[s], (ck ? ck_bytes : 0u) + uint32_t(nreq * HPU) * box_bytes);
       if (ck) s5_tma4(sb + lay.ck, &ck_map, 0, 0, U.hv0, U.b, &full[s]);
       for (int j = 0; j < nreq; ++j)
@@ -886,7 +920,6 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
     for (int i = cw, k = 0; i < nu; i += S5_NCW, ++k) {
       const S5Unit U = s5_unit(bid + i * grid, p.H, G, geo);
       bool ok = true;
-      S5In in = in0;
       if (k > 0) {
         // the key ring and result block are free once both readout warps of
         // this warp's previous unit are done with them
@@ -901,13 +934,13 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
           for (int j = 0; j < nr; ++j)
             s5_tma5(kbuf + j * box_bytes, &kr_map, 0, 0, U.h, j * geo.rb, U.b, &kfull[cw]);
         }
-        in = s5_fetch<FUSED, HPU>(p, U, lane);
+        in0 = s5_fetch<FUSED, HPU>(p, U, lane);
       }
       ok = s5_warp_wait(&kfull[cw], k & 1, p.err, abort, lane) && ok;
-      const int code = s5_code<FUSED>(in.pos, in.flag, L);
+      const int code = s5_code<FUSED>(in0.pos, in0.flag, L);
       const bool work = ok && !s5_skip(code);
       S5Append ap{};
-      if (work) ap = s5_chain<FUSED, HPU>(p, U, code, in, kbuf, res, lay, lane);
+      if (work) ap = s5_chain<FUSED, HPU>(p, U, code, in0, kbuf, res, lay, lane);
       __syncwarp();
       if (lane == 0) s5_st_release(&cseq[cw], uint32_t(k + 1));
       if (work) s5_append<FUSED, HPU>(p, U, code, ap, lane);
