@@ -53,7 +53,10 @@ def parse_args():
     ap.add_argument("--e2e-steps", type=int, default=64)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-core", action="store_true", help="skip the core-replay (config 2) block-V sweep")
+    ap.add_argument("--no-core", action="store_true", help="skip the core-replay (config 2) measurement")
+    ap.add_argument("--profile", type=int, default=None, metavar="POS",
+                    help="profiling driver for ncu: a few untimed launches of one layer's step at ring position "
+                         "POS (no timing, no JSON line)")
     return ap.parse_args()
 
 
@@ -70,7 +73,7 @@ def measured_peak():
 
 def profile_traffic():
     """dram bytes per launch of the step kernel from the committed ncu summary."""
-    p = ROOT / "profiles" / "step_kernel_b64_l16.txt"
+    p = ROOT / "profiles" / "step5_kernel_b64_l16.md"
     try:
         for line in p.read_text().splitlines():
             if line.startswith("dram_bytes_per_launch_cycle_avg"):
@@ -216,12 +219,16 @@ def cpu_workers():
         return max(1, os.cpu_count() or 1)
 
 
-def cpu_baseline(seed: int, ring_len: int):
+def cpu_baseline(seed: int, ring_len: int, target_s: float = 15.0):
     workers = cpu_workers()
-    units, wall = cpu_units(ring_len, workers, seed, ring_len)  # one full ring cycle per worker
+    _, probe = cpu_units(1, workers, seed, ring_len)  # one unit per worker: sizes the sample
+    per_unit = max(probe, 1e-3)
+    n = max(ring_len, int(target_s / per_unit))
+    n = (n + ring_len - 1) // ring_len * ring_len  # whole ring cycles (the flush included)
+    units, wall = cpu_units(n, workers, seed, ring_len)
     return {"value": units / wall, "unit": UNIT, "cores": workers, "kind": "port",
-            "sample": f"{units} sequence-layer steps ({workers} sequences x one L={ring_len} ring cycle incl. flush) "
-                      f"of the numpy oracle port of replay_decode, {wall:.1f} s wall"}
+            "sample": f"{units} sequence-layer steps ({workers} processes x {n} steps = whole L={ring_len} ring "
+                      f"cycles incl. the flush) of the numpy oracle port of replay_decode, {wall:.1f} s wall"}
 
 
 def run_reference(args, world, rank):
@@ -292,14 +299,36 @@ def build_stack(args, device):
     return layers, step_inputs, pos, err
 
 
+def flush_hint_for(s: int, L: int) -> str:
+    """All sequences share the ring position here, so whether this step flushes
+    is known on the host: no sequence ("none") or every sequence ("all")."""
+    return "all" if s == L - 1 else "none"
+
+
 def launch_position(layers, step_inputs, pos, err, s):
     import gdnr
 
+    L = len(pos)
     for li, lay in enumerate(layers):
         st = lay["state"]
         mixed, a, b = step_inputs[li][s]
         gdnr.gdn_fused_step(mixed, a, b, lay["a_log"], lay["dt_bias"], pos[s], st.checkpoint, st.scale, st.k_ring,
-                            st.v_ring, st.g_ring, st.beta_ring, out=lay["out"], error_flag=err)
+                            st.v_ring, st.g_ring, st.beta_ring, out=lay["out"], error_flag=err,
+                            flush_hint=flush_hint_for(s, L))
+
+
+def run_profile(args, local):
+    """A few eager launches of one layer's fused step at one ring position (ncu target)."""
+    import torch
+
+    args.layers = 1
+    device = torch.device("cuda", local)
+    layers, step_inputs, pos, err = build_stack(args, device)
+    s = args.profile % args.ring
+    for _ in range(3):
+        launch_position(layers, step_inputs, pos, err, s)
+    torch.cuda.synchronize()
+    print(f"profile: 3 launches at ring position {s}, device error word {int(err.item())}", flush=True)
 
 
 def run_ours(args, world, rank, local):
@@ -336,32 +365,46 @@ def run_ours(args, world, rank, local):
             graphs[step_idx % L].replay()
             step_idx += 1
     barrier(world)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # one event between consecutive graph replays: per-position durations give
+    # each kernel's average launch time (non-flush positions -> the persistent
+    # step kernel; the flush position -> the flush kernel)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    positions = []
     sampler = ClockSampler(local)
     with sampler:
         with torch.cuda.stream(stream):
-            ev0.record(stream)
-            for _ in range(args.steps):
+            evs[0].record(stream)
+            for i in range(args.steps):
+                positions.append(step_idx % L)
                 graphs[step_idx % L].replay()
                 step_idx += 1
-            ev1.record(stream)
+                evs[i + 1].record(stream)
         torch.cuda.synchronize()
     barrier(world)
-    ms = ev0.elapsed_time(ev1)
+    ms = evs[0].elapsed_time(evs[-1])
     ms_max = max_over_ranks(ms, world)
     dev_err = int(err.item())
+    step_ms = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
 
     launches = args.steps * NL
     units = launches * B * world
     value = units / (ms_max / 1e3)
     # algorithmic bytes, averaged over the ring cycle actually timed
-    first = args.warmup
-    cyc = [O.algorithmic_bytes(B, (first + i) % L + 1, L, scale_bytes=4, gate_bytes=4, ab_bytes=2)
-           for i in range(args.steps)]
+    cyc = [O.algorithmic_bytes(B, p + 1, L, scale_bytes=4, gate_bytes=4, ab_bytes=2) for p in positions]
     bytes_per_launch = sum(cyc) / len(cyc)
-    launch_s = (ms / 1e3) / launches
-    achieved = bytes_per_launch / launch_s / 1e9
     peak, peak_kind = measured_peak()
+    kernels = {}
+    for name, sel in (("step5_kernel (non-flush steps)", lambda p: p != L - 1), ("step2_kernel (flush step)",
+                                                                                 lambda p: p == L - 1)):
+        idx = [i for i, p in enumerate(positions) if sel(p)]
+        if not idx:
+            continue
+        t = sum(step_ms[i] for i in idx) / (len(idx) * NL) / 1e3
+        b = sum(cyc[i] for i in idx) / len(idx)
+        kernels[name] = {"launches": len(idx) * NL, "us_per_launch": t * 1e6, "algorithmic_bytes_per_launch": b,
+                         "achieved_GB_s": b / t / 1e9, "frac_of_peak": b / t / 1e9 / peak}
+    dom = max(kernels, key=lambda k: kernels[k]["launches"] * kernels[k]["us_per_launch"])
+    achieved = kernels[dom]["achieved_GB_s"]
 
     # ---- end to end through the public API with host buffers (pinned), per layer-step
     e2e = run_e2e(args, layers, step_inputs, pos, stream, world) if args.e2e_steps > 0 else None
@@ -401,16 +444,19 @@ def run_ours(args, world, rank, local):
         "clocks": sampler.summary(),
         "roofline": {
             "bound": "hbm",
-            "kernel": "gdnr::step_kernel<fused,e4m3,G=2>",
+            "kernel": dom,
             "achieved": achieved,
             "peak": peak,
             "peak_kind": peak_kind,
             "unit": "GB/s",
             "frac": achieved / peak,
             "traffic": profile_traffic(),
-            "algorithmic_bytes_per_launch": bytes_per_launch,
-            "note": "achieved = cycle-averaged algorithmic bytes per launch / (timed region / launches)",
+            "algorithmic_bytes_per_launch": kernels[dom]["algorithmic_bytes_per_launch"],
+            "note": "achieved = the kernel's algorithmic bytes per launch (averaged over the positions it ran) / "
+                    "its average launch time from CUDA events between graph replays on the launch stream",
         },
+        "kernels": kernels,
+        "cycle_algorithmic_bytes_per_launch": bytes_per_launch,
     }
     if e2e is not None:
         line["e2e"] = e2e
@@ -446,7 +492,8 @@ def run_e2e(args, layers, step_inputs, pos, stream, world):
                 b.copy_(hb, non_blocking=True)
                 st = lay["state"]
                 gdnr.gdn_fused_step(mixed, a, b, lay["a_log"], lay["dt_bias"], pos[s], st.checkpoint, st.scale,
-                                    st.k_ring, st.v_ring, st.g_ring, st.beta_ring, out=lay["out"])
+                                    st.k_ring, st.v_ring, st.g_ring, st.beta_ring, out=lay["out"],
+                                    flush_hint=flush_hint_for(s, L))
                 host_out[li].copy_(lay["out"], non_blocking=True)
 
     for i in range(L):
@@ -483,31 +530,31 @@ def run_core(args, device, stream):
                      torch.empty(B, HV, KD, dtype=torch.bfloat16, device=device)))
     res = {}
     nbytes = O.algorithmic_bytes(B, L, L, scale_bytes=4, gate_bytes=4, fused=False)
-    for bv in (32, 64, 128):
-        def run():
-            for ck, d, vl, fl, out in sets:
-                gdnr.gdn_replay_fp8(ck.payload, ck.scale, d["q"], d["k"], d["v"], d["g"], d["beta"], vl, fl,
-                                    block_v=bv, out=out)
-        with torch.cuda.stream(stream):
-            run()
-        torch.cuda.synchronize()
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=stream):
-            run()
-        reps = 50
-        with torch.cuda.stream(stream):
-            for _ in range(5):
-                g.replay()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            for _ in range(reps):
-                g.replay()
-            e1.record(stream)
-        torch.cuda.synchronize()
-        us = 1e3 * e0.elapsed_time(e1) / (reps * NL)
-        res[f"block_v{bv}"] = {"us_per_launch": us, "GB_s": nbytes / (us * 1e-6) / 1e9,
-                               "steps_seq_per_s": B / (us * 1e-6)}
-        del g
+
+    def run():
+        for ck, d, vl, fl, out in sets:
+            gdnr.gdn_replay_fp8(ck.payload, ck.scale, d["q"], d["k"], d["v"], d["g"], d["beta"], vl, fl, out=out,
+                                flush_hint="none")
+    with torch.cuda.stream(stream):
+        run()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        run()
+    reps = 50
+    with torch.cuda.stream(stream):
+        for _ in range(5):
+            g.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            g.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    us = 1e3 * e0.elapsed_time(e1) / (reps * NL)
+    res.update({"us_per_launch": us, "GB_s": nbytes / (us * 1e-6) / 1e9, "steps_seq_per_s": B / (us * 1e-6),
+                "frac_of_peak": nbytes / (us * 1e-6) / 1e9 / measured_peak()[0]})
+    del g
     res["algorithmic_bytes_per_launch"] = nbytes
     res["workload"] = "config2: gdn_replay_fp8 non-flush, B=64, full L=16 ring, f32 scales/gates"
     return res
@@ -520,6 +567,8 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)
+        elif args.profile is not None:
+            run_profile(args, local)
         else:
             run_ours(args, world, rank, local)
     finally:
