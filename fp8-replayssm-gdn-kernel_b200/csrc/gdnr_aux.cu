@@ -9,6 +9,7 @@
 //
 // These are API-completeness paths; the decode hot path is gdnr_fused_step.
 #include <cstring>
+#include <mutex>
 
 #include "gdnr_device.cuh"
 #include "gdnr_internal.h"
@@ -280,6 +281,41 @@ __global__ void __launch_bounds__(256) bf16_step_kernel(const __grid_constant__ 
   }
 }
 
+// ---------------------------------------------------------------- static-scratch split replay
+// gdnr_replay_split needs two caller buffers (T and c).  This variant keeps
+// them in one file-scope device array so that a caller which cannot allocate
+// device memory when it calls the replay can still use the split path; the
+// array is sized for GDNR_SPLIT_STATIC_MAX_PAIRS (sequence, value head) pairs
+// and rings of up to MAX_L slots: 4096 x (128 + 64) floats = 3 MiB per device.
+static_assert(GDNR_SPLIT_STATIC_MAX_L == MAX_L, "static scratch is sized for MAX_L ring slots");
+constexpr int64_t SPLIT_STATIC_TQ = int64_t(GDNR_SPLIT_STATIC_MAX_PAIRS) * 128;
+constexpr int64_t SPLIT_STATIC_FLOATS = int64_t(GDNR_SPLIT_STATIC_MAX_PAIRS) * (128 + MAX_L);
+static __device__ __align__(256) float g_split_scratch[SPLIT_STATIC_FLOATS];
+
+constexpr int SPLIT_STATIC_MAX_DEVICES = 64;
+static float* g_split_scratch_ptr[SPLIT_STATIC_MAX_DEVICES] = {};
+static std::mutex g_split_scratch_mu;
+
+// Device address of the scratch array on the current device, looked up once
+// per device (with that device current) and cached.
+static int split_scratch_for_current_device(float** out) {
+  int dev = -1;
+  int rc = cuda_status(cudaGetDevice(&dev), "gdnr_replay_split_static: cudaGetDevice");
+  if (rc != GDNR_OK) return rc;
+  if (dev < 0 || dev >= SPLIT_STATIC_MAX_DEVICES)
+    return set_error(GDNR_ERR_UNSUPPORTED, "gdnr_replay_split_static: device index %d above %d", dev,
+                     SPLIT_STATIC_MAX_DEVICES - 1);
+  std::lock_guard<std::mutex> lock(g_split_scratch_mu);
+  if (!g_split_scratch_ptr[dev]) {
+    void* ptr = nullptr;
+    rc = cuda_status(cudaGetSymbolAddress(&ptr, g_split_scratch), "gdnr_replay_split_static: cudaGetSymbolAddress");
+    if (rc != GDNR_OK) return rc;
+    g_split_scratch_ptr[dev] = static_cast<float*>(ptr);
+  }
+  *out = g_split_scratch_ptr[dev];
+  return GDNR_OK;
+}
+
 }  // namespace gdnr
 
 using namespace gdnr;
@@ -422,6 +458,50 @@ int gdnr_replay_split(const gdnr_replay_split_args* a, void* stream) {
   CK(cuda_status(cudaGetLastError(), "gdnr_replay_split precompute launch"));
   split_apply_kernel<<<dim3(unsigned(HV), unsigned(B), unsigned(128 / rows)), 256, 0, st>>>(p);
   return cuda_status(cudaGetLastError(), "gdnr_replay_split apply launch");
+}
+
+int gdnr_replay_split_static(const gdnr_replay_split_static_args* a, void* stream) {
+  if (!a) return set_error(GDNR_ERR_ARG, "args: null pointer");
+  if (a->k_ring.ndim != 4 || a->v_ring.ndim != 4)
+    return set_error(GDNR_ERR_ARG, "k_ring and v_ring must be 4-D [B,L,H,K] / [B,L,HV,V]");
+  const int64_t B = a->k_ring.shape[0], L = a->k_ring.shape[1], HV = a->v_ring.shape[2];
+  if (B < 0 || HV < 0 || B * HV > GDNR_SPLIT_STATIC_MAX_PAIRS)
+    return set_error(GDNR_ERR_UNSUPPORTED,
+                     "gdnr_replay_split_static: B*HV = %lld above the static scratch's %d (sequence, value head) "
+                     "pairs; use gdnr_replay_split with caller buffers",
+                     static_cast<long long>(B * HV), GDNR_SPLIT_STATIC_MAX_PAIRS);
+  if (L < 1 || L > GDNR_SPLIT_STATIC_MAX_L)
+    return set_error(GDNR_ERR_UNSUPPORTED, "gdnr_replay_split_static: ring length %lld outside [1, %d]",
+                     static_cast<long long>(L), GDNR_SPLIT_STATIC_MAX_L);
+  float* scratch = nullptr;
+  CK(split_scratch_for_current_device(&scratch));
+  gdnr_replay_split_args s;
+  memset(&s, 0, sizeof(s));
+  s.checkpoint = a->checkpoint;
+  s.scale = a->scale;
+  s.q = a->q;
+  s.k_ring = a->k_ring;
+  s.v_ring = a->v_ring;
+  s.g_ring = a->g_ring;
+  s.beta_ring = a->beta_ring;
+  s.valid_len = a->valid_len;
+  s.out = a->out;
+  s.block_v = a->block_v;
+  s.error_flag = a->error_flag;
+  // T [B,HV,128] then c [B,HV,L], both contiguous, inside the scratch; every
+  // element the apply phase reads is written by the precompute phase of the
+  // same call, so nothing has to start at zero
+  s.tq.data = scratch;
+  s.tq.dtype = GDNR_F32;
+  s.tq.ndim = 3;
+  s.tq.shape[0] = B; s.tq.shape[1] = HV; s.tq.shape[2] = 128;
+  s.tq.stride[0] = HV * 128; s.tq.stride[1] = 128; s.tq.stride[2] = 1;
+  s.coef.data = scratch + SPLIT_STATIC_TQ;
+  s.coef.dtype = GDNR_F32;
+  s.coef.ndim = 3;
+  s.coef.shape[0] = B; s.coef.shape[1] = HV; s.coef.shape[2] = L;
+  s.coef.stride[0] = HV * L; s.coef.stride[1] = L; s.coef.stride[2] = 1;
+  return gdnr_replay_split(&s, stream);
 }
 
 int gdnr_bf16_step(const gdnr_bf16_step_args* a, void* stream) {

@@ -479,7 +479,7 @@ __device__ __forceinline__ void s5_tloop(const uint8_t* kbuf, float wj, int n, f
 template <bool FUSED, int HPU>
 __device__ __forceinline__ S5Append s5_chain(const StepParams& p, const S5Unit& U, int code, const S5In& in,
                                              uint8_t* kbuf, uint8_t* res, const S5Layout& lay, int lane) {
-  S5Append ap;
+  S5Append ap{};
   const int g8 = lane >> 2, t4 = lane & 3;
   const int e = lane >> 4, t = lane & 15;
   const int n = s5_n(code), nmem = s5_nmem(code);
@@ -489,7 +489,6 @@ __device__ __forceinline__ S5Append s5_chain(const StepParams& p, const S5Unit& 
   float g_own = s5_cvt(in.g, p.gr_dt), beta_own = s5_cvt(in.beta, p.br_dt);  // gates of (head e, slot t)
   float qv[4];
   if constexpr (FUSED) {
-    const int L = p.L;
     const int pos = nmem;
     const bool bf = p.mx_dt == GDNR_BF16;
     // this token's gates for head e (every lane; slot pos keeps them)

@@ -15,6 +15,7 @@ from .ops import (  # noqa: F401
     gdn_prep_ring,
     gdn_replay_fp8,
     gdn_replay_fp8_split,
+    gdn_replay_fp8_split_static,
     quantize_checkpoint,
     read_device_error,
 )

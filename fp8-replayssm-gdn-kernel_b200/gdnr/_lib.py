@@ -76,6 +76,14 @@ class ReplaySplitArgs(ctypes.Structure):
     ]
 
 
+class ReplaySplitStaticArgs(ctypes.Structure):
+    _fields_ = [(n, Tensor) for n in ("checkpoint", "scale", "q", "k_ring", "v_ring", "g_ring", "beta_ring",
+                                      "valid_len", "out")] + [
+        ("block_v", ctypes.c_int32),
+        ("error_flag", ctypes.c_void_p),
+    ]
+
+
 class PrepArgs(ctypes.Structure):
     _fields_ = [(n, Tensor) for n in ("mixed_qkv", "a", "b", "a_log", "dt_bias", "pos", "q_out", "k_ring",
                                       "v_ring", "g_ring", "beta_ring")] + [
@@ -108,6 +116,7 @@ class Bf16StepArgs(ctypes.Structure):
 SIGNATURES = {
     "gdnr_replay": ([ctypes.POINTER(ReplayArgs), ctypes.c_void_p], ctypes.c_int),
     "gdnr_replay_split": ([ctypes.POINTER(ReplaySplitArgs), ctypes.c_void_p], ctypes.c_int),
+    "gdnr_replay_split_static": ([ctypes.POINTER(ReplaySplitStaticArgs), ctypes.c_void_p], ctypes.c_int),
     "gdnr_prep_ring": ([ctypes.POINTER(PrepArgs), ctypes.c_void_p], ctypes.c_int),
     "gdnr_fused_step": ([ctypes.POINTER(StepArgs), ctypes.c_void_p], ctypes.c_int),
     "gdnr_quantize_vblock32": ([ctypes.POINTER(CodecArgs), ctypes.c_void_p], ctypes.c_int),

@@ -169,6 +169,41 @@ def gdn_replay_fp8_split(
     return out
 
 
+def gdn_replay_fp8_split_static(
+    checkpoint: torch.Tensor,
+    checkpoint_scale: torch.Tensor,
+    q: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    g_cache: torch.Tensor,
+    beta_cache: torch.Tensor,
+    valid_len: torch.Tensor,
+    out: torch.Tensor,
+    block_v: int = 32,
+) -> torch.Tensor:
+    """:func:`gdn_replay_fp8_split` without caller scratch (no reference counterpart).
+
+    For callers that cannot allocate device memory when they call the replay:
+    T and c live in a library-owned 3 MiB device array (B*HV <= 4096, L <= 64;
+    larger calls raise), and ``out`` must be given.  The first call on a device
+    sets the array up (make it before any stream capture); calls that overlap
+    in time share the array and must be serialised.
+    """
+    args = _lib.ReplaySplitStaticArgs()
+    args.checkpoint = _lib.tensor_desc(checkpoint)
+    args.scale = _lib.tensor_desc(checkpoint_scale)
+    args.q = _lib.tensor_desc(q)
+    args.k_ring = _lib.tensor_desc(k_cache)
+    args.v_ring = _lib.tensor_desc(v_cache)
+    args.g_ring = _lib.tensor_desc(g_cache)
+    args.beta_ring = _lib.tensor_desc(beta_cache)
+    args.valid_len = _lib.tensor_desc(valid_len)
+    args.out = _lib.tensor_desc(_as_bhv(out))
+    args.block_v = int(block_v)
+    _lib.check(_lib.load().gdnr_replay_split_static(ctypes.byref(args), _lib.stream_handle(q.device)))
+    return out
+
+
 def gdn_prep_ring(
     mixed_qkv: torch.Tensor,
     a: torch.Tensor,

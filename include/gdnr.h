@@ -112,6 +112,32 @@ typedef struct {
 
 int gdnr_replay_split(const gdnr_replay_split_args* args, void* stream);
 
+/* ---- gdnr_replay_split_static: gdnr_replay_split without caller scratch --
+ * No counterpart in the reference.  The split replay needs T [B,HV,K] and
+ * c [B,HV,L] scratch; this entry point keeps them in a library-owned device
+ * array instead, for callers that cannot allocate device memory when they
+ * call the replay (e.g. a serving runtime that reserves all device memory for
+ * its state pool up front, or code inside an allocator callback that must not
+ * re-enter the allocator).  It allocates nothing.
+ *
+ * Limits: B*HV <= GDNR_SPLIT_STATIC_MAX_PAIRS and L <= GDNR_SPLIT_STATIC_MAX_L
+ * (3 MiB of scratch per device); larger calls fail with GDNR_ERR_UNSUPPORTED.
+ * The first call on a device looks up the scratch address (cudaGetSymbolAddress,
+ * with that device current) and caches it: make that first call before any
+ * stream capture.  All calls on a device share the one scratch, so calls that
+ * overlap in time (concurrent streams or host threads) race on it; serialise
+ * them.  Nothing in the scratch needs to start at zero. */
+#define GDNR_SPLIT_STATIC_MAX_PAIRS 4096
+#define GDNR_SPLIT_STATIC_MAX_L 64
+typedef struct {
+  gdnr_tensor checkpoint, scale, q, k_ring, v_ring, g_ring, beta_ring, valid_len; /* as gdnr_replay_split */
+  gdnr_tensor out;
+  int32_t block_v;
+  uint32_t* error_flag;
+} gdnr_replay_split_static_args;
+
+int gdnr_replay_split_static(const gdnr_replay_split_static_args* args, void* stream);
+
 /* ---- gdnr_prep_ring: mirror of gdn_prep_ring --------------------------- */
 typedef struct {
   gdnr_tensor mixed_qkv; /* [B, 2*H*K + HV*V] BF16|F32, inner stride 1 */

@@ -48,6 +48,7 @@ def test_struct_layout_matches_c(tmp_path):
         "gdnr_tensor": _lib.Tensor,
         "gdnr_replay_args": _lib.ReplayArgs,
         "gdnr_replay_split_args": _lib.ReplaySplitArgs,
+        "gdnr_replay_split_static_args": _lib.ReplaySplitStaticArgs,
         "gdnr_prep_args": _lib.PrepArgs,
         "gdnr_step_args": _lib.StepArgs,
         "gdnr_codec_args": _lib.CodecArgs,
