@@ -394,8 +394,8 @@ def run_ours(args, world, rank, local):
     bytes_per_launch = sum(cyc) / len(cyc)
     peak, peak_kind = measured_peak()
     kernels = {}
-    for name, sel in (("step5_kernel (non-flush steps)", lambda p: p != L - 1), ("step2_kernel (flush step)",
-                                                                                 lambda p: p == L - 1)):
+    for name, sel in (("step5_kernel<flush=false> (non-flush steps)", lambda p: p != L - 1),
+                      ("step5_kernel<flush=true> (flush step)", lambda p: p == L - 1)):
         idx = [i for i, p in enumerate(positions) if sel(p)]
         if not idx:
             continue

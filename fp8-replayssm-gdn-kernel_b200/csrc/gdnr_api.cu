@@ -231,7 +231,6 @@ int check_launch_opts(int32_t hint, int32_t flags, StepParams& p) {
   if (flags & ~GDNR_LAUNCH_PDL) return set_error(GDNR_ERR_ARG, "unknown launch_flags bits 0x%x", flags);
   p.flush_hint = hint;
   p.pdl = (flags & GDNR_LAUNCH_PDL) ? 1 : 0;
-  p.head_filter = 0;
   return GDNR_OK;
 }
 

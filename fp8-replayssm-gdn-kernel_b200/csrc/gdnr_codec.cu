@@ -45,7 +45,7 @@ __global__ void __launch_bounds__(256) quantize_kernel(const __grid_constant__ C
   const VScale vs = vblock_scale(am, p.quant_rounded);
   const float rcp = __fdiv_rn(1.0f, vs.divisor);
   uint32_t sat = 0;
-  const uint4 q = quantize16_fast(x, vs.divisor, rcp, quant_fast_ok(vs.divisor, rcp), sat);
+  const uint4 q = quantize16_fast(x, vs.divisor, rcp, p.sat != nullptr, sat);
   *reinterpret_cast<uint4*>(p.payload + int64_t(b) * p.pl_sb + int64_t(hv) * p.pl_sh + int64_t(r) * 128 + c * 16) = q;
   if (tid == 0) {
     const int64_t si = int64_t(b) * p.sc_sb + int64_t(hv) * p.sc_sh + int64_t(vb) * p.sc_sv;

@@ -246,22 +246,76 @@ __device__ __forceinline__ bool quant_fast_ok(float divisor, float rcp) {
   return isfinite(divisor) && isfinite(rcp) && divisor >= 1.17549435e-38f && rcp >= 1.17549435e-38f;
 }
 
+// ---------------------------------------------------------------- division-free exact quantiser
+// A float with the same e4m3 rounding (RNE, satfinite) as the IEEE quotient
+// q = RN(x / d), from y = RN(x * rcp) without a division.
+//
+// The e4m3 grid has 8 values per binade on [2^-6, 448] and steps of 2^-9 on
+// [0, 2^-6) -- the spacing of [2^-6, 2^-5), so that range is located by
+// shifting it up by 2^-6 (round-toward-zero keeps the shifted value below 2^-5).
+// y falls in the grid interval of the exact quotient, or -- when the quotient
+// is next to a grid value, far from any midpoint -- in a neighbouring one.  Let
+// m be the midpoint of y's interval (at most 5 significant bits, an even f32
+// mantissa) and u its f32 ulp.  Then q rounds (in e4m3) to the upper grid
+// neighbour of m iff q > m, i.e. iff x/d > m + u/2 (at exactly m + u/2 the f32
+// rounding ties to m); to the lower iff x/d < m - u/2; otherwise q == m and
+// the e4m3 tie goes to even.  r = fma(-m, d, x) is x - m d exactly whenever
+// |x/d - m| is within a few ulp (the difference then fits in 24 bits), and
+// otherwise has the right sign and is far from the thresholds +-(u/2) d, so
+// the two comparisons are exact; the result is m, or m moved one f32 ulp up or
+// down, which the e4m3 conversion rounds to the same grid value as q.  (The
+// lower threshold at m = 2^-10, a power of two, would be u/4 d; there both
+// outcomes are the grid value 0.)  NaN stays NaN.  Requires d, 1/d in
+// [2^-60, 2^60] (quant_exact_ok), so that no threshold leaves the normal range;
+// kd = quant_exact_kd(d) puts (u/2) d in bits as (bits(m) & exponent) + kd.
+__device__ __forceinline__ bool quant_exact_ok(float d, float rcp) {
+  return d >= 8.6736174e-19f && d <= 1.1529215e18f && rcp >= 8.6736174e-19f && rcp <= 1.1529215e18f;  // 2^-60, 2^60
+}
+
+__device__ __forceinline__ uint32_t quant_exact_kd(float d) { return __float_as_uint(d) - (151u << 23); }
+
+__device__ __forceinline__ float quant_exact(float x, float d, float rcp, uint32_t kd) {
+  const float y = x * rcp;
+  const uint32_t sy = __float_as_uint(y) & 0x80000000u;
+  const float a = fabsf(y);
+  const bool sub = a < 0.015625f;
+  const float t = sub ? __fadd_rz(a, 0.015625f) : a;
+  const float mt = __uint_as_float((__float_as_uint(t) & 0xFFF00000u) | 0x00080000u);
+  const float ma = sub ? mt - 0.015625f : mt;  // |m|, exact
+  const uint32_t mb = __float_as_uint(ma) | sy;
+  const float r = fmaf(__uint_as_float(mb), -d, x);                      // x - m d
+  const float hd = __uint_as_float((__float_as_uint(ma) & 0x7F800000u) + kd);  // (u/2) d
+  const float rr = __uint_as_float(__float_as_uint(r) ^ sy);             // > 0: |q| beyond |m|
+  return __uint_as_float(mb + (rr > hd ? 1u : 0u) - (rr < -hd ? 1u : 0u));
+}
+
+// Two quotients as e4m3 bytes (low byte = x0); `ok` = quant_exact_ok(d, rcp),
+// otherwise the IEEE division.
+__device__ __forceinline__ uint32_t quant_e4m3x2(float x0, float x1, float d, float rcp, uint32_t kd, bool ok) {
+  const float y0 = ok ? quant_exact(x0, d, rcp, kd) : __fdiv_rn(x0, d);
+  const float y1 = ok ? quant_exact(x1, d, rcp, kd) : __fdiv_rn(x1, d);
+  return f2_to_e4m3x2(y0, y1);
+}
+
 // e4m3 pair with satfinite: RNE, then |y| > 448 -> 448 and NaN -> NaN, which
 // equals clamp(+-448) followed by the cast (ref.py:99).
 __device__ __forceinline__ uint32_t e4m3x2_sat(float lo, float hi) { return f2_to_e4m3x2(lo, hi); }
 
-// 16 values with the fast exact quotient; counts |x/divisor| > 448.
-__device__ __forceinline__ uint4 quantize16_fast(const float* x, float divisor, float rcp, bool fast_ok,
+// 16 values (division-free exact quantiser); with count_sat, also counts
+// |x/divisor| > 448 from the IEEE quotient.
+__device__ __forceinline__ uint4 quantize16_fast(const float* x, float divisor, float rcp, bool count_sat,
                                                  uint32_t& sat) {
+  const bool ok = quant_exact_ok(divisor, rcp);
+  const uint32_t kd = quant_exact_kd(divisor);
   uint32_t w[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float y0 = quant_quotient(x[4 * i + 0], divisor, rcp, fast_ok);
-    const float y1 = quant_quotient(x[4 * i + 1], divisor, rcp, fast_ok);
-    const float y2 = quant_quotient(x[4 * i + 2], divisor, rcp, fast_ok);
-    const float y3 = quant_quotient(x[4 * i + 3], divisor, rcp, fast_ok);
-    sat += (fabsf(y0) > FP8_MAX) + (fabsf(y1) > FP8_MAX) + (fabsf(y2) > FP8_MAX) + (fabsf(y3) > FP8_MAX);
-    w[i] = e4m3x2_sat(y0, y1) | (e4m3x2_sat(y2, y3) << 16);
+  for (int i = 0; i < 4; ++i)
+    w[i] = quant_e4m3x2(x[4 * i], x[4 * i + 1], divisor, rcp, kd, ok) |
+           (quant_e4m3x2(x[4 * i + 2], x[4 * i + 3], divisor, rcp, kd, ok) << 16);
+  if (count_sat) {
+    const bool fast = quant_fast_ok(divisor, rcp);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) sat += fabsf(quant_quotient(x[i], divisor, rcp, fast)) > FP8_MAX;
   }
   return make_uint4(w[0], w[1], w[2], w[3]);
 }

@@ -505,7 +505,7 @@ __device__ __forceinline__ void head_flush(const HeadTile& T, const HeadScratch&
       amax = warp_max_nan(amax);
       vs = vblock_scale(amax, quant_rounded);
       rcp = __fdiv_rn(1.0f, vs.divisor);
-      fast = quant_fast_ok(vs.divisor, rcp);
+      fast = quant_exact_ok(vs.divisor, rcp);
     }
 #pragma unroll 2
     for (int nt = 0; nt < 16; ++nt) {
@@ -530,9 +530,7 @@ __device__ __forceinline__ void head_flush(const HeadTile& T, const HeadScratch&
           if (pass == 0) {
             amax = fmax_nan(amax, fmax_nan(fabsf(x0), fabsf(x1)));
           } else {
-            const float y0 = quant_quotient(x0, vs.divisor, rcp, fast);
-            const float y1 = quant_quotient(x1, vs.divisor, rcp, fast);
-            *reinterpret_cast<uint16_t*>(sp) = static_cast<uint16_t>(e4m3x2_sat(y0, y1));
+            *reinterpret_cast<uint16_t*>(sp) = static_cast<uint16_t>(quant_e4m3x2(x0, x1, vs.divisor, rcp, quant_exact_kd(vs.divisor), fast));
           }
         }
       }

@@ -67,7 +67,6 @@ struct StepParams {
   int32_t quant_rounded;
   uint32_t* err;
   int32_t flush_hint;   // GDNR_FLUSH_*
-  int32_t head_filter;  // 0: every head; 2: only heads that flush
   int32_t pdl;          // launch with programmatic stream serialization
 };
 

@@ -414,18 +414,7 @@ static cudaError_t launch_g(const StepParams& p, int group, cudaStream_t stream)
 }
 
 cudaError_t launch_step(const StepParams& p, bool fused, bool f32ck, int group, cudaStream_t stream) {
-  if (step5_eligible(p, fused, f32ck)) {
-    if (p.flush_hint == GDNR_FLUSH_ALL) {
-      StepParams q = p;
-      q.head_filter = 0;
-      return launch_step2(q, fused, stream);
-    }
-    cudaError_t e = launch_step5(p, fused, p.pdl != 0, stream);
-    if (e != cudaSuccess || p.flush_hint == GDNR_FLUSH_NONE) return e;
-    StepParams q = p;
-    q.head_filter = 2;  // the flush heads, which the warp-specialised kernel leaves alone
-    return launch_step2(q, fused, stream);
-  }
+  if (step5_eligible(p, fused, f32ck)) return launch_step5(p, fused, p.pdl != 0, stream);
   if (!f32ck && p.L <= STEP2_MAX_L) return launch_step2(p, fused, stream);
   if (fused) return f32ck ? launch_g<true, true>(p, group, stream) : launch_g<true, false>(p, group, stream);
   return f32ck ? launch_g<false, true>(p, group, stream) : launch_g<false, false>(p, group, stream);

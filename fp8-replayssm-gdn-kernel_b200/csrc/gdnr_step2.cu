@@ -116,8 +116,6 @@ __global__ void __launch_bounds__(128, 6) step2_kernel(const __grid_constant__ S
                                      : (static_cast<const uint8_t*>(p.flush)[int64_t(b) * p.fl_s] != 0);
   }
 
-  if (p.head_filter == 2 && !do_flush) return;  // flush-only pass: other heads are done elsewhere
-
   // ---- 1. checkpoint prefetch: warp w, rows 32w + 4it + lane/8, 16-byte chunk lane%8
   const uint8_t* ck_head =
       static_cast<const uint8_t*>(p.ck) + int64_t(b) * p.ck_sb + int64_t(hv) * p.ck_sh + int64_t(row0) * 128;

@@ -23,8 +23,12 @@
 //    e4m3 MMA against T split into five e4m3 terms, V^T c as a bf16 MMA into
 //    the spare accumulator columns, plus this token's value row (rank one).
 //
-// Units whose ring is full (flush) are skipped; the caller runs the flush
-// path for them (gdnr_step2.cu in flush-only mode).
+// Units whose ring is full (flush) take the same stages: their chain warp
+// hands the decayed Gram matrix and gates to the readout team, whose warps
+// rebuild the state in WY form on tensor cores one vblock of 32 rows at a time
+// (E = S0 [K; q]^T, the u recurrence, S_L = a S0 + W K), re-quantise it into
+// the stage (vblock32 scales, ref.py:40-106) and write both heads back with one
+// tensor-map store.  With GDNR_FLUSH_NONE they are skipped and reported.
 #include <cuda.h>
 
 #include "gdnr_device.cuh"
@@ -39,6 +43,16 @@ constexpr int S5_NRW = 8;   // readout warps
 constexpr int S5_TEAM = S5_NRW / S5_NS;  // readout warps per stage
 constexpr int S5_THREADS = 32 * (1 + S5_NCW + S5_NRW);
 constexpr int S5_GSTR = 20;  // Gram scratch row (floats): 16 key columns + 3 query terms + pad
+// A chain warp's result area: T terms of a non-flush unit (2 x 8 x T8STR), or the
+// flush data of a flush unit -- q split as f16 x 256 [2][128], then per head
+// (float offsets) a_t [16] at S5_FA, beta_t [16] at S5_FB, 1 / (operand scale) at
+// S5_FINV, and from S5_FN the f16 operand rows [T diag(d) | z]^T: hi [17][16], then
+// lo [17][16] (the chain's N [16][16] f32 scratch before that).
+constexpr uint32_t S5_FQ16 = 0, S5_FHEAD = 512;
+constexpr int S5_FA = 0, S5_FB = 16, S5_FINV = 32, S5_FN = 36, S5_TB_LO = 17 * 16;
+constexpr uint32_t S5_FHEAD_BYTES = S5_FN * 4 + 1088;  // max(N: 1024, operand rows: 2 x 17 x 16 x 2)
+constexpr uint32_t S5_T8_BYTES = S5_FHEAD + 2 * S5_FHEAD_BYTES;
+static_assert(S5_T8_BYTES >= 2 * 8 * T8STR, "flush data overlay smaller than the T terms");
 constexpr float S5_LOG2E = 1.4426950408889634f;
 
 struct S5Geo {
@@ -73,7 +87,7 @@ struct S5Layout {
   uint32_t total;
 };
 
-__host__ __device__ inline S5Layout s5_layout(const S5Geo& g, int max_units) {
+__host__ __device__ inline S5Layout s5_layout(const S5Geo& g, int max_units, bool flush) {
   S5Layout s;
   uint32_t o = 0;
   s.full = smem_take(o, S5_NS * 8);
@@ -92,7 +106,7 @@ __host__ __device__ inline S5Layout s5_layout(const S5Geo& g, int max_units) {
   s.kbuf0 = o;
   o += S5_NCW * 4096u;
   uint32_t r = 0;
-  s.t8 = smem_take(r, 2u * 8u * T8STR);
+  s.t8 = smem_take(r, flush ? S5_T8_BYTES : 2u * 8u * uint32_t(T8STR));
   s.cb = smem_take(r, 2u * 3u * 16u * 2u);
   s.misc = smem_take(r, 2u * 16u);
   s.vnew = smem_take(r, 2u * 128u * 2u);
@@ -217,10 +231,13 @@ __device__ __forceinline__ void s5_unpack4(uint4 w, bool bf16, float* x) {
 }
 
 // Unit descriptor in the table: bits 0-7 slots replayed (this token included),
-// 8-15 slots read from memory, bit 16 skip (flush elsewhere, or a bad position).
+// 8-15 slots read from memory, bit 16 skip (a bad position, or a flush the
+// caller ruled out), bit 17 flush (state rebuild + re-quantisation here).
 __device__ __forceinline__ int s5_n(int code) { return code & 0xff; }
 __device__ __forceinline__ int s5_nmem(int code) { return (code >> 8) & 0xff; }
 __device__ __forceinline__ bool s5_skip(int code) { return (code >> 16) & 1; }
+// bit 17: the unit flushes here (rebuild + re-quantisation in this kernel)
+__device__ __forceinline__ bool s5_flush(int code) { return (code >> 17) & 1; }
 
 struct S5Unit {
   int b, h, pp, hv0;
@@ -382,14 +399,17 @@ __device__ __forceinline__ S5In s5_fetch(const StepParams& p, const S5Unit& U, i
 }
 
 // Unit descriptor (see s5_n / s5_nmem / s5_skip) from its raw position inputs.
+// here: flush units are rebuilt in this kernel (bit 17); otherwise they are
+// skipped (bit 16) -- the caller promised none (GDNR_FLUSH_NONE).
 template <bool FUSED>
-__device__ __forceinline__ int s5_code(int raw, int flag, int L) {
+__device__ __forceinline__ int s5_code(int raw, int flag, int L, bool here) {
+  const int fl = here ? (1 << 17) : (1 << 16);
   if constexpr (FUSED) {
     if (raw < 0 || raw >= L) return 1 << 16;
-    return (raw + 1) | (raw << 8) | ((raw == L - 1 ? 1 : 0) << 16);
+    return (raw + 1) | (raw << 8) | (raw == L - 1 ? fl : 0);
   } else {
     const int v = raw < 0 ? 0 : (raw > L ? L : raw);
-    return v | (v << 8) | ((flag != 0 ? 1 : 0) << 16);
+    return v | (v << 8) | (flag != 0 ? fl : 0);
   }
 }
 
@@ -476,7 +496,7 @@ __device__ __forceinline__ void s5_tloop(const uint8_t* kbuf, float wj, int n, f
 
 // The chain of one unit (one warp, both heads).  kbuf: the unit's key ring
 // (swizzled, slots < nmem loaded); res: this warp's result block.
-template <bool FUSED, int HPU>
+template <bool FUSED, int HPU, bool FLUSH>
 __device__ __forceinline__ S5Append s5_chain(const StepParams& p, const S5Unit& U, int code, const S5In& in,
                                              uint8_t* kbuf, uint8_t* res, const S5Layout& lay, int lane) {
   S5Append ap{};
@@ -608,6 +628,113 @@ __device__ __forceinline__ S5Append s5_chain(const StepParams& p, const S5Unit& 
   }
   const float Llast = __shfl_sync(0xffffffffu, Lg, 15, 16);  // slots >= n add nothing
   const float a_own = s5_ex2(Lg);
+  if (FLUSH && s5_flush(code)) {
+    // flush unit: hand the rebuild's inputs to the readout team (the T chain
+    // is not needed: the flush output comes from the rebuilt state)
+    __syncwarp();  // q-split / Gram scratch is dead from here on
+    uint8_t* fd = res + lay.t8;
+    // q split as f16 x 256 (B operand of E = S0 [K; q]^T)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float hq = __half2float(__float2half_rn(qv[i] * KPOW));
+      reinterpret_cast<__half*>(fd + S5_FQ16)[4 * lane + i] = __float2half_rn(hq);
+      reinterpret_cast<__half*>(fd + S5_FQ16)[128 + 4 * lane + i] = __float2half_rn(qv[i] * KPOW - hq);
+    }
+    {
+      // per head (16-lane segment e): a_t, beta_t; N[j][m] = M[j][m] beta_m (j < m)
+      // with w_j = d_j kq_j on its diagonal; then lane t solves column t of
+      // T = (I + N)^-1 and (redundantly) z = T w by back substitution
+      float* fh = reinterpret_cast<float*>(fd + S5_FHEAD + (e < HPU ? e : 0) * S5_FHEAD_BYTES);
+      float* nm = fh + S5_FN;
+      const bool live = t < n, wr = e < HPU;
+      const float bt = live ? beta_own : 0.0f;
+      const float dt = live ? s5_ex2(Llast - Lg) : 0.0f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {  // row t of N
+        const float mj = s5_ex2(__shfl_sync(0xffffffffu, Lg, j, 16) - Lg) * grow[j];
+        const float bj = __shfl_sync(0xffffffffu, bt, j, 16);
+        if (wr) nm[t * 16 + j] = j > t ? (live ? mj * bj : 0.0f) : (j == t ? dt * kq : 0.0f);
+      }
+      if (wr) {
+        fh[S5_FA + t] = live ? a_own : 0.0f;
+        fh[S5_FB + t] = bt;
+      }
+      __syncwarp();
+      float tc[16], z[16];
+#pragma unroll
+      for (int j = 15; j >= 0; --j) {
+        float row[16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 v = reinterpret_cast<const float4*>(nm + j * 16)[q];
+          row[4 * q] = v.x;
+          row[4 * q + 1] = v.y;
+          row[4 * q + 2] = v.z;
+          row[4 * q + 3] = v.w;
+        }
+        float at = j == t ? 1.0f : 0.0f, az = row[j];
+#pragma unroll
+        for (int m = j + 1; m < 16; ++m) {
+          at = fmaf(-row[m], tc[m], at);
+          az = fmaf(-row[m], z[m], az);
+        }
+        tc[j] = at;
+        z[j] = az;
+      }
+      // B operand of U = R [T diag(d) | z]: row t = column t of T diag(d), row 16 = z,
+      // as f16 hi / lo after a power-of-two scale
+      float mx = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        tc[j] *= dt;
+        mx = fmaxf(mx, fmaxf(fabsf(tc[j]), fabsf(z[j])));
+      }
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float ts = s5_pow2_scale(mx);
+      __syncwarp();  // N is read; the operand rows overwrite it
+      __half* tb = reinterpret_cast<__half*>(nm);
+      auto put_row = [&](int r, const float* x) {
+        uint32_t hw[8], lw[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const float x0 = x[2 * c] * ts, x1 = x[2 * c + 1] * ts;
+          const float h0 = __half2float(__float2half_rn(x0)), h1 = __half2float(__float2half_rn(x1));
+          hw[c] = pack_f16x2(h0, h1);
+          lw[c] = pack_f16x2(x0 - h0, x1 - h1);
+        }
+        uint4* dh = reinterpret_cast<uint4*>(tb + r * 16);
+        uint4* dl = reinterpret_cast<uint4*>(tb + S5_TB_LO + r * 16);
+        dh[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        dh[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+        dl[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        dl[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+      };
+      if (wr) {
+        put_row(t, tc);
+        if (t == 0) {
+          put_row(16, z);
+          fh[S5_FINV] = 1.0f / ts;
+        }
+      }
+    }
+    __syncwarp();
+    // key ring in place to f16 x 256 (slots >= n zero): B operand of E and of W K
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int c = lane + 32 * i;  // 16-byte chunk; its 128-byte line is c / 8, its slot c / 16
+      uint4 w = reinterpret_cast<const uint4*>(kbuf)[c];
+      const bool live = (c >> 4) < n;
+      uint32_t* wv = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const float2 f = bf16x2_to_f2(wv[h]);
+        wv[h] = live ? pack_f16x2(f.x * KPOW, f.y * KPOW) : 0u;
+      }
+      reinterpret_cast<uint4*>(kbuf)[c] = w;
+    }
+    return ap;
+  }
   const float bsel = t < n ? beta_own : 0.0f;
   float acc = t < n ? s5_ex2(Llast - Lg) * kq : 0.0f;
   float cval = 0.0f;
@@ -719,6 +846,232 @@ __device__ __forceinline__ void s5_readout(const uint8_t* ck_s, const uint8_t* v
   }
 }
 
+// ---------------------------------------------------------------- flush (rebuild + re-quantisation)
+// One vblock (rows rb .. rb + 31 of a head) of a flush unit, by one warp, in WY form
+// (the token loop of ref.py:137-163, kern.py:200-240):
+//   E = S0 [K; q]^T                      (f16 MMA: S0 from the e4m3 tile, K and q as f16 x 256)
+//   R_t = beta_t (v_t - a_t E_t)         (accumulator layout, slots t < n)
+//   [W | y] = R [T diag(d) | z]          (f16 hi / lo MMA; T = (I + N)^-1 and z = T (d kq)
+//                                         from the chain warp, so u = R T solves
+//                                         u_t = R_t - sum_{j<t} u_j beta_t M[j][t])
+//   o = a_{n-1} (S0 q) + y,  S_L = a_{n-1} S0 + W K,
+// then the vblock32 re-quantisation (ref.py:40-106) written into the tile in place.
+// tile: the head's e4m3 tile (swizzled); vr: its value ring; vnew: this token's
+// value row (slot nmem) or null; kf: the unit's key ring as f16 x 256; fq: q split
+// [2][128] f16 x 256; fh: the head's flush block.  o(row rb + i) (before K^-1/2) -> ost[i].
+__device__ __forceinline__ void s5_flush_vblock(uint8_t* tile, const uint8_t* vr, const uint16_t* vnew,
+                                                const uint8_t* kf, const __half* fq, const float* fh, int rb,
+                                                int n, int nmem, float sc, int quant_rounded, void* scale_ptr,
+                                                int64_t sc_index, int sc_dt, float* ost, int lane) {
+  const int g8 = lane >> 2, t4 = lane & 3;
+  const float* av = fh + S5_FA;
+  const float* bv = fh + S5_FB;
+  const __half* tb = reinterpret_cast<const __half*>(fh + S5_FN);
+  const uint32_t kf_addr = smem_addr(kf), vr_addr = smem_addr(vr);
+  const int mi = lane >> 3;
+  const float alast = n > 0 ? av[n - 1] : 1.0f;
+  const float asc = alast * sc;
+  const float esc = sc * INV_KPOW;
+  // ---- E = S0 [K; q]^T for both m-tiles (rows rb + 16 mt + g8 (+8))
+  float e[2][3][4];
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < 3; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) e[mt][nt][i] = 0.0f;
+#pragma unroll 2
+  for (int ks = 0; ks < 8; ++ks) {
+    uint32_t bk[4];
+    s5_ldsm_x4(kf_addr + s5_ring_off((lane & 7) + 8 * (mi & 1), 16 * ks + 8 * (mi >> 1)), bk);
+    const uint32_t q0 = g8 < 2 ? *reinterpret_cast<const uint32_t*>(fq + g8 * 128 + 16 * ks + 2 * t4) : 0u;
+    const uint32_t q1 = g8 < 2 ? *reinterpret_cast<const uint32_t*>(fq + g8 * 128 + 16 * ks + 8 + 2 * t4) : 0u;
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+      uint32_t a[4];
+      s0_afrag_f16(tile, rb + 16 * mt, ks, g8, t4, a);
+      mma16816(e[mt][0], a, bk[0], bk[2]);
+      mma16816(e[mt][1], a, bk[1], bk[3]);
+      mma16816(e[mt][2], a, q0, q1);
+    }
+  }
+  // ---- the operand rows (n-tiles 0, 1: T diag(d); n-tile 2: z in column 0)
+  uint32_t bh[3][2], bl[3][2];
+#pragma unroll
+  for (int nt = 0; nt < 3; ++nt) {
+    const int r = 8 * nt + g8;
+    const bool ok = r < 17;
+    bh[nt][0] = ok ? *reinterpret_cast<const uint32_t*>(tb + r * 16 + 2 * t4) : 0u;
+    bh[nt][1] = ok ? *reinterpret_cast<const uint32_t*>(tb + r * 16 + 8 + 2 * t4) : 0u;
+    bl[nt][0] = ok ? *reinterpret_cast<const uint32_t*>(tb + S5_TB_LO + r * 16 + 2 * t4) : 0u;
+    bl[nt][1] = ok ? *reinterpret_cast<const uint32_t*>(tb + S5_TB_LO + r * 16 + 8 + 2 * t4) : 0u;
+  }
+  const float tinv = fh[S5_FINV];
+  // lane's slots: t = 8 nt + 2 t4 + j (accumulator columns)
+  float at[2][2], bt[2][2];
+  bool lv[2][2], nw[2][2];
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int t = 8 * nt + 2 * t4 + j;
+      at[nt][j] = av[t] * esc;
+      bt[nt][j] = bv[t];
+      lv[nt][j] = t < n;
+      nw[nt][j] = vnew != nullptr && t == nmem;
+    }
+  uint32_t ahi[2][4], alo[2][4];
+  float dsc[2];
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt) {
+    // value-ring A fragment: (row g8 / g8+8, slots 2t4.. / 8+2t4..) as bf16 pairs
+    uint32_t va[4];
+    s5_ldsm_x4_t(vr_addr + s5_ring_off((lane & 7) + 8 * (mi >> 1), rb + 16 * mt + 8 * (mi & 1)), va);
+    const float vn0 = vnew != nullptr ? bf16_to_f(vnew[rb + 16 * mt + g8]) : 0.0f;
+    const float vn1 = vnew != nullptr ? bf16_to_f(vnew[rb + 16 * mt + g8 + 8]) : 0.0f;
+    float rr[2][4];  // [n-tile][c]: row g8 + 8 (c >> 1), slot 8 nt + 2 t4 + (c & 1)
+    float rmax = 0.0f;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const float2 v2 = bf16x2_to_f2(va[2 * nt + hf]);
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          float v = j ? v2.y : v2.x;
+          v = nw[nt][j] ? (hf ? vn1 : vn0) : v;
+          const float r = bt[nt][j] * (v - at[nt][j] * e[mt][nt][2 * hf + j]);
+          rr[nt][2 * hf + j] = lv[nt][j] ? r : 0.0f;
+          rmax = fmaxf(rmax, fabsf(rr[nt][2 * hf + j]));
+        }
+      }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, o));
+    const float rs = s5_pow2_scale(rmax);
+    uint32_t rh[4], rl[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {  // A fragment c: (n-tile c >> 1, row half c & 1)
+      const float x0 = rr[c >> 1][2 * (c & 1)] * rs, x1 = rr[c >> 1][2 * (c & 1) + 1] * rs;
+      const float h0 = __half2float(__float2half_rn(x0)), h1 = __half2float(__float2half_rn(x1));
+      rh[c] = pack_f16x2(h0, h1);
+      rl[c] = pack_f16x2(x0 - h0, x1 - h1);
+    }
+    float u[3][4];
+#pragma unroll
+    for (int nt = 0; nt < 3; ++nt) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) u[nt][i] = 0.0f;
+      mma16816(u[nt], rh, bh[nt][0], bh[nt][1]);
+      mma16816(u[nt], rh, bl[nt][0], bl[nt][1]);
+      mma16816(u[nt], rl, bh[nt][0], bh[nt][1]);
+    }
+    const float us = tinv / rs;
+    // output o = a_{n-1} (S0 q) + y: column 0 of n-tile 2 / E columns q_hi, q_lo (lanes t4 == 0)
+    if (t4 == 0) {
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf)
+        ost[16 * mt + g8 + 8 * hf] =
+            fmaf(asc * INV_KPOW, e[mt][2][2 * hf] + e[mt][2][2 * hf + 1], u[2][2 * hf] * us);
+    }
+    // W (A operand of W K), split hi / lo after a power-of-two scale
+    float wmax = 0.0f;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        u[nt][i] *= us;
+        wmax = fmaxf(wmax, fabsf(u[nt][i]));
+      }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) wmax = fmaxf(wmax, __shfl_xor_sync(0xffffffffu, wmax, o));
+    const float wp = s5_pow2_scale(wmax);
+    dsc[mt] = INV_KPOW / wp;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const float x0 = u[c >> 1][2 * (c & 1)] * wp, x1 = u[c >> 1][2 * (c & 1) + 1] * wp;
+      const float h0 = __half2float(__float2half_rn(x0)), h1 = __half2float(__float2half_rn(x1));
+      ahi[mt][c] = pack_f16x2(h0, h1);
+      alo[mt][c] = pack_f16x2(x0 - h0, x1 - h1);
+    }
+  }
+  // ---- S_L = a_{n-1} sc S0 + W K over columns 16 np .. 16 np + 15: x[i], i =
+  // ((h * 2 + mt) * 2 + hf) * 2 + j  <->  row rb + 16 mt + 8 hf + g8, column
+  // 16 np + 8 h + 2 t4 + j; its tile byte: row * 128 + 16 (np ^ g8) + 8 h + 2 t4 + j.
+  // S0 enters through an e4m3 MMA against an identity slice (exact, and in the
+  // accumulator layout): n-tile 2 np + h takes key columns 8 (2 (np & 1) + h) ..
+  // of the 32-column slice np / 2, i.e. B[k][c] = 1 for k = 8 (2 (np & 1) + h) + c.
+  uint8_t* const trow = tile + (rb + g8) * 128 + 2 * t4;
+  const uint32_t tile_addr = smem_addr(tile);
+  const uint32_t id0 = ((g8 >> 2) == t4) ? (0x38u << (8 * (g8 & 3))) : 0u;        // e4m3 1.0 at k = g8
+  const uint32_t id1 = (((8 + g8) >> 2) == t4) ? (0x38u << (8 * (g8 & 3))) : 0u;  // at k = 8 + g8
+  auto sl_cols = [&](int np, float* x) {
+    uint32_t bkt[4];  // n-tile 2np: (bkt[0], bkt[2]); 2np + 1: (bkt[1], bkt[3])
+    s5_ldsm_x4_t(kf_addr + s5_ring_off((lane & 7) + 8 * (mi >> 1), 16 * np + 8 * (mi & 1)), bkt);
+    const bool odd = np & 1;
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+      uint32_t as[4];  // e4m3 A fragment of rows rb + 16 mt .., key columns 32 (np / 2) ..
+      s5_ldsm_x4(tile_addr + s0_off(rb + 16 * mt + (lane & 7) + 8 * (mi & 1), 2 * (np >> 1) + (mi >> 1)), as);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        mma16816(acc, ahi[mt], bkt[h], bkt[2 + h]);
+        mma16816(acc, alo[mt], bkt[h], bkt[2 + h]);
+        const uint32_t id = h ? id1 : id0;
+        mma16832_e4m3(sv, as, odd ? 0u : id, odd ? id : 0u);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) x[((h * 2 + mt) * 2 + (c >> 1)) * 2 + (c & 1)] = fmaf(acc[c], dsc[mt], asc * sv[c]);
+      }
+    }
+  };
+  float amax = 0.0f;
+#pragma unroll 1
+  for (int np = 0; np < 8; ++np) {
+    float x[16];
+    sl_cols(np, x);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) amax = fmax_nan(amax, fabsf(x[i]));
+  }
+  amax = warp_max_nan(amax);
+  const VScale vs = vblock_scale(amax, quant_rounded);
+  const float rcp = __fdiv_rn(1.0f, vs.divisor);
+  const bool qok = quant_exact_ok(vs.divisor, rcp);
+  const uint32_t qkd = quant_exact_kd(vs.divisor);
+  __syncwarp();
+#pragma unroll 1
+  for (int np = 0; np < 8; ++np) {
+    float x[16];
+    sl_cols(np, x);
+    uint8_t* cp = trow + 16 * (np ^ g8);
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const int i = ((h * 2 + mt) * 2 + hf) * 2;
+          *reinterpret_cast<uint16_t*>(cp + (16 * mt + 8 * hf) * 128 + 8 * h) =
+              static_cast<uint16_t>(quant_e4m3x2(x[i], x[i + 1], vs.divisor, rcp, qkd, qok));
+        }
+  }
+  __syncwarp();
+  if (lane == 0) {
+    if (sc_dt == GDNR_F16)
+      static_cast<__half*>(scale_ptr)[sc_index] = vs.stored;
+    else
+      static_cast<float*>(scale_ptr)[sc_index] = __half2float(vs.stored);
+  }
+}
+
+__device__ __forceinline__ void s5_tma_store4(const CUtensorMap* map, const void* src, int c0, int c1, int c2,
+                                              int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_addr(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
 __device__ __forceinline__ uint32_t s5_ld_acquire(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_addr(p)) : "memory");
@@ -761,7 +1114,7 @@ __device__ __forceinline__ bool s5_warp_wait_count(const uint32_t* c, uint32_t t
   return ok != 0;
 }
 
-template <bool FUSED, int HPU>
+template <bool FUSED, int HPU, bool FLUSH>
 __global__ void __launch_bounds__(S5_THREADS, 1)
     step5_kernel(const __grid_constant__ StepParams p, const __grid_constant__ CUtensorMap ck_map,
                  const __grid_constant__ CUtensorMap kr_map, const __grid_constant__ CUtensorMap vr_map) {
@@ -773,7 +1126,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
   const int grid = int(gridDim.x), bid = int(blockIdx.x);
   const int nu = total > bid ? (total - bid + grid - 1) / grid : 0;
   const int max_units = (total + grid - 1) / grid;
-  const S5Layout lay = s5_layout(geo, max_units);
+  const S5Layout lay = s5_layout(geo, max_units, FLUSH);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + lay.full);
   uint64_t* empty = reinterpret_cast<uint64_t*>(smem + lay.empty);
   uint64_t* kfull = reinterpret_cast<uint64_t*>(smem + lay.kfull);
@@ -872,7 +1225,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
   if (tid == S5_THREADS - 1) griddep_launch();
   if (ti < nu) {
     const S5Unit U = s5_unit(bid + ti * grid, p.H, G, geo);
-    const int code = s5_code<FUSED>(raw0, raw1, L);
+    const int code = s5_code<FUSED>(raw0, raw1, L, FLUSH);
     if (FUSED && s5_n(code) == 0 && U.h == 0 && U.pp == 0) atomicOr(p.err, GDNR_DEVERR_BAD_POS);
     if (s5_n(code) > 0 && s5_skip(code) && p.flush_hint == GDNR_FLUSH_NONE && U.h == 0 && U.pp == 0)
       atomicOr(p.err, GDNR_DEVERR_BAD_HINT);
@@ -936,10 +1289,10 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
         in0 = s5_fetch<FUSED, HPU>(p, U, lane);
       }
       ok = s5_warp_wait(&kfull[cw], k & 1, p.err, abort, lane) && ok;
-      const int code = s5_code<FUSED>(in0.pos, in0.flag, L);
+      const int code = s5_code<FUSED>(in0.pos, in0.flag, L, FLUSH);
       const bool work = ok && !s5_skip(code);
       S5Append ap{};
-      if (work) ap = s5_chain<FUSED, HPU>(p, U, code, in0, kbuf, res, lay, lane);
+      if (work) ap = s5_chain<FUSED, HPU, FLUSH>(p, U, code, in0, kbuf, res, lay, lane);
       __syncwarp();
       if (lane == 0) s5_st_release(&cseq[cw], uint32_t(k + 1));
       if (work) s5_append<FUSED, HPU>(p, U, code, ap, lane);
@@ -975,22 +1328,40 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
     }
     bool ok = s5_warp_wait(&full[s], (i / S5_NS) & 1, p.err, abort, lane);
     ok = s5_warp_wait_count(&cseq[ccw], uint32_t(k + 1), p.err, abort, lane) && ok;
+    const bool flush = FLUSH && s5_flush(code);
+    uint8_t* sb = smem + lay.stage0 + s * lay.stage_bytes;
     if (ok && !s5_skip(code)) {
       const S5Unit U = s5_unit(bid + i * grid, p.H, G, geo);
-      const uint8_t* sb = smem + lay.stage0 + s * lay.stage_bytes;
       const uint8_t* res = smem + lay.res0 + ccw * lay.res_bytes;
       const float* misc = reinterpret_cast<const float*>(res + lay.misc) + head_r * 4;
-      s5_readout<MW>(sb + lay.ck + head_r * 16384, sb + lay.vr + head_r * 4096, res + lay.t8 + head_r * 8 * T8STR,
-                     reinterpret_cast<const uint16_t*>(res + lay.cb + head_r * 96), misc[0], sc, sc_base,
-                     rbase, s5_nmem(code), ost, lane);
+      if (flush) {
+        // rebuild this warp's rows vblock by vblock; the tile is re-quantised in place
+        const uint8_t* fd = res + lay.t8;
+        const uint16_t* vn = FUSED ? reinterpret_cast<const uint16_t*>(res + lay.vnew + head_r * 256) : nullptr;
+        const int64_t sc_row = int64_t(U.b) * p.sc_sb + int64_t(U.hv0 + head_r) * p.sc_sh;
+#pragma unroll 1
+        for (int v = 0; v < VBW; ++v) {
+          const int rb = rbase + VBLOCK * v;
+          const float scv = __shfl_sync(0xffffffffu, sc, sc_base + v);
+          s5_flush_vblock(sb + lay.ck + head_r * 16384, sb + lay.vr + head_r * 4096, vn,
+                          smem + lay.kbuf0 + ccw * 4096, reinterpret_cast<const __half*>(fd + S5_FQ16),
+                          reinterpret_cast<const float*>(fd + S5_FHEAD + head_r * S5_FHEAD_BYTES), rb,
+                          s5_n(code), s5_nmem(code), scv, p.quant_rounded, p.sc,
+                          sc_row + int64_t(rb / VBLOCK) * p.sc_sv, p.sc_dt, ost + VBLOCK * v, lane);
+        }
+      } else {
+        s5_readout<MW>(sb + lay.ck + head_r * 16384, sb + lay.vr + head_r * 4096, res + lay.t8 + head_r * 8 * T8STR,
+                       reinterpret_cast<const uint16_t*>(res + lay.cb + head_r * 96), misc[0], sc, sc_base,
+                       rbase, s5_nmem(code), ost, lane);
+      }
       __syncwarp();
-      // this token's own slot (fused) as a rank-one term, K^-1/2, coalesced store
+      // this token's own slot (fused, no flush) as a rank-one term, K^-1/2, coalesced store
       constexpr int RPL = ROWS / 32;  // rows per lane: 4 or 2
       const int r0 = RPL * lane;
       float o[RPL];
 #pragma unroll
       for (int q = 0; q < RPL; ++q) o[q] = ost[r0 + q];
-      if constexpr (FUSED) {
+      if (FUSED && !flush) {
         const float cpos = misc[1];
         const uint16_t* vnew = reinterpret_cast<const uint16_t*>(res + lay.vnew + head_r * 256) + rbase;
 #pragma unroll
@@ -1019,12 +1390,27 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
           store_scalar(p.out, obase + int64_t(rbase + r0 + q) * p.o_sv, p.o_dt, o[q] * KSCALE_H);
       }
     }
+    if (flush) {
+      // both warps' rows are in the tile: one tensor store of the unit's
+      // checkpoint tiles (same map and swizzle as the load); the stage is
+      // released once the copy engine has read it
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      asm volatile("bar.sync %0, %1;" ::"r"(4 + team), "n"(32 * S5_TEAM) : "memory");
+      if (mem == 0 && lane == 0 && *abort == 0) {
+        const S5Unit U = s5_unit(bid + i * grid, p.H, G, geo);
+        s5_tma_store4(&ck_map, sb + lay.ck, 0, 0, U.hv0, U.b);
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+      }
+    }
     __syncwarp();
     if (lane == 0) {
       s5_arrive(&empty[s]);
       s5_add_release(&rcnt[ccw], 1u);
     }
   }
+  // the checkpoint stores are complete before the kernel ends
+  if (FLUSH && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
 // ---------------------------------------------------------------- host side
@@ -1036,6 +1422,7 @@ static int s5_sm_count() {
 }
 
 static bool s5_grid(const StepParams& p, int& grid, S5Layout& lay) {
+  const bool flush = p.flush_hint != GDNR_FLUSH_NONE;
   const int nsm = s5_sm_count();
   if (nsm <= 0) return false;
   const S5Geo g = s5_geo(p.H, p.HV, p.L);
@@ -1044,7 +1431,7 @@ static bool s5_grid(const StepParams& p, int& grid, S5Layout& lay) {
   grid = int(total < nsm ? total : nsm);
   const int max_units = int((total + grid - 1) / grid);
   if (max_units > 32 * S5_NRW) return false;  // the unit table is filled in one pass by the readout warps
-  lay = s5_layout(g, max_units);
+  lay = s5_layout(g, max_units, flush);
   return true;
 }
 
@@ -1087,10 +1474,10 @@ static S5EncodeFn s5_encode_fn() {
   return fn;
 }
 
-template <bool FUSED, int HPU>
+template <bool FUSED, int HPU, bool FLUSH>
 static cudaError_t s5_launch(const StepParams& p, const CUtensorMap& ck, const CUtensorMap& kr,
                              const CUtensorMap& vr, int grid, uint32_t smem, bool pdl, cudaStream_t stream) {
-  auto kern = step5_kernel<FUSED, HPU>;
+  auto kern = step5_kernel<FUSED, HPU, FLUSH>;
   static int configured = 0;
   if (int(smem) > configured) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
@@ -1141,11 +1528,22 @@ cudaError_t launch_step5(const StepParams& p, bool fused, bool pdl, cudaStream_t
   };
   if (ring_map(&kr, p.kr, p.H, p.kr_sh, p.kr_st, p.kr_sb) != CUDA_SUCCESS) return cudaErrorInvalidValue;
   if (ring_map(&vr, p.vr, p.HV, p.vr_sh, p.vr_st, p.vr_sb) != CUDA_SUCCESS) return cudaErrorInvalidValue;
-  if (fused)
-    return g.hpu == 2 ? s5_launch<true, 2>(p, ck, kr, vr, grid, lay.total, pdl, stream)
-                      : s5_launch<true, 1>(p, ck, kr, vr, grid, lay.total, pdl, stream);
-  return g.hpu == 2 ? s5_launch<false, 2>(p, ck, kr, vr, grid, lay.total, pdl, stream)
-                    : s5_launch<false, 1>(p, ck, kr, vr, grid, lay.total, pdl, stream);
+  // GDNR_FLUSH_NONE: the variant without the flush path (flushing units are
+  // skipped and reported); otherwise the flush-capable one
+  const bool flush = p.flush_hint != GDNR_FLUSH_NONE;
+  const uint32_t sm = lay.total;
+  if (fused) {
+    if (g.hpu == 2)
+      return flush ? s5_launch<true, 2, true>(p, ck, kr, vr, grid, sm, pdl, stream)
+                   : s5_launch<true, 2, false>(p, ck, kr, vr, grid, sm, pdl, stream);
+    return flush ? s5_launch<true, 1, true>(p, ck, kr, vr, grid, sm, pdl, stream)
+                 : s5_launch<true, 1, false>(p, ck, kr, vr, grid, sm, pdl, stream);
+  }
+  if (g.hpu == 2)
+    return flush ? s5_launch<false, 2, true>(p, ck, kr, vr, grid, sm, pdl, stream)
+                 : s5_launch<false, 2, false>(p, ck, kr, vr, grid, sm, pdl, stream);
+  return flush ? s5_launch<false, 1, true>(p, ck, kr, vr, grid, sm, pdl, stream)
+               : s5_launch<false, 1, false>(p, ck, kr, vr, grid, sm, pdl, stream);
 }
 
 }  // namespace gdnr

@@ -77,3 +77,46 @@ def test_quantize_strided_views(cuda_device):
     ref = O.quantize_checkpoint(big[1:3, ::2], "vblock", 32)
     assert np.array_equal(to_np(payload.contiguous()), ref.payload)
     assert np.array_equal(scale.cpu().numpy().view(np.uint16), ref.scale.view(np.uint16))
+
+
+def _e4m3_midpoints():
+    vals = [k * 2.0 ** -9 for k in range(8)]
+    vals += [2.0 ** e * (1 + m / 8) for e in range(-6, 9) for m in range(8) if 2.0 ** e * (1 + m / 8) <= 448.0]
+    vals = np.array(sorted(vals))
+    return ((vals[:-1] + vals[1:]) / 2).astype(np.float32)  # at most 5 significant bits: exact
+
+
+@pytest.mark.parametrize("divisor", ["oracle", "rounded"])
+def test_quantize_near_midpoints(cuda_device, divisor):
+    """Quotients on, and a few ulp around, every e4m3 rounding midpoint (normal
+    and subnormal range, both signs), for many divisors: bytes equal the IEEE
+    division's rounding, ties to even."""
+    rng = np.random.default_rng(21)
+    mids = _e4m3_midpoints()
+    B, HV = 4, 8
+    s = (0.1 * rng.standard_normal((B, HV, 128, 128))).astype(np.float32)
+    for b in range(B):
+        for hv in range(HV):
+            for vb in range(4):
+                amax = np.float32(10.0 ** rng.uniform(-4, 4))
+                d = np.float32(amax / np.float32(448.0))
+                if divisor == "rounded":
+                    d = np.float32(np.float16(d))
+                block = s[b, hv, 32 * vb:32 * vb + 32].reshape(-1)
+                x0 = (mids.astype(np.float64) * np.float64(d)).astype(np.float32)
+                vals = []
+                for k in range(-3, 4):
+                    xk = x0.copy()
+                    for _ in range(abs(k)):
+                        xk = np.nextafter(xk, np.float32(np.inf) if k > 0 else np.float32(0), dtype=np.float32)
+                    vals.append(xk)
+                v = np.concatenate(vals)
+                v = np.concatenate([v, -v])
+                v = v[np.abs(v) <= amax]
+                block[:] = np.float32(0.01) * amax * rng.standard_normal(block.size).astype(np.float32)
+                block[1:1 + v.size] = v
+                block[0] = amax
+                s[b, hv, 32 * vb:32 * vb + 32] = block.reshape(32, 128)
+    q = gdnr.quantize_checkpoint(to_dev(s, torch.float32), quant_divisor=divisor)
+    ref = O.quantize_vblock32(s, divisor=divisor)
+    assert compare_payload(to_np(q.payload), ref.payload) == 0

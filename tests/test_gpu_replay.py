@@ -68,13 +68,15 @@ def test_replay_matches_adjoint_oracle(cuda_device):
     assert O.relative_l2(to_np(out32), ref) < TOL_F32_KERNEL
 
 
+@pytest.mark.parametrize("heads", [(2, 4), (2, 2)])
 @pytest.mark.parametrize("divisor", ["oracle", "rounded"])
-def test_replay_flush_matches_oracle(cuda_device, divisor):
+def test_replay_flush_matches_oracle(cuda_device, divisor, heads):
     B, L = 4, 6
-    d, ck, dev = setup_case(3, B, L)
+    H, HV = heads
+    d, ck, dev = setup_case(3, B, L, H=H, HV=HV)
     valid = np.array([L, 3, 0, L], np.int32)
     flush = np.array([1, 1, 1, 0], np.bool_)
-    out = torch.empty(B, 4, 128, dtype=torch.float32, device="cuda")
+    out = torch.empty(B, HV, 128, dtype=torch.float32, device="cuda")
     gdnr.gdn_replay_fp8(dev["checkpoint"], dev["scale"], dev["q"], dev["k"], dev["v"], dev["g"], dev["beta"],
                         to_dev(valid, torch.int32), to_dev(flush, torch.bool), out=out, quant_divisor=divisor)
     ref_out, ref_states = oracle_replay_out(O.dequantize_checkpoint(ck), d["q"], d["k"], d["v"], d["g"], d["beta"],
