@@ -297,21 +297,48 @@ __device__ __forceinline__ uint32_t quant_e4m3x2(float x0, float x1, float d, fl
   return f2_to_e4m3x2(y0, y1);
 }
 
+// e4m3 codes of RN(x / d) for NP pairs, the common case without a division and
+// without the per-element work of quant_exact.  y = RN(x * rcp) is within one
+// ulp of the IEEE quotient RN(x / d) (rcp = RN(1 / d) has relative error at
+// most 2^-24, so |x rcp - x / d| < ulp), and RN(y (1 -+ 2^-23)) lie at least one
+// ulp below / above y, so they bracket the quotient (for a normal y; a subnormal
+// y and its quotient both convert to +-0).  When both brackets convert to the
+// same e4m3 value, so does the quotient (the conversion is monotonic) and cvt(y)
+// is exact; otherwise -- near a rounding midpoint, about 6e-5 of the values of a
+// flushed checkpoint -- the pair is redone with quant_e4m3x2 behind one
+// warp-uniform branch.  All lanes of the warp call it together.
+template <int NP>
+__device__ __forceinline__ void quant_pairs_warp(const float* x, uint32_t* c, float d, float rcp, uint32_t kd,
+                                                 bool ok) {
+  const float lo = __uint_as_float(0x3F7FFFFEu), hi = __uint_as_float(0x3F800001u);  // 1 -+ 2^-23
+  uint32_t amb = ok ? 0u : 0xFFFFFFFFu;
+#pragma unroll
+  for (int j = 0; j < NP; ++j) {
+    const float y0 = x[2 * j] * rcp, y1 = x[2 * j + 1] * rcp;
+    c[j] = f2_to_e4m3x2(y0, y1);
+    const uint32_t ca = f2_to_e4m3x2(y0 * lo, y1 * lo), cb = f2_to_e4m3x2(y0 * hi, y1 * hi);
+    amb |= uint32_t(ca != cb) << j;
+  }
+  if (__any_sync(0xffffffffu, amb != 0u)) {
+#pragma unroll
+    for (int j = 0; j < NP; ++j)
+      if ((amb >> j) & 1u) c[j] = quant_e4m3x2(x[2 * j], x[2 * j + 1], d, rcp, kd, ok);
+  }
+}
+
 // e4m3 pair with satfinite: RNE, then |y| > 448 -> 448 and NaN -> NaN, which
 // equals clamp(+-448) followed by the cast (ref.py:99).
 __device__ __forceinline__ uint32_t e4m3x2_sat(float lo, float hi) { return f2_to_e4m3x2(lo, hi); }
 
-// 16 values (division-free exact quantiser); with count_sat, also counts
-// |x/divisor| > 448 from the IEEE quotient.
+// 16 values (all lanes of the warp together; exact, see quant_pairs_warp); with
+// count_sat, also counts |x/divisor| > 448 from the IEEE quotient.
 __device__ __forceinline__ uint4 quantize16_fast(const float* x, float divisor, float rcp, bool count_sat,
                                                  uint32_t& sat) {
-  const bool ok = quant_exact_ok(divisor, rcp);
-  const uint32_t kd = quant_exact_kd(divisor);
+  uint32_t c[8];
+  quant_pairs_warp<8>(x, c, divisor, rcp, quant_exact_kd(divisor), quant_exact_ok(divisor, rcp));
   uint32_t w[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
-    w[i] = quant_e4m3x2(x[4 * i], x[4 * i + 1], divisor, rcp, kd, ok) |
-           (quant_e4m3x2(x[4 * i + 2], x[4 * i + 3], divisor, rcp, kd, ok) << 16);
+  for (int i = 0; i < 4; ++i) w[i] = c[2 * i] | (c[2 * i + 1] << 16);
   if (count_sat) {
     const bool fast = quant_fast_ok(divisor, rcp);
 #pragma unroll

@@ -512,6 +512,7 @@ __device__ __forceinline__ void head_flush(const HeadTile& T, const HeadScratch&
       const int col = 8 * nt + g8;
       const uint32_t b0 = *reinterpret_cast<const uint32_t*>(kt + col * KTSTR + 2 * t4);
       const uint32_t b1 = *reinterpret_cast<const uint32_t*>(kt + col * KTSTR + 8 + 2 * t4);
+      float x[8];  // (mt, hf) pairs: rows rw0 + 16 mt + g8 + 8 hf, columns 8 nt + 2 t4 (+1)
 #pragma unroll
       for (int mt = 0; mt < 2; ++mt) {
         float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -522,17 +523,27 @@ __device__ __forceinline__ void head_flush(const HeadTile& T, const HeadScratch&
         for (int hf = 0; hf < 2; ++hf) {
           const int r = rw0 + 16 * mt + g8 + 8 * hf;
           const int cc = 8 * nt + 2 * t4;  // even column pair (cc, cc+1)
-          uint8_t* sp = s0 + s0_off(r, cc >> 4) + (cc & 15);
+          const uint8_t* sp = s0 + s0_off(r, cc >> 4) + (cc & 15);
           const uint32_t h2 = e4m3x2_to_f16x2(*reinterpret_cast<const uint16_t*>(sp));
           const float2 sf = __half22float2(*reinterpret_cast<const __half2*>(&h2));
-          const float x0 = fmaf(acc[2 * hf], dsc, asc * sf.x);
-          const float x1 = fmaf(acc[2 * hf + 1], dsc, asc * sf.y);
-          if (pass == 0) {
-            amax = fmax_nan(amax, fmax_nan(fabsf(x0), fabsf(x1)));
-          } else {
-            *reinterpret_cast<uint16_t*>(sp) = static_cast<uint16_t>(quant_e4m3x2(x0, x1, vs.divisor, rcp, quant_exact_kd(vs.divisor), fast));
-          }
+          x[(mt * 2 + hf) * 2] = fmaf(acc[2 * hf], dsc, asc * sf.x);
+          x[(mt * 2 + hf) * 2 + 1] = fmaf(acc[2 * hf + 1], dsc, asc * sf.y);
         }
+      }
+      if (pass == 0) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax = fmax_nan(amax, fabsf(x[i]));
+      } else {
+        uint32_t c[4];
+        quant_pairs_warp<4>(x, c, vs.divisor, rcp, quant_exact_kd(vs.divisor), fast);
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            const int r = rw0 + 16 * mt + g8 + 8 * hf;
+            const int cc = 8 * nt + 2 * t4;
+            *reinterpret_cast<uint16_t*>(s0 + s0_off(r, cc >> 4) + (cc & 15)) = static_cast<uint16_t>(c[mt * 2 + hf]);
+          }
       }
     }
   }

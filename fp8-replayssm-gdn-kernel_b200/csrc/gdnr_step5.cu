@@ -46,10 +46,11 @@ constexpr int S5_GSTR = 20;  // Gram scratch row (floats): 16 key columns + 3 qu
 // A chain warp's result area: T terms of a non-flush unit (2 x 8 x T8STR), or the
 // flush data of a flush unit -- q split as f16 x 256 [2][128], then per head
 // (float offsets) a_t [16] at S5_FA, beta_t [16] at S5_FB, 1 / (operand scale) at
-// S5_FINV, and from S5_FN the f16 operand rows [T diag(d) | z]^T: hi [17][16], then
-// lo [17][16] (the chain's N [16][16] f32 scratch before that).
+// S5_FINV, the head's four vblock scales at S5_FSC, and from S5_FN the f16 operand
+// rows [T diag(d) | z]^T: hi [17][16], then lo [17][16] (the chain's N [16][16]
+// f32 scratch before that).
 constexpr uint32_t S5_FQ16 = 0, S5_FHEAD = 512;
-constexpr int S5_FA = 0, S5_FB = 16, S5_FINV = 32, S5_FN = 36, S5_TB_LO = 17 * 16;
+constexpr int S5_FA = 0, S5_FB = 16, S5_FINV = 32, S5_FSC = 36, S5_FN = 40, S5_TB_LO = 17 * 16;
 constexpr uint32_t S5_FHEAD_BYTES = S5_FN * 4 + 1088;  // max(N: 1024, operand rows: 2 x 17 x 16 x 2)
 constexpr uint32_t S5_T8_BYTES = S5_FHEAD + 2 * S5_FHEAD_BYTES;
 static_assert(S5_T8_BYTES >= 2 * 8 * T8STR, "flush data overlay smaller than the T terms");
@@ -78,7 +79,7 @@ __host__ __device__ inline S5Geo s5_geo(int H, int HV, int L) {
 //        doubles as the chain's q-split / Gram scratch before T is written)
 //   [ost: 128 floats] x S5_NRW
 struct S5Layout {
-  uint32_t full, empty, kfull, cseq, rcnt, abort, table;
+  uint32_t full, empty, kfull, cseq, rcnt, abort, vword, vdone, table;
   uint32_t stage0, stage_bytes, ck, vr;
   uint32_t kbuf0;
   uint32_t res0, res_bytes, t8, cb, misc, vnew;
@@ -96,6 +97,8 @@ __host__ __device__ inline S5Layout s5_layout(const S5Geo& g, int max_units, boo
   s.cseq = smem_take(o, S5_NCW * 4);
   s.rcnt = smem_take(o, S5_NCW * 4);
   s.abort = smem_take(o, 16);
+  s.vword = smem_take(o, S5_NS * 4);
+  s.vdone = smem_take(o, S5_NS * 4);
   s.table = smem_take(o, uint32_t(max_units) * 4u);
   o = (o + 1023u) & ~1023u;
   s.stage0 = o;
@@ -363,9 +366,10 @@ struct S5In {
   uint32_t a, bb;     // this token's gate inputs of head e (fused)
   float alog, dtb;
   int pos, flag;      // ring position (fused) / valid_len and flush (replay)
+  uint32_t scr;       // vblock scale (head e, vblock t % 4), flush-capable variant
 };
 
-template <bool FUSED, int HPU>
+template <bool FUSED, int HPU, bool FLUSH>
 __device__ __forceinline__ S5In s5_fetch(const StepParams& p, const S5Unit& U, int lane) {
   S5In in;
   const int e = lane >> 4, t = lane & 15;
@@ -373,6 +377,8 @@ __device__ __forceinline__ S5In s5_fetch(const StepParams& p, const S5Unit& U, i
   const int ts = t < p.L ? t : p.L - 1;
   in.g = s5_ld_raw(p.gr, int64_t(U.b) * p.gr_sb + int64_t(ts) * p.gr_st + int64_t(hv) * p.gr_sh, p.gr_dt);
   in.beta = s5_ld_raw(p.br, int64_t(U.b) * p.br_sb + int64_t(ts) * p.br_st + int64_t(hv) * p.br_sh, p.br_dt);
+  in.scr = FLUSH ? s5_ld_raw(p.sc, int64_t(U.b) * p.sc_sb + int64_t(hv) * p.sc_sh + int64_t(t & 3) * p.sc_sv, p.sc_dt)
+                 : 0u;
   if constexpr (FUSED) {
     const bool bf = p.mx_dt == GDNR_BF16;
     const int64_t row = int64_t(U.b) * p.mx_sb;
@@ -658,6 +664,7 @@ __device__ __forceinline__ S5Append s5_chain(const StepParams& p, const S5Unit& 
       if (wr) {
         fh[S5_FA + t] = live ? a_own : 0.0f;
         fh[S5_FB + t] = bt;
+        if (t < 4) fh[S5_FSC + t] = s5_cvt(in.scr, p.sc_dt);
       }
       __syncwarp();
       float tc[16], z[16];
@@ -1042,17 +1049,17 @@ __device__ __forceinline__ void s5_flush_vblock(uint8_t* tile, const uint8_t* vr
   for (int np = 0; np < 8; ++np) {
     float x[16];
     sl_cols(np, x);
+    uint32_t cq[8];
+    quant_pairs_warp<8>(x, cq, vs.divisor, rcp, qkd, qok);
     uint8_t* cp = trow + 16 * (np ^ g8);
 #pragma unroll
     for (int h = 0; h < 2; ++h)
 #pragma unroll
       for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          const int i = ((h * 2 + mt) * 2 + hf) * 2;
+        for (int hf = 0; hf < 2; ++hf)
           *reinterpret_cast<uint16_t*>(cp + (16 * mt + 8 * hf) * 128 + 8 * h) =
-              static_cast<uint16_t>(quant_e4m3x2(x[i], x[i + 1], vs.divisor, rcp, qkd, qok));
-        }
+              static_cast<uint16_t>(cq[(h * 2 + mt) * 2 + hf]);
   }
   __syncwarp();
   if (lane == 0) {
@@ -1114,6 +1121,54 @@ __device__ __forceinline__ bool s5_warp_wait_count(const uint32_t* c, uint32_t t
   return ok != 0;
 }
 
+// ---------------------------------------------------------------- flush task pool
+// A flush unit's vblocks (4 per head) are tasks that the readout team of the
+// unit's stage shares out: the team publishes the unit in the stage's task word
+// (unit << 8 | next task) and each warp claims tasks with compare-and-swap until
+// none is left, so the work balances between the two warps whatever the
+// per-task times.  A claim for another unit never succeeds.
+__device__ __forceinline__ int s5_claim(uint32_t* vword, int unit, int ntask, int lane) {
+  int t = -1;
+  if (lane == 0) {
+    uint32_t w = s5_ld_acquire(vword);
+    while ((w >> 8) == uint32_t(unit) && int(w & 0xffu) < ntask) {
+      const uint32_t prev = atomicCAS(vword, w, w + 1u);
+      if (prev == w) {
+        t = int(w & 0xffu);
+        break;
+      }
+      w = prev;
+    }
+  }
+  return __shfl_sync(0xffffffffu, t, 0);
+}
+
+// Task `task` of flush unit U (stage s, chain results of chain warp ccw): head
+// task / 4 (two-head units), vblock task % 4.  Its 32 outputs go through
+// `stage` (32 floats of the executing warp) to HBM; its rows of the tile are
+// re-quantised in place and made visible to the tensor-map store.
+template <bool FUSED, int HPU>
+__device__ __forceinline__ void s5_flush_task(const StepParams& p, uint8_t* smem, const S5Layout& lay,
+                                              const S5Unit& U, int s, int ccw, int code, int task, float* stage,
+                                              int lane) {
+  const int head = HPU == 2 ? task >> 2 : 0, v = task & 3;
+  uint8_t* sb = smem + lay.stage0 + s * lay.stage_bytes;
+  const uint8_t* res = smem + lay.res0 + ccw * lay.res_bytes;
+  const uint8_t* fd = res + lay.t8;
+  const float* fh = reinterpret_cast<const float*>(fd + S5_FHEAD + head * S5_FHEAD_BYTES);
+  const int hv = U.hv0 + head;
+  s5_flush_vblock(sb + lay.ck + head * 16384, sb + lay.vr + head * 4096,
+                  FUSED ? reinterpret_cast<const uint16_t*>(res + lay.vnew + head * 256) : nullptr,
+                  smem + lay.kbuf0 + ccw * 4096, reinterpret_cast<const __half*>(fd + S5_FQ16), fh, VBLOCK * v,
+                  s5_n(code), s5_nmem(code), fh[S5_FSC + v], p.quant_rounded, p.sc,
+                  int64_t(U.b) * p.sc_sb + int64_t(hv) * p.sc_sh + int64_t(v) * p.sc_sv, p.sc_dt, stage, lane);
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  __syncwarp();
+  store_scalar(p.out, int64_t(U.b) * p.o_sb + int64_t(hv) * p.o_sh + int64_t(VBLOCK * v + lane) * p.o_sv, p.o_dt,
+               stage[lane] * KSCALE_H);
+  __syncwarp();
+}
+
 template <bool FUSED, int HPU, bool FLUSH>
 __global__ void __launch_bounds__(S5_THREADS, 1)
     step5_kernel(const __grid_constant__ StepParams p, const __grid_constant__ CUtensorMap ck_map,
@@ -1133,6 +1188,8 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
   uint32_t* cseq = reinterpret_cast<uint32_t*>(smem + lay.cseq);  // chains finished, per chain warp
   uint32_t* rcnt = reinterpret_cast<uint32_t*>(smem + lay.rcnt);  // readout parts finished, per chain warp
   volatile int* abort = reinterpret_cast<volatile int*>(smem + lay.abort);
+  uint32_t* vword = reinterpret_cast<uint32_t*>(smem + lay.vword);  // flush task word per stage
+  uint32_t* vdone = reinterpret_cast<uint32_t*>(smem + lay.vdone);  // flush tasks finished per stage
   int* table = reinterpret_cast<int*>(smem + lay.table);
   const bool aligned = (smem_addr(smem) & 1023u) == 0;  // swizzled TMA boxes need 1024-byte alignment
   const uint32_t box_bytes = uint32_t(geo.rb) * 256u;
@@ -1147,6 +1204,10 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       mbar_init(&kfull[c], 1);
       cseq[c] = 0;
       rcnt[c] = 0;
+    }
+    for (int st = 0; st < S5_NS; ++st) {
+      vword[st] = 0xffffffffu;
+      vdone[st] = 0u;
     }
     *abort = aligned ? 0 : 1;
     fence_mbar_init();
@@ -1183,7 +1244,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       mbar_arrive_expect_tx(&kfull[cw], uint32_t(nr) * box_bytes);
       for (int j = 0; j < nr; ++j) s5_tma5(kbuf + j * box_bytes, &kr_map, 0, 0, U.h, j * geo.rb, U.b, &kfull[cw]);
     }
-    in0 = s5_fetch<FUSED, HPU>(p, U, lane);
+    in0 = s5_fetch<FUSED, HPU, FLUSH>(p, U, lane);
     // the key rings and these loads go out first; the producer starts the
     // checkpoint stream once the ring positions (issued alongside) are back
     // (barriers 3 and 2): DRAM serves a running stream before scattered loads
@@ -1286,7 +1347,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
           for (int j = 0; j < nr; ++j)
             s5_tma5(kbuf + j * box_bytes, &kr_map, 0, 0, U.h, j * geo.rb, U.b, &kfull[cw]);
         }
-        in0 = s5_fetch<FUSED, HPU>(p, U, lane);
+        in0 = s5_fetch<FUSED, HPU, FLUSH>(p, U, lane);
       }
       ok = s5_warp_wait(&kfull[cw], k & 1, p.err, abort, lane) && ok;
       const int code = s5_code<FUSED>(in0.pos, in0.flag, L, FLUSH);
@@ -1330,38 +1391,46 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
     ok = s5_warp_wait_count(&cseq[ccw], uint32_t(k + 1), p.err, abort, lane) && ok;
     const bool flush = FLUSH && s5_flush(code);
     uint8_t* sb = smem + lay.stage0 + s * lay.stage_bytes;
-    if (ok && !s5_skip(code)) {
+    if (flush) {
+      // publish the unit's vblock tasks, take them, then write the re-quantised
+      // tiles back with one tensor-map store
+      constexpr int NT = 4 * HPU;
+      if (mem == 0 && lane == 0) {
+        vdone[s] = 0u;
+        __threadfence_block();
+        atomicExch(&vword[s], uint32_t(i) << 8);
+      }
+      asm volatile("bar.sync %0, %1;" ::"r"(4 + team), "n"(32 * S5_TEAM) : "memory");
+      const S5Unit U = s5_unit(bid + i * grid, p.H, G, geo);
+      if (ok) {
+        for (;;) {
+          const int t = s5_claim(&vword[s], i, NT, lane);
+          if (t < 0) break;
+          s5_flush_task<FUSED, HPU>(p, smem, lay, U, s, ccw, code, t, ost, lane);
+          if (lane == 0) s5_add_release(&vdone[s], 1u);
+        }
+      }
+      s5_warp_wait_count(&vdone[s], uint32_t(NT), p.err, abort, lane);
+      if (mem == 0 && lane == 0 && *abort == 0) {
+        s5_tma_store4(&ck_map, sb + lay.ck, 0, 0, U.hv0, U.b);
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+      }
+    } else if (ok && !s5_skip(code)) {
       const S5Unit U = s5_unit(bid + i * grid, p.H, G, geo);
       const uint8_t* res = smem + lay.res0 + ccw * lay.res_bytes;
       const float* misc = reinterpret_cast<const float*>(res + lay.misc) + head_r * 4;
-      if (flush) {
-        // rebuild this warp's rows vblock by vblock; the tile is re-quantised in place
-        const uint8_t* fd = res + lay.t8;
-        const uint16_t* vn = FUSED ? reinterpret_cast<const uint16_t*>(res + lay.vnew + head_r * 256) : nullptr;
-        const int64_t sc_row = int64_t(U.b) * p.sc_sb + int64_t(U.hv0 + head_r) * p.sc_sh;
-#pragma unroll 1
-        for (int v = 0; v < VBW; ++v) {
-          const int rb = rbase + VBLOCK * v;
-          const float scv = __shfl_sync(0xffffffffu, sc, sc_base + v);
-          s5_flush_vblock(sb + lay.ck + head_r * 16384, sb + lay.vr + head_r * 4096, vn,
-                          smem + lay.kbuf0 + ccw * 4096, reinterpret_cast<const __half*>(fd + S5_FQ16),
-                          reinterpret_cast<const float*>(fd + S5_FHEAD + head_r * S5_FHEAD_BYTES), rb,
-                          s5_n(code), s5_nmem(code), scv, p.quant_rounded, p.sc,
-                          sc_row + int64_t(rb / VBLOCK) * p.sc_sv, p.sc_dt, ost + VBLOCK * v, lane);
-        }
-      } else {
-        s5_readout<MW>(sb + lay.ck + head_r * 16384, sb + lay.vr + head_r * 4096, res + lay.t8 + head_r * 8 * T8STR,
-                       reinterpret_cast<const uint16_t*>(res + lay.cb + head_r * 96), misc[0], sc, sc_base,
-                       rbase, s5_nmem(code), ost, lane);
-      }
+      s5_readout<MW>(sb + lay.ck + head_r * 16384, sb + lay.vr + head_r * 4096, res + lay.t8 + head_r * 8 * T8STR,
+                     reinterpret_cast<const uint16_t*>(res + lay.cb + head_r * 96), misc[0], sc, sc_base, rbase,
+                     s5_nmem(code), ost, lane);
       __syncwarp();
-      // this token's own slot (fused, no flush) as a rank-one term, K^-1/2, coalesced store
+      // this token's own slot (fused) as a rank-one term, K^-1/2, coalesced store
       constexpr int RPL = ROWS / 32;  // rows per lane: 4 or 2
       const int r0 = RPL * lane;
       float o[RPL];
 #pragma unroll
       for (int q = 0; q < RPL; ++q) o[q] = ost[r0 + q];
-      if (FUSED && !flush) {
+      if (FUSED) {
         const float cpos = misc[1];
         const uint16_t* vnew = reinterpret_cast<const uint16_t*>(res + lay.vnew + head_r * 256) + rbase;
 #pragma unroll
@@ -1388,19 +1457,6 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
 #pragma unroll
         for (int q = 0; q < RPL; ++q)
           store_scalar(p.out, obase + int64_t(rbase + r0 + q) * p.o_sv, p.o_dt, o[q] * KSCALE_H);
-      }
-    }
-    if (flush) {
-      // both warps' rows are in the tile: one tensor store of the unit's
-      // checkpoint tiles (same map and swizzle as the load); the stage is
-      // released once the copy engine has read it
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      asm volatile("bar.sync %0, %1;" ::"r"(4 + team), "n"(32 * S5_TEAM) : "memory");
-      if (mem == 0 && lane == 0 && *abort == 0) {
-        const S5Unit U = s5_unit(bid + i * grid, p.H, G, geo);
-        s5_tma_store4(&ck_map, sb + lay.ck, 0, 0, U.hv0, U.b);
-        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-        asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
       }
     }
     __syncwarp();
