@@ -176,12 +176,9 @@ def dist_init():
 def max_over_ranks(x: float, world: int) -> float:
     if world == 1:
         return x
-    import torch
-    import torch.distributed as dist
+    from gdnr.shard import max_over_ranks as reduce_max
 
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    return reduce_max(x)
 
 
 def barrier(world: int):
@@ -275,18 +272,23 @@ def run_reference(args, world, rank):
 
 # ---------------------------------------------------------------- GPU arm
 
-def build_stack(args, device):
+def build_stack(args, device, rank: int = 0, world: int = 1):
+    """This rank's shard of the job: sequences ShardPlan(B * world, world).local(rank)
+    of every layer, each rank with its own seeded inputs and state (weak scaling)."""
     import torch
 
     import gdnr
     from gdnr import inputs as gin
+    from gdnr.shard import ShardPlan
 
     B, L, NL = args.batch, args.ring, args.layers
+    shard = ShardPlan(B * world, world).local(rank)
+    assert len(shard) == B
     layers, step_inputs = [], []
     for li in range(NL):
         st = gdnr.ReplayState.allocate(B, H, HV, L, device=device, scale_dtype=torch.float32,
                                        gate_dtype=torch.float32)
-        raw = gin.raw_step_inputs(B, L, seed=args.seed * 1000 + li, device=device)
+        raw = gin.raw_step_inputs(B, L, seed=(args.seed * 1000 + li) * 4096 + shard.start, device=device)
         st.load_state(raw["state"])
         layers.append({"state": st, "a_log": raw["a_log"], "dt_bias": raw["dt_bias"],
                        "out": torch.empty(B, HV, KD, dtype=torch.bfloat16, device=device)})
@@ -343,7 +345,7 @@ def run_ours(args, world, rank, local):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu_line = cpu_baseline(args.seed, L)  # spawn pool; GPU untouched so far
 
-    layers, step_inputs, pos, err = build_stack(args, device)
+    layers, step_inputs, pos, err = build_stack(args, device, rank, world)
     stream = torch.cuda.Stream(device)
     torch.cuda.synchronize()
     # one graph per ring position: NL fused launches
