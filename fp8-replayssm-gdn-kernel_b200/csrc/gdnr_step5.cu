@@ -166,6 +166,20 @@ __device__ __forceinline__ void s5_tma5(void* dst, const CUtensorMap* map, int c
       : "memory");
 }
 
+// L2 prefetch of a tensor-map box (no shared memory, no completion signal).
+__device__ __forceinline__ void s5_prefetch4(const CUtensorMap* map, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+
+__device__ __forceinline__ void s5_prefetch5(const CUtensorMap* map, int c0, int c1, int c2, int c3, int c4) {
+  asm volatile("cp.async.bulk.prefetch.tensor.5d.L2.global.tile [%0, {%1, %2, %3, %4, %5}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+               : "memory");
+}
 
 // Bounded mbarrier wait that also gives up once another warp has recorded a
 // failure in *abort (then every later wait returns at once).
@@ -1323,6 +1337,20 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
 #pragma unroll
         for (int e = 0; e < HPU; ++e)
           s5_tma5(sb + lay.vr + e * 4096 + j * box_bytes, &vr_map, 0, 0, U.hv0 + e, j * geo.rb, U.b, &full[s]);
+      if (i == S5_NS - 1) {
+        // the units that wait for a free stage: their tiles and rings into L2 now,
+        // so that their stage loads later are served from L2
+        for (int u = S5_NS; u < nu; ++u) {
+          const int cu = table[u];
+          if (s5_skip(cu)) continue;
+          const S5Unit V = s5_unit(bid + u * grid, p.H, G, geo);
+          s5_prefetch4(&ck_map, 0, 0, V.hv0, V.b);
+          const int nr = (s5_nmem(cu) + geo.rb - 1) / geo.rb;
+          for (int j = 0; j < nr; ++j)
+#pragma unroll
+            for (int e = 0; e < HPU; ++e) s5_prefetch5(&vr_map, 0, 0, V.hv0 + e, j * geo.rb, V.b);
+        }
+      }
     }
     return;
   }
