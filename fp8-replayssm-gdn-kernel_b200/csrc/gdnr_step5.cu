@@ -43,6 +43,21 @@ constexpr int S5_NRW = 8;   // readout warps
 constexpr int S5_TEAM = S5_NRW / S5_NS;  // readout warps per stage
 constexpr int S5_THREADS = 32 * (1 + S5_NCW + S5_NRW);
 constexpr int S5_GSTR = 20;  // Gram scratch row (floats): 16 key columns + 3 query terms + pad
+// Readout structure.  The flush-capable variant with two-head units ("TC") reads
+// out through tensor memory with all readout warps on every unit (warp w: head
+// (w - 1 - S5_NCW) / 4, tensor-memory lanes 32 (w % 4) ..), so that a flush
+// unit's vblock tasks are shared by all of them.  Otherwise a team of S5_TEAM
+// warps per stage reads out a unit with register-fragment MMAs, four units at a
+// time -- faster when no unit flushes.
+template <int HPU, bool FLUSH>
+__host__ __device__ constexpr bool s5_tc() {
+  return HPU == 2 && FLUSH;
+}
+template <int HPU, bool FLUSH>
+__host__ __device__ constexpr int s5_rpu() {  // readout warps per unit
+  return s5_tc<HPU, FLUSH>() ? S5_NRW : S5_TEAM;
+}
+constexpr uint32_t S5_TMEM_COLS = 128;  // stages x heads x 16 accumulator columns (power of two >= 32)
 // A chain warp's result area: T terms of a non-flush unit (2 x 8 x T8STR), or the
 // flush data of a flush unit -- q split as f16 x 256 [2][128], then per head
 // (float offsets) a_t [16] at S5_FA, beta_t [16] at S5_FB, 1 / (operand scale) at
@@ -79,12 +94,12 @@ __host__ __device__ inline S5Geo s5_geo(int H, int HV, int L) {
 //        doubles as the chain's q-split / Gram scratch before T is written)
 //   [ost: 128 floats] x S5_NRW
 struct S5Layout {
-  uint32_t full, empty, kfull, cseq, rcnt, abort, vword, vdone, table;
+  uint32_t full, empty, kfull, cseq, rcnt, abort, vword, vdone, mmab, tmem, table;
   uint32_t stage0, stage_bytes, ck, vr;
   uint32_t kbuf0;
-  uint32_t res0, res_bytes, t8, cb, misc, vnew;
+  uint32_t res0, res_bytes, t8, cb, cf, misc, vnew;
   uint32_t qb, gram;  // chain scratch inside res (aliases t8)
-  uint32_t ost0;
+  uint32_t ost0, zb;
   uint32_t total;
 };
 
@@ -99,6 +114,8 @@ __host__ __device__ inline S5Layout s5_layout(const S5Geo& g, int max_units, boo
   s.abort = smem_take(o, 16);
   s.vword = smem_take(o, S5_NS * 4);
   s.vdone = smem_take(o, S5_NS * 4);
+  s.mmab = smem_take(o, S5_NS * 8);
+  s.tmem = smem_take(o, 16);
   s.table = smem_take(o, uint32_t(max_units) * 4u);
   o = (o + 1023u) & ~1023u;
   s.stage0 = o;
@@ -109,18 +126,23 @@ __host__ __device__ inline S5Layout s5_layout(const S5Geo& g, int max_units, boo
   s.kbuf0 = o;
   o += S5_NCW * 4096u;
   uint32_t r = 0;
+  // t8: the T terms (tensor-memory readout: the tensor-core B operand, 1 KB per
+  // head in K-major 8 x 16-byte core matrices; team readout: rows of T8STR), the
+  // chain's q-split / Gram scratch before that, or a flush unit's data
   s.t8 = smem_take(r, flush ? S5_T8_BYTES : 2u * 8u * uint32_t(T8STR));
   s.cb = smem_take(r, 2u * 3u * 16u * 2u);
+  s.cf = smem_take(r, 2u * 16u * 4u);
   s.misc = smem_take(r, 2u * 16u);
   s.vnew = smem_take(r, 2u * 128u * 2u);
   s.res_bytes = r;
   r = 0;
   s.qb = smem_take(r, 3u * 128u * 2u);
-  s.gram = smem_take(r, 16u * S5_GSTR * 4u);  // qb + gram fit in the t8 area
+  s.gram = smem_take(r, 16u * S5_GSTR * 4u);  // qb + gram fit in the t8 area (2048 bytes)
   s.res0 = o;
   o += S5_NCW * s.res_bytes;
   s.ost0 = o;
   o += S5_NRW * 512u;
+  s.zb = smem_take(o, 1024u);  // zeros: rows 8..15 of every T operand (N = 16)
   s.total = o;
   return s;
 }
@@ -148,6 +170,16 @@ __device__ __forceinline__ void s5_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
+// Relaxed arrive / add, for releases that only end reads whose values have
+// already been consumed (nothing to order behind them).
+__device__ __forceinline__ void s5_arrive_relaxed(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.relaxed.cta.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ void s5_add_relaxed(uint32_t* p, uint32_t v) {
+  asm volatile("red.relaxed.cta.shared::cta.add.u32 [%0], %1;" ::"r"(smem_addr(p)), "r"(v) : "memory");
+}
+
 __device__ __forceinline__ void s5_tma4(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
                                         uint64_t* bar) {
   asm volatile(
@@ -166,6 +198,20 @@ __device__ __forceinline__ void s5_tma5(void* dst, const CUtensorMap* map, int c
       : "memory");
 }
 
+// Non-blocking test of an mbarrier phase (try_wait may suspend the thread for a
+// while before it reports an incomplete phase).
+__device__ __forceinline__ bool s5_test_wait(const uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // L2 prefetch of a tensor-map box (no shared memory, no completion signal).
 __device__ __forceinline__ void s5_prefetch4(const CUtensorMap* map, int c0, int c1, int c2, int c3) {
   asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
@@ -181,11 +227,61 @@ __device__ __forceinline__ void s5_prefetch5(const CUtensorMap* map, int c0, int
                : "memory");
 }
 
+// ---------------------------------------------------------------- tensor memory (tcgen05)
+// Shared-memory matrix descriptors of tcgen05.mma (version 1):
+//   K-major with 128-byte swizzle -- the layout the checkpoint tiles land in (8-row
+//   atoms of 1 KB; leading offset unused (1), stride 1024 bytes), advanced along K
+//   by adding the byte offset to the start address;
+//   K-major 8 x 16-byte core matrices without swizzle -- lbo: next 16-byte K chunk,
+//   sbo: next group of 8 rows.
+__device__ __forceinline__ uint64_t s5_desc_sw128(uint32_t addr) {
+  return uint64_t((addr >> 4) & 0x3FFFu) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) | (uint64_t(1) << 46) |
+         (uint64_t(2) << 61);
+}
+
+__device__ __forceinline__ uint64_t s5_desc_cm(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  return uint64_t((addr >> 4) & 0x3FFFu) | (uint64_t((lbo >> 4) & 0x3FFFu) << 16) |
+         (uint64_t((sbo >> 4) & 0x3FFFu) << 32) | (uint64_t(1) << 46);
+}
+
+// Instruction descriptor: f32 accumulator, e4m3 A and B, both K-major, N = 16, M = 128.
+constexpr uint32_t S5_IDESC_E4M3_M128_N16 = (1u << 4) | ((16u >> 3) << 17) | ((128u >> 4) << 24);
+
+__device__ __forceinline__ void s5_umma_e4m3(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
+  const uint32_t z = 0u;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(S5_IDESC_E4M3_M128_N16), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z)
+      : "memory");
+}
+
+// arrives on `bar` once every tcgen05 operation this thread issued so far has completed
+__device__ __forceinline__ void s5_umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+
+// 16 consecutive 32-bit columns of this thread's tensor-memory lane (32x32b shape)
+__device__ __forceinline__ void s5_tmem_ld16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void s5_tc_before_sync() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void s5_tc_after_sync() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
 // Bounded mbarrier wait that also gives up once another warp has recorded a
 // failure in *abort (then every later wait returns at once).
 __device__ __forceinline__ bool s5_wait(uint64_t* bar, uint32_t parity, uint32_t* err, volatile int* abort) {
   const uint32_t a = smem_addr(bar);
-  if (mbar_try_wait(a, parity)) return true;
+  if (s5_test_wait(bar, parity)) return true;
   if (*abort) return false;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 1; it < WAIT_LIMIT_ITERS; ++it) {
@@ -288,9 +384,18 @@ __device__ __forceinline__ float s5_pow2_scale(float m) {
 }
 
 // Two heads' T (4 elements per lane each: 4 lane .. 4 lane + 3) -> five e4m3
-// terms per head in t8 rows 0..4 (rows 5..7 zero):
+// terms per head, rows 0..4 of an 8-row operand (rows 5..7 zero):
 // T sigma = sum_i term_i 16^-i, max |T sigma| in [128, 256); misc[0] = 1/sigma.
-template <int HPU>
+// Tensor-memory readout: head h's operand at t8 + 1024 h as K-major 8 x 16-byte
+// core matrices (byte k of row j at 128 (k / 16) + 16 j + k % 16); team readout:
+// row j of head h at t8 + T8STR (8 h + j).
+template <bool TC>
+__device__ __forceinline__ uint32_t s5_t8_off(int h, int j, int lane) {
+  if constexpr (TC) return uint32_t(h * 1024 + (lane >> 2) * 128 + j * 16 + (lane & 3) * 4);
+  return uint32_t((h * 8 + j) * T8STR + lane * 4);
+}
+
+template <int HPU, bool TC>
 __device__ __forceinline__ void s5_tsplit(const float (*Tq)[4], uint8_t* t8, float* misc, int lane) {
   float m[HPU];
 #pragma unroll
@@ -313,7 +418,7 @@ __device__ __forceinline__ void s5_tsplit(const float (*Tq)[4], uint8_t* t8, flo
     for (int h = 0; h < HPU; ++h) {
       const uint32_t p01 = e4m3x2_sat(x[h][0], x[h][1]);
       const uint32_t p23 = e4m3x2_sat(x[h][2], x[h][3]);
-      *reinterpret_cast<uint32_t*>(t8 + (h * 8 + j) * T8STR + lane * 4) = p01 | (p23 << 16);
+      *reinterpret_cast<uint32_t*>(t8 + s5_t8_off<TC>(h, j, lane)) = p01 | (p23 << 16);
       {
         const uint32_t h01 = e4m3x2_to_f16x2(p01), h23 = e4m3x2_to_f16x2(p23);
         const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&h01));
@@ -328,7 +433,7 @@ __device__ __forceinline__ void s5_tsplit(const float (*Tq)[4], uint8_t* t8, flo
 #pragma unroll
   for (int h = 0; h < HPU; ++h) {
 #pragma unroll
-    for (int j = 5; j < 8; ++j) *reinterpret_cast<uint32_t*>(t8 + (h * 8 + j) * T8STR + lane * 4) = 0u;
+    for (int j = 5; j < 8; ++j) *reinterpret_cast<uint32_t*>(t8 + s5_t8_off<TC>(h, j, lane)) = 0u;
     if (lane == 0) misc[h * 4] = 1.0f / sig[h];
   }
 }
@@ -766,7 +871,9 @@ __device__ __forceinline__ S5Append s5_chain(const StepParams& p, const S5Unit& 
   s5_solve(em, bsel, acc, cval, t);
   // ---- c -> [c_hi; c_mid; c_lo] bf16 over the slots read from memory (ring
   // columns of the readout); this token's own slot is a rank-one term
-  if (e < HPU) {
+  constexpr bool TC = s5_tc<HPU, FLUSH>();
+  if (TC && e < HPU) reinterpret_cast<float*>(res + lay.cf)[e * 16 + t] = t < nmem ? cval : 0.0f;
+  if (!TC && e < HPU) {
     uint16_t* cb = reinterpret_cast<uint16_t*>(res + lay.cb + e * 96);
     const float cc = t < nmem ? cval : 0.0f;
     const uint16_t chi = f_to_bf16(cc);
@@ -793,7 +900,7 @@ __device__ __forceinline__ S5Append s5_chain(const StepParams& p, const S5Unit& 
   }
   s5_tloop<HPU>(kbuf, wj, n, T, lane);
   __syncwarp();  // q-split / Gram scratch (aliases t8) is dead from here on
-  s5_tsplit<HPU>(T, res + lay.t8, misc, lane);
+  s5_tsplit<HPU, s5_tc<HPU, FLUSH>()>(T, res + lay.t8, misc, lane);
   return ap;
 }
 
@@ -1188,6 +1295,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
     step5_kernel(const __grid_constant__ StepParams p, const __grid_constant__ CUtensorMap ck_map,
                  const __grid_constant__ CUtensorMap kr_map, const __grid_constant__ CUtensorMap vr_map) {
   extern __shared__ __align__(1024) uint8_t smem[];
+  constexpr bool TC = s5_tc<HPU, FLUSH>();
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int L = p.L, G = p.HV / p.H;
   const S5Geo geo = s5_geo(p.H, p.HV, L);
@@ -1204,6 +1312,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
   volatile int* abort = reinterpret_cast<volatile int*>(smem + lay.abort);
   uint32_t* vword = reinterpret_cast<uint32_t*>(smem + lay.vword);  // flush task word per stage
   uint32_t* vdone = reinterpret_cast<uint32_t*>(smem + lay.vdone);  // flush tasks finished per stage
+  uint64_t* mmab = reinterpret_cast<uint64_t*>(smem + lay.mmab);    // tensor-core readout of a stage done
   int* table = reinterpret_cast<int*>(smem + lay.table);
   const bool aligned = (smem_addr(smem) & 1023u) == 0;  // swizzled TMA boxes need 1024-byte alignment
   const uint32_t box_bytes = uint32_t(geo.rb) * 256u;
@@ -1212,7 +1321,8 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
   if (tid == 0) {
     for (int s = 0; s < S5_NS; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], S5_TEAM);
+      mbar_init(&empty[s], s5_rpu<HPU, FLUSH>());
+      mbar_init(&mmab[s], 1);
     }
     for (int c = 0; c < S5_NCW; ++c) {
       mbar_init(&kfull[c], 1);
@@ -1229,6 +1339,16 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
   }
   __syncthreads();
   if (!aligned) return;
+  // two-head units: the first readout warp allocates the readout's tensor
+  // memory (released by the same warp at the end); the other readout warps see
+  // the address after barrier 1
+  if (TC && warp == 1 + S5_NCW) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(smem + lay.tmem)),
+                 "r"(S5_TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    s5_tc_before_sync();
+  }
 
   // Checkpoint tiles of the first stages: decode state, not output of the
   // preceding kernel (see GDNR_LAUNCH_PDL), so under programmatic dependent
@@ -1266,22 +1386,28 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
   } else if (warp == 0) {
     asm volatile("bar.sync 3, %0;" ::"n"(32 * (1 + S5_NCW)) : "memory");
   }
-  // readout warps: vblock scales of their first units (lane l: team unit
-  // l / (2 HPU), vblock l % (2 HPU) of the warp's rows), raw until used
-  constexpr int VBW = 2 * HPU;  // vblocks per readout warp and unit
-  constexpr int SC_UNITS = 32 / VBW;
+  // readout warps: vblock scales of their first units, raw until used.
+  // Two-head units (every readout warp reads every unit): lane l holds unit l's
+  // scale of the warp's head and vblock.  One-head units (teams): lane l holds
+  // team unit l / (2 HPU), vblock l % (2 HPU) of the warp's rows.
+  constexpr int VBW = 2 * HPU;  // vblocks per readout warp and unit (teams)
+  constexpr int SC_UNITS = TC ? 32 : 32 / VBW;
   uint32_t scl_raw = 0u;
   const int rw = warp - 1 - S5_NCW;
   const int team = rw / S5_TEAM, mem = rw % S5_TEAM;
-  const int head_r = HPU == 2 ? mem : 0;
+  const int head_r = TC ? (rw >> 2) : (HPU == 2 ? mem : 0);
   const int rbase = HPU == 2 ? 0 : 64 * mem;
   if (warp > S5_NCW) {
-    int i = team + S5_NS * (lane / VBW);
+    int i = TC ? lane : team + S5_NS * (lane / VBW);
     i = i < nu ? i : 0;
     const S5Unit U = s5_unit(bid + i * grid, p.H, G, geo);
-    scl_raw = s5_ld_raw(p.sc, int64_t(U.b) * p.sc_sb + int64_t(U.hv0 + head_r) * p.sc_sh +
-                                  int64_t(rbase / VBLOCK + lane % VBW) * p.sc_sv,
+    const int vb = TC ? (warp & 3) : rbase / VBLOCK + lane % VBW;
+    scl_raw = s5_ld_raw(p.sc, int64_t(U.b) * p.sc_sb + int64_t(U.hv0 + head_r) * p.sc_sh + int64_t(vb) * p.sc_sv,
                         p.sc_dt);
+    if (TC) {  // the zero rows of the tensor-core T operands
+      reinterpret_cast<uint32_t*>(smem + lay.zb)[tid - 32 * (1 + S5_NCW)] = 0u;
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
   }
   // ring positions of this CTA's units for the producer and the readout, read
   // by the threads from the top of the block down (the producer is busy
@@ -1320,11 +1446,11 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
   }
 
   if (warp == 0) {
-    // =================== producer ===================
+    // =================== producer / scheduler ===================
     if (lane != 0) return;
-    for (int i = 0; i < nu; ++i) {
+    // stage loads of unit i (stage i % S5_NS, free once its previous unit is read out)
+    auto load_unit = [&](int i) {
       const int s = i % S5_NS;
-      if (i >= S5_NS && !s5_wait(&empty[s], ((i / S5_NS) - 1) & 1, p.err, abort)) return;
       const int code = table[i];
       const S5Unit U = s5_unit(bid + i * grid, p.H, G, geo);
       uint8_t* sb = smem + lay.stage0 + s * lay.stage_bytes;
@@ -1351,6 +1477,64 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
             for (int e = 0; e < HPU; ++e) s5_prefetch5(&vr_map, 0, 0, V.hv0 + e, j * geo.rb, V.b);
         }
       }
+    };
+    if constexpr (TC) {
+      // Tensor-memory readout: this thread also issues each unit's tensor-core readout
+      // as soon as its stage has landed and its chain is done -- per head 4 x
+      // tcgen05.mma (M = 128 rows, N = 16: five T terms + zeros, K = 32) from the
+      // stage tile and the chain's T operand into the stage's 32 tensor-memory
+      // columns -- and commits it to mmab[s], one commit per unit (none issued
+      // for a flush or skipped unit: the commit then arrives at once), so that
+      // mmab[s] completes one phase per unit of the stage.  The columns are free:
+      // a stage's next load needs all readout warps to release it first.
+      // Nothing here blocks: loads and readouts progress as stages free up and
+      // chains finish.
+      s5_tc_after_sync();
+      const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + lay.tmem);
+      const uint32_t zb = smem_addr(smem + lay.zb);
+      int nl = 0, nm = 0;
+      const uint64_t t0 = globaltimer_ns();
+      for (uint32_t it = 0; (nl < nu || nm < nu) && it < WAIT_LIMIT_ITERS; ++it) {
+        bool progress = false;
+        while (nl < nu && (nl < S5_NS || s5_test_wait(&empty[nl % S5_NS], uint32_t(((nl / S5_NS) - 1) & 1)))) {
+          load_unit(nl++);
+          progress = true;
+        }
+        if (nm < nl && s5_test_wait(&full[nm % S5_NS], uint32_t((nm / S5_NS) & 1)) &&
+            s5_ld_acquire(&cseq[nm % S5_NCW]) >= uint32_t(nm / S5_NCW + 1)) {
+          const int su = nm % S5_NS, cu = table[nm];
+          if (!(FLUSH && s5_flush(cu)) && !s5_skip(cu)) {
+            const uint8_t* res = smem + lay.res0 + (nm % S5_NCW) * lay.res_bytes;
+            const uint8_t* sbu = smem + lay.stage0 + su * lay.stage_bytes;
+            s5_tc_after_sync();
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+              for (int ks = 0; ks < 4; ++ks) {
+                const uint32_t bs = smem_addr(res + lay.t8 + h * 1024) + 256 * ks;
+                s5_umma_e4m3(tmem + uint32_t(su * 32 + h * 16),
+                             s5_desc_sw128(smem_addr(sbu + lay.ck + h * 16384) + 32 * ks), s5_desc_cm(bs, 128, zb - bs),
+                             ks > 0 ? 1u : 0u);
+              }
+          }
+          s5_umma_commit(&mmab[su]);
+          ++nm;
+          progress = true;
+        }
+        if (!progress) {
+          if ((it & 63u) == 0 && (*abort || globaltimer_ns() - t0 > 4 * WAIT_LIMIT_NS)) break;
+          __nanosleep(32);
+        }
+      }
+      if (nl < nu || nm < nu) {
+        *abort = 1;
+        atomicOr(p.err, GDNR_DEVERR_WAIT_TIMEOUT);
+      }
+    } else {
+      for (int i = 0; i < nu; ++i) {
+        if (i >= S5_NS && !s5_wait(&empty[i % S5_NS], ((i / S5_NS) - 1) & 1, p.err, abort)) return;
+        load_unit(i);
+      }
     }
     return;
   }
@@ -1364,7 +1548,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       if (k > 0) {
         // the key ring and result block are free once both readout warps of
         // this warp's previous unit are done with them
-        ok = s5_warp_wait_count(&rcnt[cw], uint32_t(S5_TEAM * k), p.err, abort, lane);
+        ok = s5_warp_wait_count(&rcnt[cw], uint32_t(s5_rpu<HPU, FLUSH>() * k), p.err, abort, lane);
         // every lane's earlier generic accesses to kbuf, ordered before the
         // copy engine overwrites it
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -1382,6 +1566,8 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       const bool work = ok && !s5_skip(code);
       S5Append ap{};
       if (work) ap = s5_chain<FUSED, HPU, FLUSH>(p, U, code, in0, kbuf, res, lay, lane);
+      // the T operand is read by the tensor cores (async proxy)
+      if (TC) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0) s5_st_release(&cseq[cw], uint32_t(k + 1));
       if (work) s5_append<FUSED, HPU>(p, U, code, ap, lane);
@@ -1389,6 +1575,136 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
     return;
   }
 
+  if constexpr (TC) {
+    // =================== readout through tensor memory ===================
+    // Every unit is read out by all S5_NRW warps; warp w takes head head_r and the
+    // 32 rows 32 (w % 4) .. of it (the tensor-memory lanes a warp may access).  The
+    // scheduler thread (producer) has issued the unit's MMAs; per lane and row:
+    // the five terms' weighted sum, V^T c over the ring slots, this token's own
+    // slot, K^-1/2, one store.  Every unit's commit is waited for (also of flush
+    // and skipped units, which have none to read) so that the waits stay in step
+    // with mmab's phases.
+    s5_tc_after_sync();
+    const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + lay.tmem);
+    const int qd = warp & 3, row = 32 * qd + lane;
+    float* ost = reinterpret_cast<float*>(smem + lay.ost0 + rw * 512);
+    for (int i = 0; i < nu; ++i) {
+      const int s = i % S5_NS;
+      const uint32_t par = (i / S5_NS) & 1;
+      const int ccw = i % S5_NCW, k = i / S5_NCW;
+      const int code = table[i];
+      const float sc_pref = s5_cvt(__shfl_sync(0xffffffffu, scl_raw, i & 31), p.sc_dt);
+      bool ok = s5_warp_wait(&full[s], par, p.err, abort, lane);
+      ok = s5_warp_wait_count(&cseq[ccw], uint32_t(k + 1), p.err, abort, lane) && ok;
+      const bool flush = FLUSH && s5_flush(code);
+      uint8_t* sb = smem + lay.stage0 + s * lay.stage_bytes;
+      const S5Unit U = s5_unit(bid + i * grid, p.H, G, geo);
+      const bool mma = ok && !flush && !s5_skip(code);
+      const uint8_t* res = smem + lay.res0 + ccw * lay.res_bytes;
+      // V^T c over the slots read from memory (no tensor memory needed yet)
+      float ov = 0.0f;
+      if (mma) {
+        const float* cf = reinterpret_cast<const float*>(res + lay.cf) + head_r * 16;
+        const uint8_t* vr = sb + lay.vr + head_r * 4096;
+        const int nmem = s5_nmem(code);
+        float vt[16];
+#pragma unroll
+        for (int t = 0; t < 16; ++t)  // slots >= nmem hold stale or unloaded data
+          vt[t] = t < nmem ? bf16_to_f(*reinterpret_cast<const uint16_t*>(vr + s5_ring_off(t, row))) : 0.0f;
+#pragma unroll
+        for (int t = 0; t < 16; ++t) ov = fmaf(cf[t], vt[t], ov);
+        if constexpr (FUSED) {
+          const float* misc = reinterpret_cast<const float*>(res + lay.misc) + head_r * 4;
+          ov = fmaf(misc[1], bf16_to_f(reinterpret_cast<const uint16_t*>(res + lay.vnew + head_r * 256)[row]), ov);
+        }
+      }
+      const bool mok = s5_warp_wait(&mmab[s], par, p.err, abort, lane);
+      if (flush) {
+        // The unit's 8 vblock tasks among the readout warps, then one tensor-map
+        // store.  The first warp here publishes the tasks: its stage has landed,
+        // so the stage's previous unit and its tasks are finished.  It parks the
+        // task word in a resetting state (no claim succeeds) while it clears the
+        // done count; the other warps wait out that state.
+        constexpr int NT = 4 * HPU;
+        if (lane == 0) {
+          const uint32_t parked = (uint32_t(i) << 8) | 0xffu;
+          uint32_t w = s5_ld_acquire(&vword[s]);
+          if ((w >> 8) != uint32_t(i) && atomicCAS(&vword[s], w, parked) == w) {
+            vdone[s] = 0u;
+            __threadfence_block();
+            atomicExch(&vword[s], uint32_t(i) << 8);
+          } else {
+            const uint64_t t0 = globaltimer_ns();
+            for (uint32_t it = 0; it < WAIT_LIMIT_ITERS; ++it) {
+              w = s5_ld_acquire(&vword[s]);
+              if ((w >> 8) == uint32_t(i) && w != parked) break;
+              if ((it & 63u) == 0 && (*abort || globaltimer_ns() - t0 > WAIT_LIMIT_NS)) break;
+            }
+          }
+        }
+        __syncwarp();
+        if (ok) {
+          for (;;) {
+            const int t = s5_claim(&vword[s], i, NT, lane);
+            if (t < 0) break;
+            s5_flush_task<FUSED, HPU>(p, smem, lay, U, s, ccw, code, t, ost, lane);
+            if (lane == 0) s5_add_release(&vdone[s], 1u);
+          }
+        }
+        // the first readout warp stores the unit once every task is done; the
+        // others release the stage now (it is reloaded only after all have)
+        if (rw == 0) {
+          s5_warp_wait_count(&vdone[s], uint32_t(NT), p.err, abort, lane);
+          if (lane == 0 && *abort == 0) {
+            s5_tma_store4(&ck_map, sb + lay.ck, 0, 0, U.hv0, U.b);
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+            asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+          }
+        }
+      } else if (mma) {
+        float sc = sc_pref;
+        if (i >= 32)
+          sc = load_scalar(p.sc, int64_t(U.b) * p.sc_sb + int64_t(U.hv0 + head_r) * p.sc_sh + int64_t(qd) * p.sc_sv,
+                           p.sc_dt);
+        const float* misc = reinterpret_cast<const float*>(res + lay.misc) + head_r * 4;
+        s5_tc_after_sync();
+        uint32_t d[16];
+        s5_tmem_ld16(tmem + (uint32_t(32 * qd) << 16) + uint32_t(s * 32 + head_r * 16), d);
+        float ot = __uint_as_float(d[4]) * (1.0f / 16.0f);
+        ot = (ot + __uint_as_float(d[3])) * (1.0f / 16.0f);
+        ot = (ot + __uint_as_float(d[2])) * (1.0f / 16.0f);
+        ot = (ot + __uint_as_float(d[1])) * (1.0f / 16.0f);
+        ot = ot + __uint_as_float(d[0]);
+        const float o = mok ? fmaf(ot, misc[0] * sc, ov) : 0.0f;
+        // release the stage and the chain's results before the output store: every
+        // read of them has been consumed, so relaxed releases suffice
+        s5_tc_before_sync();
+        __syncwarp();
+        if (lane == 0) {
+          s5_arrive_relaxed(&empty[s]);
+          s5_add_relaxed(&rcnt[ccw], 1u);
+        }
+        store_scalar(p.out, int64_t(U.b) * p.o_sb + int64_t(U.hv0 + head_r) * p.o_sh + int64_t(row) * p.o_sv, p.o_dt,
+                     o * KSCALE_H);
+        continue;
+      }
+      s5_tc_before_sync();
+      __syncwarp();
+      if (lane == 0) {
+        s5_arrive(&empty[s]);
+        s5_add_release(&rcnt[ccw], 1u);
+      }
+    }
+    // the last commit covers every MMA this CTA issued: complete before the
+    // tensor memory is released
+    if (rw == 0 && nu > 0) s5_warp_wait(&mmab[(nu - 1) % S5_NS], uint32_t(((nu - 1) / S5_NS) & 1), p.err, abort, lane);
+    s5_tc_before_sync();
+    asm volatile("bar.sync 1, %0;" ::"n"(32 * S5_NRW) : "memory");
+    if (rw == 0) {
+      s5_tc_after_sync();
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(S5_TMEM_COLS) : "memory");
+    }
+  } else {
   // =================== readout teams ===================
   // Team j (2 warps) reads out the units of stage j in order; with two heads
   // per unit each warp takes one head (8 m-tiles), with one head each warp
@@ -1492,6 +1808,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       s5_arrive(&empty[s]);
       s5_add_release(&rcnt[ccw], 1u);
     }
+  }
   }
   // the checkpoint stores are complete before the kernel ends
   if (FLUSH && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
