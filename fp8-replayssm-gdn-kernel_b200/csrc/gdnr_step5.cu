@@ -94,7 +94,7 @@ __host__ __device__ inline S5Geo s5_geo(int H, int HV, int L) {
 //        doubles as the chain's q-split / Gram scratch before T is written)
 //   [ost: 128 floats] x S5_NRW
 struct S5Layout {
-  uint32_t full, empty, kfull, cseq, rcnt, abort, vword, vdone, mmab, tmem, table;
+  uint32_t full, empty, kfull, cbar, rbar, abort, vword, vdone, mmab, tmem, table;
   uint32_t stage0, stage_bytes, ck, vr;
   uint32_t kbuf0;
   uint32_t res0, res_bytes, t8, cb, cf, misc, vnew;
@@ -109,8 +109,8 @@ __host__ __device__ inline S5Layout s5_layout(const S5Geo& g, int max_units, boo
   s.full = smem_take(o, S5_NS * 8);
   s.empty = smem_take(o, S5_NS * 8);
   s.kfull = smem_take(o, S5_NCW * 8);
-  s.cseq = smem_take(o, S5_NCW * 4);
-  s.rcnt = smem_take(o, S5_NCW * 4);
+  s.cbar = smem_take(o, S5_NCW * 8);
+  s.rbar = smem_take(o, S5_NCW * 8);
   s.abort = smem_take(o, 16);
   s.vword = smem_take(o, S5_NS * 4);
   s.vdone = smem_take(o, S5_NS * 4);
@@ -279,9 +279,10 @@ __device__ __forceinline__ void s5_tc_after_sync() { asm volatile("tcgen05.fence
 
 // Bounded mbarrier wait that also gives up once another warp has recorded a
 // failure in *abort (then every later wait returns at once).
-__device__ __forceinline__ bool s5_wait(uint64_t* bar, uint32_t parity, uint32_t* err, volatile int* abort) {
+// (The waiting part is one out-of-line copy: every inlined copy of it would
+// cost instruction-cache space next to the hot code.)
+__device__ __noinline__ bool s5_wait_slow(uint64_t* bar, uint32_t parity, uint32_t* err, volatile int* abort) {
   const uint32_t a = smem_addr(bar);
-  if (s5_test_wait(bar, parity)) return true;
   if (*abort) return false;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 1; it < WAIT_LIMIT_ITERS; ++it) {
@@ -294,6 +295,11 @@ __device__ __forceinline__ bool s5_wait(uint64_t* bar, uint32_t parity, uint32_t
   *abort = 1;
   atomicOr(err, GDNR_DEVERR_WAIT_TIMEOUT);
   return false;
+}
+
+__device__ __forceinline__ bool s5_wait(uint64_t* bar, uint32_t parity, uint32_t* err, volatile int* abort) {
+  if (s5_test_wait(bar, parity)) return true;
+  return s5_wait_slow(bar, parity, err, abort);
 }
 
 __device__ __forceinline__ bool s5_warp_wait(uint64_t* bar, uint32_t parity, uint32_t* err, volatile int* abort,
@@ -1307,8 +1313,10 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + lay.full);
   uint64_t* empty = reinterpret_cast<uint64_t*>(smem + lay.empty);
   uint64_t* kfull = reinterpret_cast<uint64_t*>(smem + lay.kfull);
-  uint32_t* cseq = reinterpret_cast<uint32_t*>(smem + lay.cseq);  // chains finished, per chain warp
-  uint32_t* rcnt = reinterpret_cast<uint32_t*>(smem + lay.rcnt);  // readout parts finished, per chain warp
+  // per chain warp, one phase per unit: its chain is finished (cbar), its
+  // readout warps are finished with it (rbar)
+  uint64_t* cbar = reinterpret_cast<uint64_t*>(smem + lay.cbar);
+  uint64_t* rbar = reinterpret_cast<uint64_t*>(smem + lay.rbar);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + lay.abort);
   uint32_t* vword = reinterpret_cast<uint32_t*>(smem + lay.vword);  // flush task word per stage
   uint32_t* vdone = reinterpret_cast<uint32_t*>(smem + lay.vdone);  // flush tasks finished per stage
@@ -1318,6 +1326,10 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
   const uint32_t box_bytes = uint32_t(geo.rb) * 256u;
   const uint32_t ck_bytes = uint32_t(HPU) * 16384u;
 
+  if (warp == 1 && lane < 3) {  // the tensor maps' descriptors, ahead of their first copies
+    const CUtensorMap* m = lane == 0 ? &kr_map : (lane == 1 ? &ck_map : &vr_map);
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
+  }
   if (tid == 0) {
     for (int s = 0; s < S5_NS; ++s) {
       mbar_init(&full[s], 1);
@@ -1326,8 +1338,8 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
     }
     for (int c = 0; c < S5_NCW; ++c) {
       mbar_init(&kfull[c], 1);
-      cseq[c] = 0;
-      rcnt[c] = 0;
+      mbar_init(&cbar[c], 1);
+      mbar_init(&rbar[c], s5_rpu<HPU, FLUSH>());
     }
     for (int st = 0; st < S5_NS; ++st) {
       vword[st] = 0xffffffffu;
@@ -1501,7 +1513,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
           progress = true;
         }
         if (nm < nl && s5_test_wait(&full[nm % S5_NS], uint32_t((nm / S5_NS) & 1)) &&
-            s5_ld_acquire(&cseq[nm % S5_NCW]) >= uint32_t(nm / S5_NCW + 1)) {
+            s5_test_wait(&cbar[nm % S5_NCW], uint32_t((nm / S5_NCW) & 1))) {
           const int su = nm % S5_NS, cu = table[nm];
           if (!(FLUSH && s5_flush(cu)) && !s5_skip(cu)) {
             const uint8_t* res = smem + lay.res0 + (nm % S5_NCW) * lay.res_bytes;
@@ -1548,7 +1560,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       if (k > 0) {
         // the key ring and result block are free once both readout warps of
         // this warp's previous unit are done with them
-        ok = s5_warp_wait_count(&rcnt[cw], uint32_t(s5_rpu<HPU, FLUSH>() * k), p.err, abort, lane);
+        ok = s5_warp_wait(&rbar[cw], uint32_t((k - 1) & 1), p.err, abort, lane);
         // every lane's earlier generic accesses to kbuf, ordered before the
         // copy engine overwrites it
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -1569,7 +1581,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       // the T operand is read by the tensor cores (async proxy)
       if (TC) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
-      if (lane == 0) s5_st_release(&cseq[cw], uint32_t(k + 1));
+      if (lane == 0) s5_arrive(&cbar[cw]);
       if (work) s5_append<FUSED, HPU>(p, U, code, ap, lane);
     }
     return;
@@ -1595,7 +1607,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       const int code = table[i];
       const float sc_pref = s5_cvt(__shfl_sync(0xffffffffu, scl_raw, i & 31), p.sc_dt);
       bool ok = s5_warp_wait(&full[s], par, p.err, abort, lane);
-      ok = s5_warp_wait_count(&cseq[ccw], uint32_t(k + 1), p.err, abort, lane) && ok;
+      ok = s5_warp_wait(&cbar[ccw], uint32_t(k & 1), p.err, abort, lane) && ok;
       const bool flush = FLUSH && s5_flush(code);
       uint8_t* sb = smem + lay.stage0 + s * lay.stage_bytes;
       const S5Unit U = s5_unit(bid + i * grid, p.H, G, geo);
@@ -1682,7 +1694,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
         __syncwarp();
         if (lane == 0) {
           s5_arrive_relaxed(&empty[s]);
-          s5_add_relaxed(&rcnt[ccw], 1u);
+          s5_arrive_relaxed(&rbar[ccw]);
         }
         store_scalar(p.out, int64_t(U.b) * p.o_sb + int64_t(U.hv0 + head_r) * p.o_sh + int64_t(row) * p.o_sv, p.o_dt,
                      o * KSCALE_H);
@@ -1692,7 +1704,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       __syncwarp();
       if (lane == 0) {
         s5_arrive(&empty[s]);
-        s5_add_release(&rcnt[ccw], 1u);
+        s5_arrive(&rbar[ccw]);
       }
     }
     // the last commit covers every MMA this CTA issued: complete before the
@@ -1732,7 +1744,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       }
     }
     bool ok = s5_warp_wait(&full[s], (i / S5_NS) & 1, p.err, abort, lane);
-    ok = s5_warp_wait_count(&cseq[ccw], uint32_t(k + 1), p.err, abort, lane) && ok;
+    ok = s5_warp_wait(&cbar[ccw], uint32_t(k & 1), p.err, abort, lane) && ok;
     const bool flush = FLUSH && s5_flush(code);
     uint8_t* sb = smem + lay.stage0 + s * lay.stage_bytes;
     if (flush) {
@@ -1806,7 +1818,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
     __syncwarp();
     if (lane == 0) {
       s5_arrive(&empty[s]);
-      s5_add_release(&rcnt[ccw], 1u);
+      s5_arrive(&rbar[ccw]);
     }
   }
   }
