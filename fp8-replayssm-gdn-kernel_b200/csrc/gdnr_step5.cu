@@ -57,7 +57,12 @@ template <int HPU, bool FLUSH>
 __host__ __device__ constexpr int s5_rpu() {  // readout warps per unit
   return s5_tc<HPU, FLUSH>() ? S5_NRW : S5_TEAM;
 }
-constexpr uint32_t S5_TMEM_COLS = 128;  // stages x heads x 16 accumulator columns (power of two >= 32)
+// Tensor memory of the tensor-memory readout: columns 0..127 the readout's
+// accumulators (stages x heads x 16); from S5_TM_STASH, 128 columns per readout
+// warp of a lane quarter, where a flush task parks its rebuilt state between
+// the amax and the re-quantisation pass.
+constexpr uint32_t S5_TM_STASH = 128;
+constexpr uint32_t S5_TMEM_COLS = 512;  // power of two >= S5_TM_STASH + 2 x 128
 // A chain warp's result area: T terms of a non-flush unit (2 x 8 x T8STR), or the
 // flush data of a flush unit -- q split as f16 x 256 [2][128], then per head
 // (float offsets) a_t [16] at S5_FA, beta_t [16] at S5_FB, 1 / (operand scale) at
@@ -272,6 +277,16 @@ __device__ __forceinline__ void s5_tmem_ld16(uint32_t taddr, uint32_t* r) {
       : "r"(taddr)
       : "memory");
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// 16 consecutive 32-bit columns of this thread's lane, stored (32x32b shape)
+__device__ __forceinline__ void s5_tmem_st16(uint32_t taddr, const float* x) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};" ::"r"(taddr),
+      "f"(x[0]), "f"(x[1]), "f"(x[2]), "f"(x[3]), "f"(x[4]), "f"(x[5]), "f"(x[6]), "f"(x[7]), "f"(x[8]), "f"(x[9]),
+      "f"(x[10]), "f"(x[11]), "f"(x[12]), "f"(x[13]), "f"(x[14]), "f"(x[15])
+      : "memory");
 }
 
 __device__ __forceinline__ void s5_tc_before_sync() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -993,10 +1008,14 @@ __device__ __forceinline__ void s5_readout(const uint8_t* ck_s, const uint8_t* v
 // tile: the head's e4m3 tile (swizzled); vr: its value ring; vnew: this token's
 // value row (slot nmem) or null; kf: the unit's key ring as f16 x 256; fq: q split
 // [2][128] f16 x 256; fh: the head's flush block.  o(row rb + i) (before K^-1/2) -> ost[i].
+// STASH: the tensor memory at `stash` (this warp's lane quarter, 128 columns)
+// holds the rebuilt state between the two passes; otherwise the second pass
+// rebuilds it again.
+template <bool STASH>
 __device__ __forceinline__ void s5_flush_vblock(uint8_t* tile, const uint8_t* vr, const uint16_t* vnew,
                                                 const uint8_t* kf, const __half* fq, const float* fh, int rb,
                                                 int n, int nmem, float sc, int quant_rounded, void* scale_ptr,
-                                                int64_t sc_index, int sc_dt, float* ost, int lane) {
+                                                int64_t sc_index, int sc_dt, float* ost, uint32_t stash, int lane) {
   const int g8 = lane >> 2, t4 = lane & 3;
   const float* av = fh + S5_FA;
   const float* bv = fh + S5_FB;
@@ -1165,7 +1184,9 @@ __device__ __forceinline__ void s5_flush_vblock(uint8_t* tile, const uint8_t* vr
     sl_cols(np, x);
 #pragma unroll
     for (int i = 0; i < 16; ++i) amax = fmax_nan(amax, fabsf(x[i]));
+    if constexpr (STASH) s5_tmem_st16(stash + 16u * uint32_t(np), x);
   }
+  if constexpr (STASH) asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
   amax = warp_max_nan(amax);
   const VScale vs = vblock_scale(amax, quant_rounded);
   const float rcp = __fdiv_rn(1.0f, vs.divisor);
@@ -1175,7 +1196,14 @@ __device__ __forceinline__ void s5_flush_vblock(uint8_t* tile, const uint8_t* vr
 #pragma unroll 1
   for (int np = 0; np < 8; ++np) {
     float x[16];
-    sl_cols(np, x);
+    if constexpr (STASH) {
+      uint32_t xr[16];
+      s5_tmem_ld16(stash + 16u * uint32_t(np), xr);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) x[i] = __uint_as_float(xr[i]);
+    } else {
+      sl_cols(np, x);
+    }
     uint32_t cq[8];
     quant_pairs_warp<8>(x, cq, vs.divisor, rcp, qkd, qok);
     uint8_t* cp = trow + 16 * (np ^ g8);
@@ -1277,18 +1305,19 @@ __device__ __forceinline__ int s5_claim(uint32_t* vword, int unit, int ntask, in
 template <bool FUSED, int HPU>
 __device__ __forceinline__ void s5_flush_task(const StepParams& p, uint8_t* smem, const S5Layout& lay,
                                               const S5Unit& U, int s, int ccw, int code, int task, float* stage,
-                                              int lane) {
+                                              uint32_t stash, int lane) {
   const int head = HPU == 2 ? task >> 2 : 0, v = task & 3;
   uint8_t* sb = smem + lay.stage0 + s * lay.stage_bytes;
   const uint8_t* res = smem + lay.res0 + ccw * lay.res_bytes;
   const uint8_t* fd = res + lay.t8;
   const float* fh = reinterpret_cast<const float*>(fd + S5_FHEAD + head * S5_FHEAD_BYTES);
   const int hv = U.hv0 + head;
-  s5_flush_vblock(sb + lay.ck + head * 16384, sb + lay.vr + head * 4096,
+  s5_flush_vblock<s5_tc<HPU, true>()>(sb + lay.ck + head * 16384, sb + lay.vr + head * 4096,
                   FUSED ? reinterpret_cast<const uint16_t*>(res + lay.vnew + head * 256) : nullptr,
                   smem + lay.kbuf0 + ccw * 4096, reinterpret_cast<const __half*>(fd + S5_FQ16), fh, VBLOCK * v,
                   s5_n(code), s5_nmem(code), fh[S5_FSC + v], p.quant_rounded, p.sc,
-                  int64_t(U.b) * p.sc_sb + int64_t(hv) * p.sc_sh + int64_t(v) * p.sc_sv, p.sc_dt, stage, lane);
+                  int64_t(U.b) * p.sc_sb + int64_t(hv) * p.sc_sh + int64_t(v) * p.sc_sv, p.sc_dt, stage, stash,
+                  lane);
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   __syncwarp();
   store_scalar(p.out, int64_t(U.b) * p.o_sb + int64_t(hv) * p.o_sh + int64_t(VBLOCK * v + lane) * p.o_sv, p.o_dt,
@@ -1599,6 +1628,8 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
     s5_tc_after_sync();
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + lay.tmem);
     const int qd = warp & 3, row = 32 * qd + lane;
+    // this warp's flush stash: its lane quarter, 128 columns (two warps share a quarter)
+    const uint32_t stash = tmem + (uint32_t(32 * qd) << 16) + S5_TM_STASH + 128u * uint32_t(rw >> 2);
     float* ost = reinterpret_cast<float*>(smem + lay.ost0 + rw * 512);
     for (int i = 0; i < nu; ++i) {
       const int s = i % S5_NS;
@@ -1659,7 +1690,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
           for (;;) {
             const int t = s5_claim(&vword[s], i, NT, lane);
             if (t < 0) break;
-            s5_flush_task<FUSED, HPU>(p, smem, lay, U, s, ccw, code, t, ost, lane);
+            s5_flush_task<FUSED, HPU>(p, smem, lay, U, s, ccw, code, t, ost, stash, lane);
             if (lane == 0) s5_add_release(&vdone[s], 1u);
           }
         }
@@ -1762,7 +1793,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
         for (;;) {
           const int t = s5_claim(&vword[s], i, NT, lane);
           if (t < 0) break;
-          s5_flush_task<FUSED, HPU>(p, smem, lay, U, s, ccw, code, t, ost, lane);
+          s5_flush_task<FUSED, HPU>(p, smem, lay, U, s, ccw, code, t, ost, 0u, lane);
           if (lane == 0) s5_add_release(&vdone[s], 1u);
         }
       }
