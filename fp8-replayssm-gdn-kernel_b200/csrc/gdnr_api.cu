@@ -368,6 +368,96 @@ int gdnr_fused_step(const gdnr_step_args* a, void* stream) {
   return cuda_status(launch_step(p, true, f32ck, group, static_cast<cudaStream_t>(stream)), "gdnr_fused_step launch");
 }
 
+// The serving engine's decode call over a state-slot pool (see include/gdnr.h):
+// gdnr_fused_step with every state tensor indexed through state_indices.
+int gdnr_packed_decode(const gdnr_packed_decode_args* a, void* stream) {
+  if (!a) return set_error(GDNR_ERR_ARG, "args: null pointer");
+  StepParams p;
+  memset(&p, 0, sizeof(p));
+  bool f32ck = false;
+  int group = 0;
+  CHECK(validate_state(a->checkpoint, a->scale, a->k_ring, a->v_ring, a->g_ring, a->beta_ring, p, f32ck, group));
+  if (f32ck) return set_error(GDNR_ERR_UNSUPPORTED, "packed decode: E4M3 checkpoints only");
+  const int32_t slots = p.B;
+  CHECK(check_tensor(a->mixed_qkv, "mixed_qkv", 2, DT_ACT, 2, nullptr));
+  const int64_t B = a->mixed_qkv.shape[0];
+  if (B > 65535) return set_error(GDNR_ERR_UNSUPPORTED, "batch above 65535");
+  p.B = int32_t(B);
+  p.S = slots;
+  const int64_t width = 2 * int64_t(p.H) * 128 + int64_t(p.HV) * 128;
+  const int64_t want_m[2] = {B, width};
+  CHECK(check_tensor(a->mixed_qkv, "mixed_qkv", 2, DT_ACT, 2, want_m));
+  CHECK(check_inner_contiguous(a->mixed_qkv, "mixed_qkv"));
+  const int64_t want_ab[2] = {B, p.HV};
+  CHECK(check_tensor(a->a, "a", 2, DT_GATE, 3, want_ab));
+  CHECK(check_tensor(a->b, "b", 2, DT_GATE, 3, want_ab));
+  const int64_t want_hv[1] = {p.HV};
+  CHECK(check_tensor(a->a_log, "A_log", 1, DT_F32, 1, want_hv));
+  CHECK(check_tensor(a->dt_bias, "dt_bias", 1, DT_F32, 1, want_hv));
+  const int64_t want_b[1] = {B};
+  CHECK(check_tensor(a->state_indices, "state_indices", 1, DT_I32, 1, want_b));
+  const int64_t want_s[1] = {slots};
+  CHECK(check_tensor(a->pos, "pos", 1, DT_I32, 1, want_s));
+  if (present(a->pos_out)) {
+    CHECK(check_tensor(a->pos_out, "pos_out", 1, DT_I32, 1, want_s));
+    if (overlaps(a->pos, a->pos_out)) return set_error(GDNR_ERR_ALIAS, "pos_out must not overlap pos");
+    p.pos_out = static_cast<int32_t*>(a->pos_out.data);
+    p.po_s = a->pos_out.stride[0];
+  }
+  // out [B,1,HV,V] (the production layout) or [B,HV,V]
+  gdnr_tensor out = a->out;
+  if (out.ndim == 4) {
+    if (out.shape[1] != 1) return set_error(GDNR_ERR_ARG, "out: dim 1 of a rank-4 out must be 1");
+    out.ndim = 3;
+    out.shape[1] = out.shape[2];
+    out.shape[2] = out.shape[3];
+    out.stride[1] = out.stride[2];
+    out.stride[2] = out.stride[3];
+    out.shape[3] = 0;
+    out.stride[3] = 0;
+  }
+  CHECK(validate_out(out, p));
+  if (a->use_qk_l2norm != 1)
+    return set_error(GDNR_ERR_UNSUPPORTED, "use_qk_l2norm_in_kernel must be true (the kernel always normalises q, k)");
+  const float kscale = 0.08838834764831845f;  // 128^-1/2
+  if (!(fabsf(a->qk_scale - kscale) <= 1e-6f * kscale))
+    return set_error(GDNR_ERR_UNSUPPORTED, "scale must be head_k_dim^-1/2 = %.9g (got %.9g)", double(kscale),
+                     double(a->qk_scale));
+  if (a->quant_divisor != 0 && a->quant_divisor != 1)
+    return set_error(GDNR_ERR_ARG, "quant_divisor must be 0 or 1");
+  p.mixed = a->mixed_qkv.data;
+  p.mx_sb = a->mixed_qkv.stride[0];
+  p.mx_dt = a->mixed_qkv.dtype;
+  p.a = a->a.data;
+  p.a_sb = a->a.stride[0];
+  p.a_sh = a->a.stride[1];
+  p.a_dt = a->a.dtype;
+  p.bb = a->b.data;
+  p.b_sb = a->b.stride[0];
+  p.b_sh = a->b.stride[1];
+  p.b_dt = a->b.dtype;
+  p.a_log = static_cast<const float*>(a->a_log.data);
+  p.al_s = a->a_log.stride[0];
+  p.dt_bias = static_cast<const float*>(a->dt_bias.data);
+  p.db_s = a->dt_bias.stride[0];
+  p.pos = static_cast<const int32_t*>(a->pos.data);
+  p.pos_s = a->pos.stride[0];
+  p.sidx = static_cast<const int32_t*>(a->state_indices.data);
+  p.si_s = a->state_indices.stride[0];
+  p.rows = 128;
+  p.quant_rounded = a->quant_divisor;
+  p.err = a->error_flag ? a->error_flag : default_error_word();
+  if (!p.err) return set_error(GDNR_ERR_CUDA, "no device error word available");
+  CHECK(check_launch_opts(a->flush_hint, a->launch_flags, p));
+  if (!step5_eligible(p, true, false))
+    return set_error(GDNR_ERR_UNSUPPORTED,
+                     "packed decode: layout outside the persistent step kernel (16-byte aligned rows and rings, "
+                     "HV/H = 1 or even, 4 <= L <= 16)");
+  if (p.B == 0) return GDNR_OK;
+  return cuda_status(launch_step(p, true, false, group, static_cast<cudaStream_t>(stream)),
+                     "gdnr_packed_decode launch");
+}
+
 static int validate_codec(const gdnr_codec_args* a, CodecParams& p) {
   if (!a) return set_error(GDNR_ERR_ARG, "args: null pointer");
   CHECK(check_tensor(a->state, "state", 4, DT_F32, 1, nullptr));

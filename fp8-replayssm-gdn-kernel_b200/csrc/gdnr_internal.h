@@ -68,6 +68,11 @@ struct StepParams {
   uint32_t* err;
   int32_t flush_hint;   // GDNR_FLUSH_*
   int32_t pdl;          // launch with programmatic stream serialization
+  // packed decode: batch row b uses state slot sidx[b * si_s] of every state
+  // tensor (S slots; slot 0 is the null slot); null = the state is indexed by b
+  const int32_t* sidx;
+  int64_t si_s;
+  int32_t S;
 };
 
 struct SmemLayout {

@@ -415,6 +415,7 @@ static cudaError_t launch_g(const StepParams& p, int group, cudaStream_t stream)
 
 cudaError_t launch_step(const StepParams& p, bool fused, bool f32ck, int group, cudaStream_t stream) {
   if (step5_eligible(p, fused, f32ck)) return launch_step5(p, fused, p.pdl != 0, stream);
+  if (p.sidx) return cudaErrorNotSupported;  // slot indirection: the persistent kernel only
   if (!f32ck && p.L <= STEP2_MAX_L) return launch_step2(p, fused, stream);
   if (fused) return f32ck ? launch_g<true, true>(p, group, stream) : launch_g<true, false>(p, group, stream);
   return f32ck ? launch_g<false, true>(p, group, stream) : launch_g<false, false>(p, group, stream);

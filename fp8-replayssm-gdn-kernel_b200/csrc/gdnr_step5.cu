@@ -373,18 +373,27 @@ __device__ __forceinline__ bool s5_skip(int code) { return (code >> 16) & 1; }
 // bit 17: the unit flushes here (rebuild + re-quantisation in this kernel)
 __device__ __forceinline__ bool s5_flush(int code) { return (code >> 17) & 1; }
 
+// A unit: batch row b, key head h, pair pp of its value heads (first value head
+// hv0); s: the row's state slot -- b, or under packed decode state_indices[b],
+// with -1 for the null slot 0 and -2 for an index outside [0, S) (both skipped).
 struct S5Unit {
-  int b, h, pp, hv0;
+  int b, h, pp, hv0, s;
 };
 
-__device__ __forceinline__ S5Unit s5_unit(int u, int H, int G, const S5Geo& g) {
+template <bool SIDX>
+__device__ __forceinline__ S5Unit s5_unit(int u, const StepParams& p, int G, const S5Geo& g) {
   S5Unit x;
-  const int per_b = H * g.upk;
+  const int per_b = p.H * g.upk;
   x.b = u / per_b;
   const int r = u - x.b * per_b;
   x.h = r / g.upk;
   x.pp = r - x.h * g.upk;
   x.hv0 = x.h * G + x.pp * g.hpu;
+  x.s = x.b;
+  if constexpr (SIDX) {
+    const int v = __ldg(p.sidx + int64_t(x.b) * p.si_s);
+    x.s = v == 0 ? -1 : ((v < 0 || v >= p.S) ? -2 : v);
+  }
   return x;
 }
 
@@ -515,9 +524,9 @@ __device__ __forceinline__ S5In s5_fetch(const StepParams& p, const S5Unit& U, i
   const int e = lane >> 4, t = lane & 15;
   const int hv = U.hv0 + (e < HPU ? e : 0);
   const int ts = t < p.L ? t : p.L - 1;
-  in.g = s5_ld_raw(p.gr, int64_t(U.b) * p.gr_sb + int64_t(ts) * p.gr_st + int64_t(hv) * p.gr_sh, p.gr_dt);
-  in.beta = s5_ld_raw(p.br, int64_t(U.b) * p.br_sb + int64_t(ts) * p.br_st + int64_t(hv) * p.br_sh, p.br_dt);
-  in.scr = FLUSH ? s5_ld_raw(p.sc, int64_t(U.b) * p.sc_sb + int64_t(hv) * p.sc_sh + int64_t(t & 3) * p.sc_sv, p.sc_dt)
+  in.g = s5_ld_raw(p.gr, int64_t(U.s) * p.gr_sb + int64_t(ts) * p.gr_st + int64_t(hv) * p.gr_sh, p.gr_dt);
+  in.beta = s5_ld_raw(p.br, int64_t(U.s) * p.br_sb + int64_t(ts) * p.br_st + int64_t(hv) * p.br_sh, p.br_dt);
+  in.scr = FLUSH ? s5_ld_raw(p.sc, int64_t(U.s) * p.sc_sb + int64_t(hv) * p.sc_sh + int64_t(t & 3) * p.sc_sv, p.sc_dt)
                  : 0u;
   if constexpr (FUSED) {
     const bool bf = p.mx_dt == GDNR_BF16;
@@ -531,7 +540,7 @@ __device__ __forceinline__ S5In s5_fetch(const StepParams& p, const S5Unit& U, i
     in.bb = s5_ld_raw(p.bb, int64_t(U.b) * p.b_sb + int64_t(hv) * p.b_sh, p.b_dt);
     in.alog = p.a_log[int64_t(hv) * p.al_s];
     in.dtb = p.dt_bias[int64_t(hv) * p.db_s];
-    in.pos = p.pos[int64_t(U.b) * p.pos_s];
+    in.pos = U.s >= 0 ? p.pos[int64_t(U.s) * p.pos_s] : INT_MIN;  // null / bad slot: skipped
     in.flag = 0;
   } else {
     in.q = s5_load4(p.q, int64_t(U.b) * p.q_sb + int64_t(U.h) * p.q_sh + 4 * lane, p.q_dt == GDNR_BF16);
@@ -576,7 +585,7 @@ __device__ __forceinline__ void s5_append(const StepParams& p, const S5Unit& U, 
     const int e = lane >> 4, t = lane & 15;
     const bool owner = U.pp == 0;
     if (owner) {
-      *reinterpret_cast<uint2*>(p.kr + int64_t(U.b) * p.kr_sb + int64_t(pos) * p.kr_st + int64_t(U.h) * p.kr_sh +
+      *reinterpret_cast<uint2*>(p.kr + int64_t(U.s) * p.kr_sb + int64_t(pos) * p.kr_st + int64_t(U.h) * p.kr_sh +
                                 4 * lane) = a.kw;
       if (p.q_out) {
 #pragma unroll
@@ -586,13 +595,13 @@ __device__ __forceinline__ void s5_append(const StepParams& p, const S5Unit& U, 
     }
 #pragma unroll
     for (int h = 0; h < HPU; ++h)
-      *reinterpret_cast<uint2*>(p.vr + int64_t(U.b) * p.vr_sb + int64_t(pos) * p.vr_st +
+      *reinterpret_cast<uint2*>(p.vr + int64_t(U.s) * p.vr_sb + int64_t(pos) * p.vr_st +
                                 int64_t(U.hv0 + h) * p.vr_sh + 4 * lane) = a.vw[h];
     if (t == pos && e < HPU) {
       const int hv = U.hv0 + e;
-      store_scalar(p.gr, int64_t(U.b) * p.gr_sb + int64_t(pos) * p.gr_st + int64_t(hv) * p.gr_sh, p.gr_dt, a.g);
-      store_scalar(p.br, int64_t(U.b) * p.br_sb + int64_t(pos) * p.br_st + int64_t(hv) * p.br_sh, p.br_dt, a.beta);
-      if (p.pos_out && hv == 0) p.pos_out[int64_t(U.b) * p.po_s] = (pos + 1) % p.L;
+      store_scalar(p.gr, int64_t(U.s) * p.gr_sb + int64_t(pos) * p.gr_st + int64_t(hv) * p.gr_sh, p.gr_dt, a.g);
+      store_scalar(p.br, int64_t(U.s) * p.br_sb + int64_t(pos) * p.br_st + int64_t(hv) * p.br_sh, p.br_dt, a.beta);
+      if (p.pos_out && hv == 0) p.pos_out[int64_t(U.s) * p.po_s] = (pos + 1) % p.L;
     }
   }
 }
@@ -1316,7 +1325,7 @@ __device__ __forceinline__ void s5_flush_task(const StepParams& p, uint8_t* smem
                   FUSED ? reinterpret_cast<const uint16_t*>(res + lay.vnew + head * 256) : nullptr,
                   smem + lay.kbuf0 + ccw * 4096, reinterpret_cast<const __half*>(fd + S5_FQ16), fh, VBLOCK * v,
                   s5_n(code), s5_nmem(code), fh[S5_FSC + v], p.quant_rounded, p.sc,
-                  int64_t(U.b) * p.sc_sb + int64_t(hv) * p.sc_sh + int64_t(v) * p.sc_sv, p.sc_dt, stage, stash,
+                  int64_t(U.s) * p.sc_sb + int64_t(hv) * p.sc_sh + int64_t(v) * p.sc_sv, p.sc_dt, stage, stash,
                   lane);
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   __syncwarp();
@@ -1325,7 +1334,8 @@ __device__ __forceinline__ void s5_flush_task(const StepParams& p, uint8_t* smem
   __syncwarp();
 }
 
-template <bool FUSED, int HPU, bool FLUSH>
+// SIDX: packed decode (state slots through StepParams::sidx)
+template <bool FUSED, int HPU, bool FLUSH, bool SIDX>
 __global__ void __launch_bounds__(S5_THREADS, 1)
     step5_kernel(const __grid_constant__ StepParams p, const __grid_constant__ CUtensorMap ck_map,
                  const __grid_constant__ CUtensorMap kr_map, const __grid_constant__ CUtensorMap vr_map) {
@@ -1397,12 +1407,12 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
   const int npro = nu < S5_NS ? nu : S5_NS;
   auto prologue = [&]() {
     for (int i = 0; i < npro; ++i) {
-      const S5Unit U = s5_unit(bid + i * grid, p.H, G, geo);
+      const S5Unit U = s5_unit<SIDX>(bid + i * grid, p, G, geo);
       s5_expect_tx(&full[i], ck_bytes);
-      s5_tma4(smem + lay.stage0 + i * lay.stage_bytes + lay.ck, &ck_map, 0, 0, U.hv0, U.b, &full[i]);
+      s5_tma4(smem + lay.stage0 + i * lay.stage_bytes + lay.ck, &ck_map, 0, 0, U.hv0, U.s, &full[i]);
     }
   };
-  if (p.pdl && warp == 0 && lane == 0) prologue();
+  if (p.pdl && !p.sidx && warp == 0 && lane == 0) prologue();  // slots come from an input
   griddep_wait();
   // Chain warps: the first unit's inputs and whole key ring (small, on the
   // critical path), alongside the checkpoint stream.
@@ -1413,11 +1423,11 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
   S5In in0;
   if (chain_warp) {
     const int i0 = cw < nu ? cw : 0;
-    const S5Unit U = s5_unit(bid + i0 * grid, p.H, G, geo);
+    const S5Unit U = s5_unit<SIDX>(bid + i0 * grid, p, G, geo);
     if (lane == 0) {
-      const int nr = cw < nu ? nreq_k : 0;
+      const int nr = cw < nu && U.s >= 0 ? nreq_k : 0;
       mbar_arrive_expect_tx(&kfull[cw], uint32_t(nr) * box_bytes);
-      for (int j = 0; j < nr; ++j) s5_tma5(kbuf + j * box_bytes, &kr_map, 0, 0, U.h, j * geo.rb, U.b, &kfull[cw]);
+      for (int j = 0; j < nr; ++j) s5_tma5(kbuf + j * box_bytes, &kr_map, 0, 0, U.h, j * geo.rb, U.s, &kfull[cw]);
     }
     in0 = s5_fetch<FUSED, HPU, FLUSH>(p, U, lane);
     // the key rings and these loads go out first; the producer starts the
@@ -1441,9 +1451,9 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
   if (warp > S5_NCW) {
     int i = TC ? lane : team + S5_NS * (lane / VBW);
     i = i < nu ? i : 0;
-    const S5Unit U = s5_unit(bid + i * grid, p.H, G, geo);
+    const S5Unit U = s5_unit<SIDX>(bid + i * grid, p, G, geo);
     const int vb = TC ? (warp & 3) : rbase / VBLOCK + lane % VBW;
-    scl_raw = s5_ld_raw(p.sc, int64_t(U.b) * p.sc_sb + int64_t(U.hv0 + head_r) * p.sc_sh + int64_t(vb) * p.sc_sv,
+    scl_raw = s5_ld_raw(p.sc, int64_t(U.s < 0 ? 0 : U.s) * p.sc_sb + int64_t(U.hv0 + head_r) * p.sc_sh + int64_t(vb) * p.sc_sv,
                         p.sc_dt);
     if (TC) {  // the zero rows of the tensor-core T operands
       reinterpret_cast<uint32_t*>(smem + lay.zb)[tid - 32 * (1 + S5_NCW)] = 0u;
@@ -1456,9 +1466,9 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
   const int ti = S5_THREADS - 1 - tid;
   int raw0 = 0, raw1 = 0;
   if (ti < nu) {
-    const S5Unit U = s5_unit(bid + ti * grid, p.H, G, geo);
+    const S5Unit U = s5_unit<SIDX>(bid + ti * grid, p, G, geo);
     if constexpr (FUSED) {
-      raw0 = p.pos[int64_t(U.b) * p.pos_s];
+      raw0 = U.s >= 0 ? p.pos[int64_t(U.s) * p.pos_s] : INT_MIN;  // null / bad slot: skipped
     } else {
       raw0 = p.valid_len[int64_t(U.b) * p.vl_s];
       raw1 = s5_ld_flag(p.flush, int64_t(U.b) * p.fl_s, p.fl_dt);
@@ -1466,9 +1476,10 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
   }
   if (tid == S5_THREADS - 1) griddep_launch();
   if (ti < nu) {
-    const S5Unit U = s5_unit(bid + ti * grid, p.H, G, geo);
+    const S5Unit U = s5_unit<SIDX>(bid + ti * grid, p, G, geo);
     const int code = s5_code<FUSED>(raw0, raw1, L, FLUSH);
-    if (FUSED && s5_n(code) == 0 && U.h == 0 && U.pp == 0) atomicOr(p.err, GDNR_DEVERR_BAD_POS);
+    if (FUSED && s5_n(code) == 0 && U.s >= 0 && U.h == 0 && U.pp == 0) atomicOr(p.err, GDNR_DEVERR_BAD_POS);
+    if (U.s == -2 && U.h == 0 && U.pp == 0) atomicOr(p.err, GDNR_DEVERR_BAD_SLOT);
     if (s5_n(code) > 0 && s5_skip(code) && p.flush_hint == GDNR_FLUSH_NONE && U.h == 0 && U.pp == 0)
       atomicOr(p.err, GDNR_DEVERR_BAD_HINT);
     if (!FUSED && s5_skip(code) && p.flush_hint == GDNR_FLUSH_NONE && U.h == 0 && U.pp == 0)
@@ -1493,29 +1504,29 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
     auto load_unit = [&](int i) {
       const int s = i % S5_NS;
       const int code = table[i];
-      const S5Unit U = s5_unit(bid + i * grid, p.H, G, geo);
+      const S5Unit U = s5_unit<SIDX>(bid + i * grid, p, G, geo);
       uint8_t* sb = smem + lay.stage0 + s * lay.stage_bytes;
       const bool skip = s5_skip(code);
       const int nreq = skip ? 0 : (s5_nmem(code) + geo.rb - 1) / geo.rb;
-      const bool ck = i >= (p.pdl ? npro : 0) && !skip;  // not already requested before griddepcontrol.wait
+      const bool ck = i >= (p.pdl && !p.sidx ? npro : 0) && !skip;  // not already requested before griddepcontrol.wait
       mbar_arrive_expect_tx(&full[s], (ck ? ck_bytes : 0u) + uint32_t(nreq * HPU) * box_bytes);
-      if (ck) s5_tma4(sb + lay.ck, &ck_map, 0, 0, U.hv0, U.b, &full[s]);
+      if (ck) s5_tma4(sb + lay.ck, &ck_map, 0, 0, U.hv0, U.s, &full[s]);
       for (int j = 0; j < nreq; ++j)
 #pragma unroll
         for (int e = 0; e < HPU; ++e)
-          s5_tma5(sb + lay.vr + e * 4096 + j * box_bytes, &vr_map, 0, 0, U.hv0 + e, j * geo.rb, U.b, &full[s]);
+          s5_tma5(sb + lay.vr + e * 4096 + j * box_bytes, &vr_map, 0, 0, U.hv0 + e, j * geo.rb, U.s, &full[s]);
       if (i == S5_NS - 1) {
         // the units that wait for a free stage: their tiles and rings into L2 now,
         // so that their stage loads later are served from L2
         for (int u = S5_NS; u < nu; ++u) {
           const int cu = table[u];
           if (s5_skip(cu)) continue;
-          const S5Unit V = s5_unit(bid + u * grid, p.H, G, geo);
-          s5_prefetch4(&ck_map, 0, 0, V.hv0, V.b);
+          const S5Unit V = s5_unit<SIDX>(bid + u * grid, p, G, geo);
+          s5_prefetch4(&ck_map, 0, 0, V.hv0, V.s);
           const int nr = (s5_nmem(cu) + geo.rb - 1) / geo.rb;
           for (int j = 0; j < nr; ++j)
 #pragma unroll
-            for (int e = 0; e < HPU; ++e) s5_prefetch5(&vr_map, 0, 0, V.hv0 + e, j * geo.rb, V.b);
+            for (int e = 0; e < HPU; ++e) s5_prefetch5(&vr_map, 0, 0, V.hv0 + e, j * geo.rb, V.s);
         }
       }
     };
@@ -1584,7 +1595,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
     // =================== chain warps ===================
     uint8_t* res = smem + lay.res0 + cw * lay.res_bytes;
     for (int i = cw, k = 0; i < nu; i += S5_NCW, ++k) {
-      const S5Unit U = s5_unit(bid + i * grid, p.H, G, geo);
+      const S5Unit U = s5_unit<SIDX>(bid + i * grid, p, G, geo);
       bool ok = true;
       if (k > 0) {
         // the key ring and result block are free once both readout warps of
@@ -1595,10 +1606,10 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
         if (lane == 0) {
-          const int nr = ok ? nreq_k : 0;
+          const int nr = ok && U.s >= 0 ? nreq_k : 0;
           mbar_arrive_expect_tx(&kfull[cw], uint32_t(nr) * box_bytes);
           for (int j = 0; j < nr; ++j)
-            s5_tma5(kbuf + j * box_bytes, &kr_map, 0, 0, U.h, j * geo.rb, U.b, &kfull[cw]);
+            s5_tma5(kbuf + j * box_bytes, &kr_map, 0, 0, U.h, j * geo.rb, U.s, &kfull[cw]);
         }
         in0 = s5_fetch<FUSED, HPU, FLUSH>(p, U, lane);
       }
@@ -1641,7 +1652,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       ok = s5_warp_wait(&cbar[ccw], uint32_t(k & 1), p.err, abort, lane) && ok;
       const bool flush = FLUSH && s5_flush(code);
       uint8_t* sb = smem + lay.stage0 + s * lay.stage_bytes;
-      const S5Unit U = s5_unit(bid + i * grid, p.H, G, geo);
+      const S5Unit U = s5_unit<SIDX>(bid + i * grid, p, G, geo);
       const bool mma = ok && !flush && !s5_skip(code);
       const uint8_t* res = smem + lay.res0 + ccw * lay.res_bytes;
       // V^T c over the slots read from memory (no tensor memory needed yet)
@@ -1699,7 +1710,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
         if (rw == 0) {
           s5_warp_wait_count(&vdone[s], uint32_t(NT), p.err, abort, lane);
           if (lane == 0 && *abort == 0) {
-            s5_tma_store4(&ck_map, sb + lay.ck, 0, 0, U.hv0, U.b);
+            s5_tma_store4(&ck_map, sb + lay.ck, 0, 0, U.hv0, U.s);
             asm volatile("cp.async.bulk.commit_group;" ::: "memory");
             asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
           }
@@ -1707,7 +1718,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       } else if (mma) {
         float sc = sc_pref;
         if (i >= 32)
-          sc = load_scalar(p.sc, int64_t(U.b) * p.sc_sb + int64_t(U.hv0 + head_r) * p.sc_sh + int64_t(qd) * p.sc_sv,
+          sc = load_scalar(p.sc, int64_t(U.s) * p.sc_sb + int64_t(U.hv0 + head_r) * p.sc_sh + int64_t(qd) * p.sc_sv,
                            p.sc_dt);
         const float* misc = reinterpret_cast<const float*>(res + lay.misc) + head_r * 4;
         s5_tc_after_sync();
@@ -1768,8 +1779,8 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       sc = 1.0f;
       sc_base = 0;
       if (lane < VBW && !s5_skip(code)) {
-        const S5Unit U = s5_unit(bid + i * grid, p.H, G, geo);
-        sc = load_scalar(p.sc, int64_t(U.b) * p.sc_sb + int64_t(U.hv0 + head_r) * p.sc_sh +
+        const S5Unit U = s5_unit<SIDX>(bid + i * grid, p, G, geo);
+        sc = load_scalar(p.sc, int64_t(U.s) * p.sc_sb + int64_t(U.hv0 + head_r) * p.sc_sh +
                                    int64_t(rbase / VBLOCK + lane) * p.sc_sv,
                          p.sc_dt);
       }
@@ -1788,7 +1799,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
         atomicExch(&vword[s], uint32_t(i) << 8);
       }
       asm volatile("bar.sync %0, %1;" ::"r"(4 + team), "n"(32 * S5_TEAM) : "memory");
-      const S5Unit U = s5_unit(bid + i * grid, p.H, G, geo);
+      const S5Unit U = s5_unit<SIDX>(bid + i * grid, p, G, geo);
       if (ok) {
         for (;;) {
           const int t = s5_claim(&vword[s], i, NT, lane);
@@ -1799,12 +1810,12 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       }
       s5_warp_wait_count(&vdone[s], uint32_t(NT), p.err, abort, lane);
       if (mem == 0 && lane == 0 && *abort == 0) {
-        s5_tma_store4(&ck_map, sb + lay.ck, 0, 0, U.hv0, U.b);
+        s5_tma_store4(&ck_map, sb + lay.ck, 0, 0, U.hv0, U.s);
         asm volatile("cp.async.bulk.commit_group;" ::: "memory");
         asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
       }
     } else if (ok && !s5_skip(code)) {
-      const S5Unit U = s5_unit(bid + i * grid, p.H, G, geo);
+      const S5Unit U = s5_unit<SIDX>(bid + i * grid, p, G, geo);
       const uint8_t* res = smem + lay.res0 + ccw * lay.res_bytes;
       const float* misc = reinterpret_cast<const float*>(res + lay.misc) + head_r * 4;
       s5_readout<MW>(sb + lay.ck + head_r * 16384, sb + lay.vr + head_r * 4096, res + lay.t8 + head_r * 8 * T8STR,
@@ -1918,10 +1929,10 @@ static S5EncodeFn s5_encode_fn() {
   return fn;
 }
 
-template <bool FUSED, int HPU, bool FLUSH>
+template <bool FUSED, int HPU, bool FLUSH, bool SIDX = false>
 static cudaError_t s5_launch(const StepParams& p, const CUtensorMap& ck, const CUtensorMap& kr,
                              const CUtensorMap& vr, int grid, uint32_t smem, bool pdl, cudaStream_t stream) {
-  auto kern = step5_kernel<FUSED, HPU, FLUSH>;
+  auto kern = step5_kernel<FUSED, HPU, FLUSH, SIDX>;
   static int configured = 0;
   if (int(smem) > configured) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
@@ -1949,9 +1960,10 @@ cudaError_t launch_step5(const StepParams& p, bool fused, bool pdl, cudaStream_t
   S5Layout lay;
   if (!s5_grid(p, grid, lay)) return cudaErrorInvalidValue;
   CUtensorMap ck, kr, vr;
+  const int nst = p.sidx ? p.S : p.B;  // state slots (packed decode: the pool's)
   {
-    // checkpoint [B][HV][V][K] e4m3: box = hpu whole 128 x 128 head tiles
-    const cuuint64_t dims[4] = {128, 128, cuuint64_t(p.HV), cuuint64_t(p.B)};
+    // checkpoint [slots][HV][V][K] e4m3: box = hpu whole 128 x 128 head tiles
+    const cuuint64_t dims[4] = {128, 128, cuuint64_t(p.HV), cuuint64_t(nst)};
     const cuuint64_t strides[3] = {128, cuuint64_t(p.ck_sh), cuuint64_t(p.ck_sb)};
     const cuuint32_t box[4] = {128, 128, cuuint32_t(g.hpu), 1};
     const cuuint32_t es[4] = {1, 1, 1, 1};
@@ -1963,7 +1975,7 @@ cudaError_t launch_step5(const StepParams& p, bool fused, bool pdl, cudaStream_t
   // rings [B][L][heads][128] bf16 viewed as [B][L][heads][2][64]: a box of rb
   // slots lands as rb x 256-byte rows, each 128-byte half swizzled
   auto ring_map = [&](CUtensorMap* m, void* base, int heads, int64_t s_head, int64_t s_slot, int64_t s_b) {
-    const cuuint64_t dims[5] = {64, 2, cuuint64_t(heads), cuuint64_t(p.L), cuuint64_t(p.B)};
+    const cuuint64_t dims[5] = {64, 2, cuuint64_t(heads), cuuint64_t(p.L), cuuint64_t(nst)};
     const cuuint64_t strides[4] = {128, cuuint64_t(s_head * 2), cuuint64_t(s_slot * 2), cuuint64_t(s_b * 2)};
     const cuuint32_t box[5] = {64, 2, 1, cuuint32_t(g.rb), 1};
     const cuuint32_t es[5] = {1, 1, 1, 1, 1};
@@ -1976,6 +1988,14 @@ cudaError_t launch_step5(const StepParams& p, bool fused, bool pdl, cudaStream_t
   // skipped and reported); otherwise the flush-capable one
   const bool flush = p.flush_hint != GDNR_FLUSH_NONE;
   const uint32_t sm = lay.total;
+  if (fused && p.sidx) {
+    if (g.hpu == 2)
+      return flush ? s5_launch<true, 2, true, true>(p, ck, kr, vr, grid, sm, pdl, stream)
+                   : s5_launch<true, 2, false, true>(p, ck, kr, vr, grid, sm, pdl, stream);
+    return flush ? s5_launch<true, 1, true, true>(p, ck, kr, vr, grid, sm, pdl, stream)
+                 : s5_launch<true, 1, false, true>(p, ck, kr, vr, grid, sm, pdl, stream);
+  }
+  if (p.sidx) return cudaErrorNotSupported;  // packed decode: fused steps only
   if (fused) {
     if (g.hpu == 2)
       return flush ? s5_launch<true, 2, true>(p, ck, kr, vr, grid, sm, pdl, stream)

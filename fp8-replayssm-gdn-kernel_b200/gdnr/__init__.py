@@ -10,6 +10,7 @@ from ._lib import GdnrError, GdnrValueError, load as load_library  # noqa: F401
 from .ops import (  # noqa: F401
     QuantizedCheckpoint,
     dequantize_checkpoint,
+    fused_recurrent_gated_delta_rule_packed_decode,
     gdn_bf16_step,
     gdn_fused_step,
     gdn_prep_ring,

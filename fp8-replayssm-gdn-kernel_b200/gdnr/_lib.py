@@ -42,6 +42,7 @@ STATUS_NAMES = {
 DEVERR_WAIT_TIMEOUT = 0x1
 DEVERR_BAD_POS = 0x2
 DEVERR_BAD_HINT = 0x4
+DEVERR_BAD_SLOT = 0x8
 
 
 class Tensor(ctypes.Structure):
@@ -101,6 +102,18 @@ class StepArgs(ctypes.Structure):
     ]
 
 
+class PackedDecodeArgs(ctypes.Structure):
+    _fields_ = [(n, Tensor) for n in ("mixed_qkv", "a", "b", "a_log", "dt_bias", "state_indices", "pos", "pos_out",
+                                      "checkpoint", "scale", "k_ring", "v_ring", "g_ring", "beta_ring", "out")] + [
+        ("qk_scale", ctypes.c_float),
+        ("use_qk_l2norm", ctypes.c_int32),
+        ("quant_divisor", ctypes.c_int32),
+        ("error_flag", ctypes.c_void_p),
+        ("flush_hint", ctypes.c_int32),
+        ("launch_flags", ctypes.c_int32),
+    ]
+
+
 class CodecArgs(ctypes.Structure):
     _fields_ = [(n, Tensor) for n in ("state", "payload", "scale")] + [
         ("quant_divisor", ctypes.c_int32),
@@ -119,6 +132,7 @@ SIGNATURES = {
     "gdnr_replay_split_static": ([ctypes.POINTER(ReplaySplitStaticArgs), ctypes.c_void_p], ctypes.c_int),
     "gdnr_prep_ring": ([ctypes.POINTER(PrepArgs), ctypes.c_void_p], ctypes.c_int),
     "gdnr_fused_step": ([ctypes.POINTER(StepArgs), ctypes.c_void_p], ctypes.c_int),
+    "gdnr_packed_decode": ([ctypes.POINTER(PackedDecodeArgs), ctypes.c_void_p], ctypes.c_int),
     "gdnr_quantize_vblock32": ([ctypes.POINTER(CodecArgs), ctypes.c_void_p], ctypes.c_int),
     "gdnr_dequantize_vblock32": ([ctypes.POINTER(CodecArgs), ctypes.c_void_p], ctypes.c_int),
     "gdnr_bf16_step": ([ctypes.POINTER(Bf16StepArgs), ctypes.c_void_p], ctypes.c_int),

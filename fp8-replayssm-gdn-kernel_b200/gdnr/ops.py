@@ -261,11 +261,12 @@ def gdn_fused_step(
     distinct from ``pos``) receives ``(pos+1) % L``.
 
     ``flush_hint``: "auto" (some sequences may be at ``L-1``: the
-    non-flushing heads and the flushing heads run as two launches), "none"
-    (no ``pos[b] == L-1``: one launch; a violation is reported in the device
-    error word as ``GDNR_DEVERR_BAD_HINT`` and that sequence is left
-    unprocessed) or "all" (one launch of the flush-capable kernel).  ``pdl``
-    as in :func:`gdn_replay_fp8`.
+    flush-capable kernel decides per sequence on the device), "none" (no
+    ``pos[b] == L-1``: the kernel without the flush path, the fastest when it
+    holds; a violation is reported in the device error word as
+    ``GDNR_DEVERR_BAD_HINT`` and that sequence is left unprocessed) or "all"
+    (the flush-capable kernel, as "auto").  ``pdl`` as in
+    :func:`gdn_replay_fp8`.
     """
     batch = mixed_qkv.shape[0]
     value_heads = v_ring.shape[2]
@@ -292,6 +293,77 @@ def gdn_fused_step(
     args.flush_hint = _flush_hint(flush_hint)
     args.launch_flags = LAUNCH_PDL if pdl else 0
     _lib.check(_lib.load().gdnr_fused_step(ctypes.byref(args), _lib.stream_handle(mixed_qkv.device)))
+    return out
+
+
+KEY_SCALE = 128 ** -0.5  # the output scale head_k_dim^-1/2 the kernels apply
+
+
+def fused_recurrent_gated_delta_rule_packed_decode(
+    mixed_qkv: torch.Tensor,
+    a: torch.Tensor,
+    b: torch.Tensor,
+    A_log: torch.Tensor,
+    dt_bias: torch.Tensor,
+    scale: float,
+    initial_state,
+    out: torch.Tensor,
+    ssm_state_indices: torch.Tensor,
+    use_qk_l2norm_in_kernel: bool = True,
+    *,
+    quant_divisor: str = "oracle",
+    error_flag: torch.Tensor | None = None,
+    flush_hint: str = "auto",
+    pdl: bool = False,
+) -> torch.Tensor:
+    """The serving engine's GDN decode call over a pool of FP8 replay states.
+
+    Same arguments as the production operator the reference swaps out
+    (``fused_recurrent_gated_delta_rule_packed_decode`` at vLLM's
+    ``_forward_core_decode_non_spec`` call site; reference
+    prototype/bench_gdn_full_contract.py:157-170, contract notes
+    findings.md:37-45), except that ``initial_state`` is a
+    :class:`gdnr.ReplayState` whose leading dimension is the slot pool instead
+    of the bf16 state cache ``[slots, HV, V, K]``.  Batch row ``i`` runs one
+    fused decode step (prep, ring append, replay, and the flush when the slot's
+    ring position is ``L-1``) on slot ``ssm_state_indices[i]`` of every state
+    tensor and advances that slot's ring position.  Slot 0 is the null slot
+    (padding rows): nothing is read or written for it and its ``out`` rows are
+    left as they are; an index outside ``[0, slots)`` is treated the same way
+    and reported in the device error word as ``GDNR_DEVERR_BAD_SLOT``.
+    ``out`` is ``[B, 1, HV, V]`` (or ``[B, HV, V]``).  q and k are always
+    L2-normalised in the kernel and the output is scaled by ``K^-1/2``:
+    ``use_qk_l2norm_in_kernel`` must be true and ``scale`` must be
+    ``head_k_dim ** -0.5``.  The other keywords as in :func:`gdn_fused_step`.
+    """
+    if not use_qk_l2norm_in_kernel:
+        raise _lib.GdnrValueError(_lib.ERR_UNSUPPORTED,
+                                  "use_qk_l2norm_in_kernel must be True: the kernel always normalises q and k")
+    if abs(float(scale) - KEY_SCALE) > 1e-6 * KEY_SCALE:
+        raise _lib.GdnrValueError(_lib.ERR_UNSUPPORTED,
+                                  f"scale must be head_k_dim ** -0.5 = {KEY_SCALE!r} (got {scale!r})")
+    st = initial_state
+    # the ring positions advance through a staging copy: the kernel reads
+    # st.pos and writes the batch's slots of pos_next, then st.pos takes it
+    pos_next = getattr(st, "_pos_next", None)
+    if pos_next is None or pos_next.shape != st.pos.shape or pos_next.device != st.pos.device:
+        pos_next = torch.empty_like(st.pos)
+        st._pos_next = pos_next
+    pos_next.copy_(st.pos)
+    args = _lib.PackedDecodeArgs()
+    for name, t in (("mixed_qkv", mixed_qkv), ("a", a), ("b", b), ("a_log", A_log), ("dt_bias", dt_bias),
+                    ("state_indices", ssm_state_indices), ("pos", st.pos), ("pos_out", pos_next),
+                    ("checkpoint", st.checkpoint), ("scale", st.scale), ("k_ring", st.k_ring), ("v_ring", st.v_ring),
+                    ("g_ring", st.g_ring), ("beta_ring", st.beta_ring), ("out", out)):
+        setattr(args, name, _lib.tensor_desc(t))
+    args.qk_scale = float(scale)
+    args.use_qk_l2norm = 1
+    args.quant_divisor = _divisor(quant_divisor)
+    args.error_flag = _err_ptr(error_flag)
+    args.flush_hint = _flush_hint(flush_hint)
+    args.launch_flags = LAUNCH_PDL if pdl else 0
+    _lib.check(_lib.load().gdnr_packed_decode(ctypes.byref(args), _lib.stream_handle(mixed_qkv.device)))
+    st.pos.copy_(pos_next)
     return out
 
 

@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define GDNR_ABI_VERSION 1
+#define GDNR_ABI_VERSION 2 /* 2: adds gdnr_packed_decode (the other structs are unchanged) */
 
 typedef enum {
   GDNR_DT_NONE = 0,
@@ -58,6 +58,7 @@ typedef enum {
 #define GDNR_DEVERR_WAIT_TIMEOUT 0x1u /* a bounded mbarrier wait gave up */
 #define GDNR_DEVERR_BAD_POS 0x2u      /* fused step: pos[b] outside [0, L) */
 #define GDNR_DEVERR_BAD_HINT 0x4u     /* flush_hint NONE but a sequence's ring was full */
+#define GDNR_DEVERR_BAD_SLOT 0x8u     /* packed decode: state_indices[i] outside [0, slots) */
 
 /* flush_hint: what the caller knows about which sequences flush in this call */
 #define GDNR_FLUSH_AUTO 0 /* unknown: every head is checked on the device */
@@ -169,6 +170,44 @@ typedef struct {
 } gdnr_step_args;
 
 int gdnr_fused_step(const gdnr_step_args* args, void* stream);
+
+/* ---- gdnr_packed_decode: the production decode call over a state-slot pool --
+ * Replaces the serving engine's decode call
+ *   fused_recurrent_gated_delta_rule_packed_decode(mixed_qkv, a, b, A_log, dt_bias, scale,
+ *       initial_state, out, ssm_state_indices, use_qk_l2norm_in_kernel=True)
+ * as the reference drives it (prototype/bench_gdn_full_contract.py:157-170; contract notes
+ * findings.md:37-45), with the bf16 state cache [slots,HV,V,K] replaced by the FP8
+ * checkpoint + ring pool below: batch row i uses slot state_indices[i] of every state
+ * tensor.  Slot 0 is the null slot (the serving engine's padding): that row is skipped --
+ * no state is read or written and its out rows are left as they are.  An index outside
+ * [0, slots) is skipped the same way and reported as GDNR_DEVERR_BAD_SLOT.  q and k are
+ * always L2-normalised in the kernel and the output is scaled by K^-1/2: the production
+ * call's use_qk_l2norm_in_kernel and scale arguments must be 1 and K^-1/2.  The step is
+ * gdnr_fused_step's (prep + ring append + replay, and the flush when a slot's pos is L-1);
+ * pos_out (optional, [slots]) receives (pos+1) % L for the slots of the batch.  E4M3
+ * checkpoints only, in the layout gdnr_fused_step's persistent kernel takes (16-byte
+ * aligned rows and rings, HV/H = 1 or even, 4 <= L <= 16); anything else fails with
+ * GDNR_ERR_UNSUPPORTED. */
+typedef struct {
+  gdnr_tensor mixed_qkv, a, b, a_log, dt_bias; /* [B,...] as gdnr_step_args */
+  gdnr_tensor state_indices; /* [B] I32: slot of each batch row */
+  gdnr_tensor pos;        /* [slots] I32: ring slot of this token, per state slot */
+  gdnr_tensor pos_out;    /* optional [slots] I32 (distinct from pos) */
+  gdnr_tensor checkpoint; /* [slots,HV,V,K] E4M3, in/out */
+  gdnr_tensor scale;      /* [slots,HV,V/32] F16|F32, in/out */
+  gdnr_tensor k_ring, v_ring, g_ring, beta_ring; /* [slots,L,...] in/out */
+  gdnr_tensor out;        /* [B,HV,V] or [B,1,HV,V] BF16|F32 */
+  float qk_scale;         /* must be K^-1/2 */
+  int32_t use_qk_l2norm;  /* must be 1 */
+  int32_t quant_divisor;
+  uint32_t* error_flag;
+  int32_t flush_hint;     /* GDNR_FLUSH_* */
+  int32_t launch_flags;   /* GDNR_LAUNCH_*; GDNR_LAUNCH_PDL is accepted, but the early
+                             checkpoint requests wait for griddepcontrol.wait here (the
+                             slots come from state_indices, an input) */
+} gdnr_packed_decode_args;
+
+int gdnr_packed_decode(const gdnr_packed_decode_args* args, void* stream);
 
 /* ---- FP8 vblock32 codec ------------------------------------------------ */
 typedef struct {

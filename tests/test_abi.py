@@ -37,7 +37,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_version_strings():
     lib = _lib.load()
-    assert lib.gdnr_abi_version() == 1
+    assert lib.gdnr_abi_version() == 2
     assert b"sm_100a" in lib.gdnr_version()
 
 
