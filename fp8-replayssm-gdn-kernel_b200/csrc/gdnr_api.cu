@@ -130,6 +130,7 @@ const int DT_F32[] = {GDNR_F32};
 const int DT_I32[] = {GDNR_I32};
 const int DT_BF16[] = {GDNR_BF16};
 const int DT_E4M3[] = {GDNR_E4M3};
+const int DT_PAYLOAD[] = {GDNR_E4M3, GDNR_I8};
 const int DT_CK[] = {GDNR_E4M3, GDNR_F32};
 const int DT_SCALE[] = {GDNR_F16, GDNR_F32};
 const int DT_ACT[] = {GDNR_BF16, GDNR_F32};
@@ -464,7 +465,7 @@ static int validate_codec(const gdnr_codec_args* a, CodecParams& p) {
   const int64_t B = a->state.shape[0], HV = a->state.shape[1], V = a->state.shape[2], K = a->state.shape[3];
   if (K != 128 || V != 128) return set_error(GDNR_ERR_UNSUPPORTED, "only V = K = 128 is implemented");
   const int64_t want[4] = {B, HV, V, K};
-  CHECK(check_tensor(a->payload, "payload", 4, DT_E4M3, 1, want));
+  CHECK(check_tensor(a->payload, "payload", 4, DT_PAYLOAD, 2, want));
   const int64_t want_s[3] = {B, HV, V / VBLOCK};
   CHECK(check_tensor(a->scale, "scale", 3, DT_SCALE, 2, want_s));
   CHECK(check_inner_contiguous(a->state, "state"));
@@ -491,6 +492,7 @@ static int validate_codec(const gdnr_codec_args* a, CodecParams& p) {
   p.HV = int(HV);
   p.quant_rounded = a->quant_divisor;
   p.sat = a->saturation_count;
+  p.int8 = a->payload.dtype == GDNR_I8 ? 1 : 0;
   return GDNR_OK;
 }
 

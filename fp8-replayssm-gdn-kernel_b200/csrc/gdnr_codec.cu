@@ -7,6 +7,11 @@
 // exactly what this kernel writes for the same float32 state.
 //
 // dequantize: payload * scale[row/32] (ref.py:109-134).
+//
+// INT8 payloads ("vblock_int8", ref.py:44-47, :96-97): scale amax/127 (1 for a
+// zero block), code = round-half-even(x / divisor) clamped to +-127 -- the
+// IEEE quotient, then the integer rounding, as the reference's
+// `(source / scale).round().clamp(-127, 127)` does.
 #include "gdnr_device.cuh"
 #include "gdnr_internal.h"
 
@@ -42,10 +47,28 @@ __global__ void __launch_bounds__(256) quantize_kernel(const __grid_constant__ C
   am = red[0];
 #pragma unroll
   for (int w = 1; w < 8; ++w) am = fmax_nan(am, red[w]);
-  const VScale vs = vblock_scale(am, p.quant_rounded);
-  const float rcp = __fdiv_rn(1.0f, vs.divisor);
   uint32_t sat = 0;
-  const uint4 q = quantize16_fast(x, vs.divisor, rcp, p.sat != nullptr, sat);
+  VScale vs;
+  uint4 q;
+  if (p.int8) {
+    const float s32 = am > 0.0f ? __fdiv_rn(am, 127.0f) : 1.0f;
+    vs.stored = __float2half_rn(s32);
+    vs.divisor = p.quant_rounded ? __half2float(vs.stored) : s32;
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float y = __fdiv_rn(x[i], vs.divisor);
+      sat += fabsf(y) > 127.0f ? 1u : 0u;
+      // NaN -> 0 (what the reference's float -> int8 cast gives on its host)
+      const float c = y != y ? 0.0f : fminf(fmaxf(rintf(y), -127.0f), 127.0f);
+      w[i >> 2] |= (uint32_t(__float2int_rn(c)) & 0xFFu) << (8 * (i & 3));
+    }
+    q = make_uint4(w[0], w[1], w[2], w[3]);
+  } else {
+    vs = vblock_scale(am, p.quant_rounded);
+    const float rcp = __fdiv_rn(1.0f, vs.divisor);
+    q = quantize16_fast(x, vs.divisor, rcp, p.sat != nullptr, sat);
+  }
   *reinterpret_cast<uint4*>(p.payload + int64_t(b) * p.pl_sb + int64_t(hv) * p.pl_sh + int64_t(r) * 128 + c * 16) = q;
   if (tid == 0) {
     const int64_t si = int64_t(b) * p.sc_sb + int64_t(hv) * p.sc_sh + int64_t(vb) * p.sc_sv;
@@ -79,10 +102,16 @@ __global__ void __launch_bounds__(256) dequantize_kernel(const __grid_constant__
   const uint4 w =
       *reinterpret_cast<const uint4*>(p.payload + int64_t(b) * p.pl_sb + int64_t(hv) * p.pl_sh + int64_t(r) * 128 + c * 16);
   float f[16];
-  e4m3x4_to_f4(w.x, f);
-  e4m3x4_to_f4(w.y, f + 4);
-  e4m3x4_to_f4(w.z, f + 8);
-  e4m3x4_to_f4(w.w, f + 12);
+  if (p.int8) {
+    const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 16; ++i) f[i] = float(int8_t(uint8_t(wv[i >> 2] >> (8 * (i & 3)))));
+  } else {
+    e4m3x4_to_f4(w.x, f);
+    e4m3x4_to_f4(w.y, f + 4);
+    e4m3x4_to_f4(w.z, f + 8);
+    e4m3x4_to_f4(w.w, f + 12);
+  }
   float4* dst = reinterpret_cast<float4*>(p.state + int64_t(b) * p.st_sb + int64_t(hv) * p.st_sh + int64_t(r) * 128 + c * 16);
 #pragma unroll
   for (int i = 0; i < 4; ++i) dst[i] = make_float4(f[4 * i] * sc, f[4 * i + 1] * sc, f[4 * i + 2] * sc, f[4 * i + 3] * sc);

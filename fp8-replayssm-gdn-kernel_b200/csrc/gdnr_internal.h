@@ -127,6 +127,7 @@ struct CodecParams {
   int32_t B, HV;
   int32_t quant_rounded;
   uint32_t* sat;
+  int32_t int8;  // payload: int8 codes with amax/127 scales ("vblock_int8"), else e4m3
 };
 
 cudaError_t launch_quantize(const CodecParams& p, cudaStream_t stream);

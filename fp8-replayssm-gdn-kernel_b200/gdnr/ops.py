@@ -403,18 +403,22 @@ def quantize_checkpoint(
     scale: torch.Tensor | None = None,
     compute_saturation: bool = True,
 ) -> QuantizedCheckpoint:
-    """GPU vblock32 FP8 quantiser, bit-exact with ``quantize_checkpoint(state, 'vblock', 32)``.
+    """GPU vblock32 quantiser, bit-exact with ``quantize_checkpoint(state, granularity, 32)``
+    for ``granularity`` "vblock" (FP8 E4M3 payload) and "vblock_int8" (int8
+    payload, scales amax/127; ref.py:44-47, :96-97).
 
     ``state`` [B,HV,V,K] float32 on CUDA.  ``compute_saturation`` reads the
     saturation count back (one synchronisation), like the reference's
-    ``.item()`` at ref.py:95.
+    ``.item()`` at ref.py:95.  INT8 checkpoints are a codec option: the replay
+    and step entry points take E4M3 (or float32) checkpoints.
     """
-    if granularity != "vblock" or tile_size != 32:
-        raise ValueError("the GPU codec implements granularity='vblock', tile_size=32 only")
+    if granularity not in ("vblock", "vblock_int8") or tile_size != 32:
+        raise ValueError("the GPU codec implements granularity 'vblock' / 'vblock_int8' with tile_size=32 only")
+    int8 = granularity == "vblock_int8"
     state = state if state.dtype == torch.float32 else state.float()
     b, hv, v, k = state.shape
     if payload is None:
-        payload = torch.empty(b, hv, v, k, dtype=torch.float8_e4m3fn, device=state.device)
+        payload = torch.empty(b, hv, v, k, dtype=torch.int8 if int8 else torch.float8_e4m3fn, device=state.device)
     if scale is None:
         scale = torch.empty(b, hv, v // 32, dtype=scale_dtype, device=state.device)
     sat = torch.zeros(1, dtype=torch.int32, device=state.device) if compute_saturation else None
@@ -426,13 +430,13 @@ def quantize_checkpoint(
     args.saturation_count = sat.data_ptr() if sat is not None else None
     _lib.check(_lib.load().gdnr_quantize_vblock32(ctypes.byref(args), _lib.stream_handle(state.device)))
     frac = float(sat.item()) / max(state.numel(), 1) if sat is not None else 0.0
-    return QuantizedCheckpoint(payload, scale, "vblock", 32, frac)
+    return QuantizedCheckpoint(payload, scale, granularity, 32, frac)
 
 
 def dequantize_checkpoint(ckpt: QuantizedCheckpoint, out: torch.Tensor | None = None) -> torch.Tensor:
-    """payload * scale[row/32] as float32 (ref.py:109-134), on the GPU."""
-    if ckpt.granularity != "vblock" or ckpt.tile_size != 32:
-        raise ValueError("the GPU codec implements granularity='vblock', tile_size=32 only")
+    """payload * scale[row/32] as float32 (ref.py:109-134), on the GPU (E4M3 or int8 payload)."""
+    if ckpt.granularity not in ("vblock", "vblock_int8") or ckpt.tile_size != 32:
+        raise ValueError("the GPU codec implements granularity 'vblock' / 'vblock_int8' with tile_size=32 only")
     if out is None:
         out = torch.empty(ckpt.payload.shape, dtype=torch.float32, device=ckpt.payload.device)
     args = _lib.CodecArgs()

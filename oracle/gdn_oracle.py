@@ -509,26 +509,34 @@ def fused_step(st: RingState, mixed_qkv, a, b, a_log, dt_bias, pos, heads, key_d
     return replay_step(st, qn, pos, out_dtype, quant_divisor), qn
 
 
-def quantize_vblock32(state, divisor="oracle") -> QuantizedCheckpoint:
-    """vblock32 FP8 quantiser with a selectable divisor convention.
+def quantize_vblock32(state, divisor="oracle", int8=False) -> QuantizedCheckpoint:
+    """vblock32 quantiser (FP8 E4M3, or int8 with ``int8``) with a selectable
+    divisor convention.
 
-    ``divisor='oracle'`` is exactly ``quantize_checkpoint(state,'vblock',32)``;
-    ``'rounded'`` divides by float32(float16(scale)) as kern.py:231-236 does
-    (but keeps the oracle's amax==0 -> 1.0 rule of ref.py:36-37).
+    ``divisor='oracle'`` is exactly ``quantize_checkpoint(state,'vblock',32)``
+    (``'vblock_int8'`` with ``int8``, ref.py:44-47, :96-97); ``'rounded'``
+    divides by float32(float16(scale)) as kern.py:231-236 does (but keeps the
+    oracle's amax==0 -> 1.0 rule of ref.py:36-37).
     """
+    gran = "vblock_int8" if int8 else "vblock"
     if divisor == "oracle":
-        return quantize_checkpoint(state, "vblock", 32)
+        return quantize_checkpoint(state, gran, 32)
+    qmax = INT8_MAX if int8 else FP8_MAX
     source = np.asarray(state, _F32)
     vd, kd = source.shape[-2:]
     blocks = source.reshape(*source.shape[:-2], vd // 32, 32, kd)
-    s16 = fp16_round(safe_scale(_nan_amax(blocks, (-2, -1)), FP8_MAX))
+    s16 = fp16_round(safe_scale(_nan_amax(blocks, (-2, -1)), qmax))
     with np.errstate(all="ignore"):
         normalized = (blocks / s16.astype(_F32)).astype(_F32)
-        sat = float(np.mean(np.abs(normalized) > FP8_MAX))
-        c = np.where(normalized > FP8_MAX, _F32(FP8_MAX), normalized)
-        c = np.where(c < -FP8_MAX, _F32(-FP8_MAX), c)
-    payload = e4m3_encode(c).reshape(source.shape)
-    return QuantizedCheckpoint(payload, s16.squeeze(-1).squeeze(-1), "vblock", 32, sat)
+        sat = float(np.mean(np.abs(normalized) > qmax))
+        c = np.where(normalized > qmax, _F32(qmax), normalized)
+        c = np.where(c < -qmax, _F32(-qmax), c)
+    if int8:
+        with np.errstate(invalid="ignore"):
+            payload = np.rint(c).astype(np.int8).reshape(source.shape)
+    else:
+        payload = e4m3_encode(c).reshape(source.shape)
+    return QuantizedCheckpoint(payload, s16.squeeze(-1).squeeze(-1), gran, 32, sat)
 
 
 # --------------------------------------------------------------------------

@@ -120,3 +120,47 @@ def test_quantize_near_midpoints(cuda_device, divisor):
     q = gdnr.quantize_checkpoint(to_dev(s, torch.float32), quant_divisor=divisor)
     ref = O.quantize_vblock32(s, divisor=divisor)
     assert compare_payload(to_np(q.payload), ref.payload) == 0
+
+
+def int8_edge_state(rng, B=3, HV=4):
+    """Finite edge cases for the int8 codec (NaN codes are host-defined)."""
+    s = (0.05 * rng.standard_normal((B, HV, 128, 128))).astype(np.float32)
+    s[0, 0, 0:32] = 0.0  # amax 0 -> scale 1
+    s[0, 1, 32:64] *= np.float32(1e-6)  # fp16 scale underflow -> x/0
+    s[0, 2, 64:96] *= np.float32(1e9)  # fp16 scale overflow
+    # exact ties of x / scale: amax = 127/8 -> scale 1/8, x = (k + 1/2)/8
+    t = (rng.integers(-126, 126, (32, 128)).astype(np.float32) + np.float32(0.5)) * np.float32(0.125)
+    t[0, 0] = np.float32(127.0 * 0.125)
+    s[1, 0, 0:32] = t
+    s[2, 3, 32:64, 7] = np.float32(1e30)  # one huge value: everything else rounds to 0
+    return s
+
+
+@pytest.mark.parametrize("divisor", ["oracle", "rounded"])
+@pytest.mark.parametrize("scale_dtype", [torch.float16, torch.float32])
+def test_quantize_int8_bit_exact(cuda_device, divisor, scale_dtype):
+    """granularity 'vblock_int8' (ref.py:44-47, :96-97): int8 codes and scales
+    bit-exact with the oracle, ties of x/scale rounded to even."""
+    rng = np.random.default_rng(44)
+    s = int8_edge_state(rng)
+    q = gdnr.quantize_checkpoint(to_dev(s, torch.float32), "vblock_int8", scale_dtype=scale_dtype,
+                                 quant_divisor=divisor)
+    ref = O.quantize_vblock32(s, divisor=divisor, int8=True)
+    assert q.payload.dtype == torch.int8 and q.granularity == "vblock_int8"
+    assert np.array_equal(q.payload.cpu().numpy(), ref.payload)
+    got_scale = q.scale.float().cpu().numpy()
+    assert np.array_equal(np.nan_to_num(got_scale, posinf=7e7), np.nan_to_num(ref.scale.astype(np.float32), posinf=7e7))
+    assert q.saturation_fraction == pytest.approx(ref.saturation_fraction, rel=1e-6, abs=1e-12)
+    # the tie block really has ties, and they went to even
+    y = (s[1, 0, 0:32] / np.float32(0.125)).ravel()[1:]  # [0, 0] is the amax element
+    assert np.all(np.abs(y - np.floor(y)) == 0.5)
+
+
+def test_dequantize_int8_exact(cuda_device):
+    rng = np.random.default_rng(45)
+    s = (0.05 * rng.standard_normal((2, 8, 128, 128))).astype(np.float32)
+    ref = O.quantize_checkpoint(s, "vblock_int8", 32)
+    ck = gdnr.QuantizedCheckpoint(to_dev(ref.payload, torch.int8), to_dev(ref.scale, torch.float16),
+                                  "vblock_int8", 32, 0.0)
+    d = gdnr.dequantize_checkpoint(ck)
+    assert np.array_equal(to_np(d), O.dequantize_checkpoint(ref))
