@@ -1257,6 +1257,13 @@ __device__ __forceinline__ void s5_add_release(uint32_t* p, uint32_t v) {
   asm volatile("red.release.cta.shared::cta.add.u32 [%0], %1;" ::"r"(smem_addr(p)), "r"(v) : "memory");
 }
 
+// add with acquire-release semantics; returns the previous value
+__device__ __forceinline__ uint32_t s5_add_acq_rel(uint32_t* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], %2;" : "=r"(old) : "r"(smem_addr(p)), "r"(v) : "memory");
+  return old;
+}
+
 // Bounded wait (by lane 0, broadcast) for a shared counter to reach `target`.
 __device__ __forceinline__ bool s5_warp_wait_count(const uint32_t* c, uint32_t target, uint32_t* err,
                                                    volatile int* abort, int lane) {
@@ -1697,23 +1704,23 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
           }
         }
         __syncwarp();
+        int last = 0;
         if (ok) {
           for (;;) {
             const int t = s5_claim(&vword[s], i, NT, lane);
             if (t < 0) break;
             s5_flush_task<FUSED, HPU>(p, smem, lay, U, s, ccw, code, t, ost, stash, lane);
-            if (lane == 0) s5_add_release(&vdone[s], 1u);
+            if (lane == 0 && s5_add_acq_rel(&vdone[s], 1u) == uint32_t(NT - 1)) last = 1;
           }
         }
-        // the first readout warp stores the unit once every task is done; the
-        // others release the stage now (it is reloaded only after all have)
-        if (rw == 0) {
-          s5_warp_wait_count(&vdone[s], uint32_t(NT), p.err, abort, lane);
-          if (lane == 0 && *abort == 0) {
-            s5_tma_store4(&ck_map, sb + lay.ck, 0, 0, U.hv0, U.s);
-            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-            asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-          }
+        // the warp that finished the unit's last task stores it (the other
+        // tasks' released rows are visible to it through its acquire-release
+        // add); the others release the stage now (it is reloaded only after
+        // all have)
+        if (__shfl_sync(0xffffffffu, last, 0) && lane == 0 && *abort == 0) {
+          s5_tma_store4(&ck_map, sb + lay.ck, 0, 0, U.hv0, U.s);
+          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+          asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
         }
       } else if (mma) {
         float sc = sc_pref;
