@@ -99,7 +99,7 @@ __host__ __device__ inline S5Geo s5_geo(int H, int HV, int L) {
 //        doubles as the chain's q-split / Gram scratch before T is written)
 //   [ost: 128 floats] x S5_NRW
 struct S5Layout {
-  uint32_t full, empty, kfull, cbar, rbar, abort, vword, vdone, mmab, tmem, table;
+  uint32_t full, empty, kfull, cbar, rbar, abort, vword, vdone, mmab, tmem, table, tdone;
   uint32_t stage0, stage_bytes, ck, vr;
   uint32_t kbuf0;
   uint32_t res0, res_bytes, t8, cb, cf, misc, vnew;
@@ -122,6 +122,7 @@ __host__ __device__ inline S5Layout s5_layout(const S5Geo& g, int max_units, boo
   s.mmab = smem_take(o, S5_NS * 8);
   s.tmem = smem_take(o, 16);
   s.table = smem_take(o, uint32_t(max_units) * 4u);
+  s.tdone = smem_take(o, uint32_t(max_units) * 4u);
   o = (o + 1023u) & ~1023u;
   s.stage0 = o;
   s.ck = 0;
@@ -1368,6 +1369,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
   uint32_t* vdone = reinterpret_cast<uint32_t*>(smem + lay.vdone);  // flush tasks finished per stage
   uint64_t* mmab = reinterpret_cast<uint64_t*>(smem + lay.mmab);    // tensor-core readout of a stage done
   int* table = reinterpret_cast<int*>(smem + lay.table);
+  uint32_t* tdone = reinterpret_cast<uint32_t*>(smem + lay.tdone);  // flush tasks done per unit (tensor-memory readout)
   const bool aligned = (smem_addr(smem) & 1023u) == 0;  // swizzled TMA boxes need 1024-byte alignment
   const uint32_t box_bytes = uint32_t(geo.rb) * 256u;
   const uint32_t ck_bytes = uint32_t(HPU) * 16384u;
@@ -1492,6 +1494,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
     if (!FUSED && s5_skip(code) && p.flush_hint == GDNR_FLUSH_NONE && U.h == 0 && U.pp == 0)
       atomicOr(p.err, GDNR_DEVERR_BAD_HINT);
     table[ti] = code;
+    tdone[ti] = 0u;
   }
   // The table is for the producer and the readout warps: the readout warps
   // sync on it (barrier 1) and signal it to the producer (barrier 2), which
@@ -1681,42 +1684,17 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       }
       const bool mok = s5_warp_wait(&mmab[s], par, p.err, abort, lane);
       if (flush) {
-        // The unit's 8 vblock tasks among the readout warps, then one tensor-map
-        // store.  The first warp here publishes the tasks: its stage has landed,
-        // so the stage's previous unit and its tasks are finished.  It parks the
-        // task word in a resetting state (no claim succeeds) while it clears the
-        // done count; the other warps wait out that state.
-        constexpr int NT = 4 * HPU;
-        if (lane == 0) {
-          const uint32_t parked = (uint32_t(i) << 8) | 0xffu;
-          uint32_t w = s5_ld_acquire(&vword[s]);
-          if ((w >> 8) != uint32_t(i) && atomicCAS(&vword[s], w, parked) == w) {
-            vdone[s] = 0u;
-            __threadfence_block();
-            atomicExch(&vword[s], uint32_t(i) << 8);
-          } else {
-            const uint64_t t0 = globaltimer_ns();
-            for (uint32_t it = 0; it < WAIT_LIMIT_ITERS; ++it) {
-              w = s5_ld_acquire(&vword[s]);
-              if ((w >> 8) == uint32_t(i) && w != parked) break;
-              if ((it & 63u) == 0 && (*abort || globaltimer_ns() - t0 > WAIT_LIMIT_NS)) break;
-            }
-          }
-        }
-        __syncwarp();
+        // The unit's 4 x 2 vblock tasks, one per readout warp (task rw), then
+        // one tensor-map store by the warp whose acquire-release increment of
+        // the unit's done count completes it (the other tasks' released rows
+        // are visible to it); the others release the stage now (it is reloaded
+        // only after all have).
+        static_assert(4 * HPU == S5_NRW, "one flush task per readout warp");
         int last = 0;
         if (ok) {
-          for (;;) {
-            const int t = s5_claim(&vword[s], i, NT, lane);
-            if (t < 0) break;
-            s5_flush_task<FUSED, HPU>(p, smem, lay, U, s, ccw, code, t, ost, stash, lane);
-            if (lane == 0 && s5_add_acq_rel(&vdone[s], 1u) == uint32_t(NT - 1)) last = 1;
-          }
+          s5_flush_task<FUSED, HPU>(p, smem, lay, U, s, ccw, code, rw, ost, stash, lane);
+          if (lane == 0 && s5_add_acq_rel(&tdone[i], 1u) == uint32_t(S5_NRW - 1)) last = 1;
         }
-        // the warp that finished the unit's last task stores it (the other
-        // tasks' released rows are visible to it through its acquire-release
-        // add); the others release the stage now (it is reloaded only after
-        // all have)
         if (__shfl_sync(0xffffffffu, last, 0) && lane == 0 && *abort == 0) {
           s5_tma_store4(&ck_map, sb + lay.ck, 0, 0, U.hv0, U.s);
           asm volatile("cp.async.bulk.commit_group;" ::: "memory");
