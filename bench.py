@@ -412,8 +412,10 @@ def run_ours(args, world, rank, local):
     e2e = run_e2e(args, layers, step_inputs, pos, stream, world) if args.e2e_steps > 0 else None
 
     core = None
+    widened = None
     if not args.no_core and world == 1:
         core = run_core(args, device, stream)
+        widened = run_widened(args, device, stream)
 
     del graphs
     torch.cuda.synchronize()
@@ -464,6 +466,8 @@ def run_ours(args, world, rank, local):
         line["e2e"] = e2e
     if core is not None:
         line["core_replay"] = core
+    if widened is not None:
+        line.update(widened)
     if cpu_line is not None:
         line["cpu_baseline"] = cpu_line
     print(json.dumps(line), flush=True)
@@ -563,6 +567,91 @@ def run_e2e(args, layers, step_inputs, pos, stream, world):
             "path": "gdnr.gdn_fused_step (Python) -> libgdnr C ABI, captured per ring position in a CUDA graph "
                     "with, per layer, one pinned H2D copy of the packed raw inputs and one pinned D2H copy of the "
                     "output on forked streams (copies overlap other layers' kernels)"}
+
+
+def _graph_us(fn, stream, reps):
+    """Mean device time of ``fn`` (captured once in a CUDA graph) over ``reps`` replays."""
+    import torch
+
+    with torch.cuda.stream(stream):
+        fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        fn()
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            g.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            g.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    del g
+    return 1e3 * e0.elapsed_time(e1) / reps
+
+
+def run_widened(args, device, stream):
+    """The rows beyond the core path, measured like it: the packed decode
+    (serving call over a slot pool, one random slot per batch row) through a
+    whole ring cycle, and the vblock32 codec (E4M3 and INT8) on a BASELINE-size
+    state."""
+    import torch
+
+    import gdnr
+    from gdnr import inputs as gin
+
+    B, L, NL = args.batch, args.ring, min(args.layers, 4)
+    S = 2 * B + 1
+    gen = torch.Generator().manual_seed(args.seed + 17)
+    pools = []
+    for li in range(NL):
+        pool = gdnr.ReplayState.allocate(S, H, HV, L, device=device, scale_dtype=torch.float32,
+                                         gate_dtype=torch.float32)
+        raw = gin.raw_step_inputs(S, L, seed=(args.seed * 1000 + li) * 4096 + 7, device=device)
+        pool.load_state(raw["state"])
+        idx = (torch.randperm(S - 1, generator=gen)[:B] + 1).to(torch.int32).to(device)
+        posf = [torch.zeros(S, dtype=torch.int32, device=device).index_fill_(0, idx.long(), s) for s in range(L)]
+        inputs = [(raw["mixed_qkv"][:B, s].contiguous(), raw["a"][:B, s].contiguous(), raw["b"][:B, s].contiguous())
+                  for s in range(L)]
+        pools.append((pool, idx, posf, inputs, raw["a_log"], raw["dt_bias"],
+                      torch.empty(B, 1, HV, KD, dtype=torch.bfloat16, device=device)))
+        del raw
+    total = 0.0
+    for s in range(L):
+        def step(s=s):
+            for pool, idx, posf, inputs, a_log, dt_bias, out in pools:
+                pool.pos.copy_(posf[s])
+                m, a, b = inputs[s]
+                gdnr.fused_recurrent_gated_delta_rule_packed_decode(
+                    m, a, b, a_log, dt_bias, KD ** -0.5, pool, out, idx, flush_hint=flush_hint_for(s, L))
+        total += _graph_us(step, stream, 10) / NL
+    packed_us = total / L
+    del pools
+    res = {"packed_decode": {
+        "us_per_layer_step": packed_us, "steps_seq_per_s": B / (packed_us * 1e-6),
+        "workload": f"fused_recurrent_gated_delta_rule_packed_decode: batch {B} rows on random slots of a "
+                    f"{S}-slot pool (slot 0 null), {NL} layers, one ring cycle (flush at position {L - 1}); "
+                    "includes the wrapper's position copies"}}
+    # codec: [B, HV, V, K] float32 state (134 MB > L2)
+    state = torch.randn(B, HV, KD, KD, generator=gen).mul_(0.05).to(device)
+    codec = {}
+    n = state.numel()
+    for gran, pdt, pbytes in (("vblock", torch.float8_e4m3fn, 1), ("vblock_int8", torch.int8, 1)):
+        payload = torch.empty(B, HV, KD, KD, dtype=pdt, device=device)
+        scale = torch.empty(B, HV, KD // 32, dtype=torch.float16, device=device)
+        q_us = _graph_us(lambda: gdnr.quantize_checkpoint(state, gran, payload=payload, scale=scale,
+                                                          compute_saturation=False), stream, 20)
+        ck = gdnr.QuantizedCheckpoint(payload, scale, gran, 32, 0.0)
+        out = torch.empty_like(state)
+        d_us = _graph_us(lambda: gdnr.dequantize_checkpoint(ck, out=out), stream, 20)
+        moved = n * (4 + pbytes) + scale.numel() * 2
+        codec[gran] = {"quantize_us": q_us, "quantize_GB_s": moved / (q_us * 1e-6) / 1e9,
+                       "dequantize_us": d_us, "dequantize_GB_s": moved / (d_us * 1e-6) / 1e9}
+    codec["shape"] = [B, HV, KD, KD]
+    res["codec"] = codec
+    return res
 
 
 def run_core(args, device, stream):
