@@ -416,6 +416,7 @@ def run_ours(args, world, rank, local):
     if not args.no_core and world == 1:
         core = run_core(args, device, stream)
         widened = run_widened(args, device, stream)
+        widened["comparators"] = run_comparators(args, device, stream, 1e3 * ms_max / launches)
 
     del graphs
     torch.cuda.synchronize()
@@ -651,6 +652,67 @@ def run_widened(args, device, stream):
                        "dequantize_us": d_us, "dequantize_GB_s": moved / (d_us * 1e-6) / 1e9}
     codec["shape"] = [B, HV, KD, KD]
     res["codec"] = codec
+    return res
+
+
+def run_comparators(args, device, stream, ours_us):
+    """Same-box comparators for the reference's speed-up table
+    (bench_gdn_vs_production.py:279-292, bench_gdn_full_contract.py:225-308):
+    the production operator the reference swaps out -- vLLM's FLA
+    ``fused_recurrent_gated_delta_rule_packed_decode`` (a Triton kernel shipped
+    in this image; bf16 state read-modify-write through ``ssm_state_indices``)
+    -- and this library's sm_100a bf16 read-modify-write step (kern.py:245-341),
+    both at the bench's batch over 4 layers of state (> 2x L2).  ``ours_us`` is
+    the cycle-amortised fused step per layer measured above."""
+    import torch
+
+    import gdnr
+    from gdnr import inputs as gin
+
+    B, NL = args.batch, 4
+    state_bytes = 2 * B * HV * KD * KD * 2  # bf16 state read + write per layer step
+    res = {"ours_us_per_layer_step": ours_us}
+    sets = []
+    for li in range(NL):
+        d = gin.replay_ring_inputs(B, 1, seed=args.seed * 11 + li, device=device)
+        sets.append((d["state"].to(torch.bfloat16), d["q"], d["k"][:, 0].contiguous(), d["v"][:, 0].contiguous(),
+                     d["g"][:, 0].contiguous(), d["beta"][:, 0].contiguous()))
+        del d
+
+    def bf16_step():
+        for st, q, k, v, g, be in sets:
+            gdnr.gdn_bf16_step(st, q, k, v, g, be)
+    us = _graph_us(bf16_step, stream, 20) / NL
+    res["bf16_step_sm100a"] = {"us_per_layer_step": us, "state_GB_s": state_bytes / (us * 1e-6) / 1e9,
+                               "speedup_of_ours": us / ours_us}
+    del sets
+    try:
+        from vllm.model_executor.layers.fla.ops.fused_recurrent import \
+            fused_recurrent_gated_delta_rule_packed_decode as fla_decode
+    except Exception as e:  # the comparator is optional: the image may lack vLLM or Triton
+        res["fla_packed_decode"] = {"unavailable": f"{type(e).__name__}: {e}"[:200]}
+        return res
+    gen = torch.Generator().manual_seed(args.seed + 23)
+    layers = []
+    for li in range(NL):
+        raw = gin.raw_step_inputs(B, 1, seed=(args.seed * 1000 + li) * 4096 + 11, device=device)
+        pool = torch.zeros(B + 1, HV, KD, KD, dtype=torch.bfloat16, device=device)  # slot 0 = null
+        pool[1:] = raw["state"].to(torch.bfloat16)
+        idx = (torch.randperm(B, generator=gen) + 1).to(torch.int32).to(device)
+        layers.append((raw["mixed_qkv"][:, 0].contiguous(), raw["a"][:, 0].contiguous(), raw["b"][:, 0].contiguous(),
+                       raw["a_log"], raw["dt_bias"], pool, torch.empty(B, 1, HV, KD, dtype=torch.bfloat16,
+                                                                       device=device), idx))
+        del raw
+
+    def fla_step():
+        for m, a, b, al, db, pool, out, idx in layers:
+            fla_decode(m, a, b, al, db, KD ** -0.5, pool, out, idx, use_qk_l2norm_in_kernel=True)
+    us = _graph_us(fla_step, stream, 20) / NL
+    res["fla_packed_decode"] = {
+        "us_per_layer_step": us, "state_GB_s": state_bytes / (us * 1e-6) / 1e9, "speedup_of_ours": us / ours_us,
+        "workload": f"vLLM FLA packed decode (Triton, JIT-compiled for this GPU), batch {B}, bf16 state pool of "
+                    f"{B + 1} slots, random slot order, {NL} layers"}
+    del layers
     return res
 
 

@@ -376,7 +376,9 @@ __device__ __forceinline__ bool s5_flush(int code) { return (code >> 17) & 1; }
 
 // A unit: batch row b, key head h, pair pp of its value heads (first value head
 // hv0); s: the row's state slot -- b, or under packed decode state_indices[b],
-// with -1 for the null slot 0 and -2 for an index outside [0, S) (both skipped).
+// with -1 for a null slot (index <= 0, the production op's NULL_BLOCK_ID test,
+// fused_recurrent.py:292-297) and -2 for an index >= S (both skipped; their
+// output rows are written as zeros).
 struct S5Unit {
   int b, h, pp, hv0, s;
 };
@@ -393,7 +395,7 @@ __device__ __forceinline__ S5Unit s5_unit(int u, const StepParams& p, int G, con
   x.s = x.b;
   if constexpr (SIDX) {
     const int v = __ldg(p.sidx + int64_t(x.b) * p.si_s);
-    x.s = v == 0 ? -1 : ((v < 0 || v >= p.S) ? -2 : v);
+    x.s = v <= 0 ? -1 : (v >= p.S ? -2 : v);
   }
   return x;
 }
@@ -1489,6 +1491,13 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
     const int code = s5_code<FUSED>(raw0, raw1, L, FLUSH);
     if (FUSED && s5_n(code) == 0 && U.s >= 0 && U.h == 0 && U.pp == 0) atomicOr(p.err, GDNR_DEVERR_BAD_POS);
     if (U.s == -2 && U.h == 0 && U.pp == 0) atomicOr(p.err, GDNR_DEVERR_BAD_SLOT);
+    if constexpr (SIDX) {
+      if (U.s < 0) {  // null / bad slot: a zero output row, as the production op stores
+        for (int e = 0; e < geo.hpu; ++e)
+          for (int r = 0; r < VD; ++r)
+            store_scalar(p.out, int64_t(U.b) * p.o_sb + int64_t(U.hv0 + e) * p.o_sh + int64_t(r) * p.o_sv, p.o_dt, 0.f);
+      }
+    }
     if (s5_n(code) > 0 && s5_skip(code) && p.flush_hint == GDNR_FLUSH_NONE && U.h == 0 && U.pp == 0)
       atomicOr(p.err, GDNR_DEVERR_BAD_HINT);
     if (!FUSED && s5_skip(code) && p.flush_hint == GDNR_FLUSH_NONE && U.h == 0 && U.pp == 0)

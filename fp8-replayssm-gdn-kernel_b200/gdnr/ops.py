@@ -327,9 +327,10 @@ def fused_recurrent_gated_delta_rule_packed_decode(
     of the bf16 state cache ``[slots, HV, V, K]``.  Batch row ``i`` runs one
     fused decode step (prep, ring append, replay, and the flush when the slot's
     ring position is ``L-1``) on slot ``ssm_state_indices[i]`` of every state
-    tensor and advances that slot's ring position.  Slot 0 is the null slot
-    (padding rows): nothing is read or written for it and its ``out`` rows are
-    left as they are; an index outside ``[0, slots)`` is treated the same way
+    tensor and advances that slot's ring position.  An index ``<= 0`` is the
+    null slot (padding rows, the production kernel's ``NULL_BLOCK_ID`` test):
+    no state is read or written for it and its ``out`` rows are set to zero,
+    as the production op does; an index ``>= slots`` is treated the same way
     and reported in the device error word as ``GDNR_DEVERR_BAD_SLOT``.
     ``out`` is ``[B, 1, HV, V]`` (or ``[B, HV, V]``).  q and k are always
     L2-normalised in the kernel and the output is scaled by ``K^-1/2``:

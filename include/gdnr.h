@@ -58,7 +58,7 @@ typedef enum {
 #define GDNR_DEVERR_WAIT_TIMEOUT 0x1u /* a bounded mbarrier wait gave up */
 #define GDNR_DEVERR_BAD_POS 0x2u      /* fused step: pos[b] outside [0, L) */
 #define GDNR_DEVERR_BAD_HINT 0x4u     /* flush_hint NONE but a sequence's ring was full */
-#define GDNR_DEVERR_BAD_SLOT 0x8u     /* packed decode: state_indices[i] outside [0, slots) */
+#define GDNR_DEVERR_BAD_SLOT 0x8u     /* packed decode: state_indices[i] >= slots */
 
 /* flush_hint: what the caller knows about which sequences flush in this call */
 #define GDNR_FLUSH_AUTO 0 /* unknown: every head is checked on the device */
@@ -178,9 +178,10 @@ int gdnr_fused_step(const gdnr_step_args* args, void* stream);
  * as the reference drives it (prototype/bench_gdn_full_contract.py:157-170; contract notes
  * findings.md:37-45), with the bf16 state cache [slots,HV,V,K] replaced by the FP8
  * checkpoint + ring pool below: batch row i uses slot state_indices[i] of every state
- * tensor.  Slot 0 is the null slot (the serving engine's padding): that row is skipped --
- * no state is read or written and its out rows are left as they are.  An index outside
- * [0, slots) is skipped the same way and reported as GDNR_DEVERR_BAD_SLOT.  q and k are
+ * tensor.  An index <= 0 is the null slot (the serving engine's padding; the production
+ * kernel's NULL_BLOCK_ID test, vLLM fused_recurrent.py:292-297): no state is read or written
+ * for that row and its out rows are written as zeros, as the production op does.  An index
+ * >= slots is treated the same way and reported as GDNR_DEVERR_BAD_SLOT.  q and k are
  * always L2-normalised in the kernel and the output is scaled by K^-1/2: the production
  * call's use_qk_l2norm_in_kernel and scale arguments must be 1 and K^-1/2.  The step is
  * gdnr_fused_step's (prep + ring append + replay, and the flush when a slot's pos is L-1);

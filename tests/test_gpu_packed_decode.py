@@ -1,7 +1,8 @@
 """gdnr_packed_decode (the serving engine's decode call over a state-slot pool,
 bench_gdn_full_contract.py:157-170 call shape) against gdn_fused_step on the
-same slots gathered into a contiguous batch: bit-identical outputs and state,
-padding rows (null slot 0) and rows with an out-of-range slot left untouched."""
+same slots gathered into a contiguous batch: bit-identical outputs and state;
+null rows (index <= 0, the production op's NULL_BLOCK_ID test) and rows with an
+index >= slots get zero outputs and leave every slot's state untouched."""
 
 import numpy as np
 import pytest
@@ -50,8 +51,8 @@ def test_packed_decode_matches_fused_step_on_gathered_slots(cuda_device, heads, 
     rng = np.random.default_rng(31)
     H, HV = heads
     S, L = 7, 4
-    rows = [3, 0, 5, 1, 6]  # row 1 is padding (null slot 0)
-    active = [i for i, s in enumerate(rows) if s != 0]
+    rows = [3, 0, 5, 1, 6, -1]  # rows 1 and 5 are padding (null: index <= 0)
+    active = [i for i, s in enumerate(rows) if s > 0]
     pool, a_log, dt_bias = make_pool(rng, S, H, HV, L)
     ref = gather(pool, [rows[i] for i in active])
     untouched = {name: raw(getattr(pool, name))[[0, 2, 4]].clone() for name in STATE}
@@ -70,7 +71,7 @@ def test_packed_decode_matches_fused_step_on_gathered_slots(cuda_device, heads, 
         ref.pos.copy_(nxt)
         torch.cuda.synchronize()
         assert torch.equal(out[active].view(len(active), HV, 128), want)
-        assert torch.all(out[1] == 7.0)  # padding row left as it was
+        assert torch.all(out[1] == 0) and torch.all(out[5] == 0)  # padding rows: zeros, as the production op
     assert int(err.item()) == 0
     for name in STATE:
         assert torch.equal(raw(getattr(pool, name))[[rows[i] for i in active]], raw(getattr(ref, name))), name
@@ -91,7 +92,7 @@ def test_packed_decode_out_of_range_slot_is_reported_and_skipped(cuda_device):
         to_dev(a_log, torch.float32), to_dev(dt_bias, torch.float32), 128 ** -0.5, pool, out, sidx, error_flag=err)
     torch.cuda.synchronize()
     assert int(err.item()) & gdnr._lib.DEVERR_BAD_SLOT
-    assert torch.all(out[1] == 5.0) and not torch.all(out[0] == 5.0)
+    assert torch.all(out[1] == 0) and not torch.all(out[0] == 0)
     assert int(pool.pos[2]) == (int(before["pos"][2]) + 1) % L
     for s in (0, 1, 3):
         for name in STATE:
