@@ -57,6 +57,8 @@ def parse_args():
     ap.add_argument("--profile", type=int, default=None, metavar="POS",
                     help="profiling driver for ncu: a few untimed launches of one layer's step at ring position "
                          "POS (no timing, no JSON line)")
+    ap.add_argument("--checkpoint", choices=["e4m3", "int8"], default="e4m3",
+                    help="checkpoint payload of the --profile driver (int8: the 'vblock_int8' option)")
     return ap.parse_args()
 
 
@@ -272,7 +274,7 @@ def run_reference(args, world, rank):
 
 # ---------------------------------------------------------------- GPU arm
 
-def build_stack(args, device, rank: int = 0, world: int = 1):
+def build_stack(args, device, rank: int = 0, world: int = 1, checkpoint_dtype=None):
     """This rank's shard of the job: sequences ShardPlan(B * world, world).local(rank)
     of every layer, each rank with its own seeded inputs and state (weak scaling)."""
     import torch
@@ -287,7 +289,8 @@ def build_stack(args, device, rank: int = 0, world: int = 1):
     layers, step_inputs = [], []
     for li in range(NL):
         st = gdnr.ReplayState.allocate(B, H, HV, L, device=device, scale_dtype=torch.float32,
-                                       gate_dtype=torch.float32)
+                                       gate_dtype=torch.float32,
+                                       checkpoint_dtype=checkpoint_dtype or torch.float8_e4m3fn)
         raw = gin.raw_step_inputs(B, L, seed=(args.seed * 1000 + li) * 4096 + shard.start, device=device)
         st.load_state(raw["state"])
         layers.append({"state": st, "a_log": raw["a_log"], "dt_bias": raw["dt_bias"],
@@ -325,7 +328,8 @@ def run_profile(args, local):
 
     args.layers = 1
     device = torch.device("cuda", local)
-    layers, step_inputs, pos, err = build_stack(args, device)
+    layers, step_inputs, pos, err = build_stack(
+        args, device, checkpoint_dtype=torch.int8 if args.checkpoint == "int8" else None)
     s = args.profile % args.ring
     for _ in range(3):
         launch_position(layers, step_inputs, pos, err, s)
@@ -595,9 +599,9 @@ def _graph_us(fn, stream, reps):
 
 def run_widened(args, device, stream):
     """The rows beyond the core path, measured like it: the packed decode
-    (serving call over a slot pool, one random slot per batch row) through a
-    whole ring cycle, and the vblock32 codec (E4M3 and INT8) on a BASELINE-size
-    state."""
+    (serving call over a slot pool, one random slot per batch row) and the
+    fused step on an INT8 checkpoint, each through a whole ring cycle, and the
+    vblock32 codec (E4M3 and INT8) on a BASELINE-size state."""
     import torch
 
     import gdnr
@@ -635,6 +639,34 @@ def run_widened(args, device, stream):
         "workload": f"fused_recurrent_gated_delta_rule_packed_decode: batch {B} rows on random slots of a "
                     f"{S}-slot pool (slot 0 null), {NL} layers, one ring cycle (flush at position {L - 1}); "
                     "includes the wrapper's position copies"}}
+    # the INT8 checkpoint option ("vblock_int8") through the fused step, one ring cycle
+    layers8 = []
+    for li in range(NL):
+        st = gdnr.ReplayState.allocate(B, H, HV, L, device=device, scale_dtype=torch.float32,
+                                       gate_dtype=torch.float32, checkpoint_dtype=torch.int8)
+        raw = gin.raw_step_inputs(B, L, seed=(args.seed * 1000 + li) * 4096 + 13, device=device)
+        st.load_state(raw["state"])
+        inputs = [(raw["mixed_qkv"][:, s].contiguous(), raw["a"][:, s].contiguous(), raw["b"][:, s].contiguous())
+                  for s in range(L)]
+        posf = [torch.full((B,), s, dtype=torch.int32, device=device) for s in range(L)]
+        layers8.append((st, inputs, posf, raw["a_log"], raw["dt_bias"],
+                        torch.empty(B, HV, KD, dtype=torch.bfloat16, device=device)))
+        del raw
+    total = 0.0
+    for s in range(L):
+        def step8(s=s):
+            for st, inputs, posf, a_log, dt_bias, out in layers8:
+                st.pos.copy_(posf[s])
+                m, a, b = inputs[s]
+                st.step(m, a, b, a_log, dt_bias, out=out, flush_hint=flush_hint_for(s, L))
+        total += _graph_us(step8, stream, 10) / NL
+    int8_us = total / L
+    del layers8
+    res["int8_checkpoint_step"] = {
+        "us_per_layer_step": int8_us, "steps_seq_per_s": B / (int8_us * 1e-6),
+        "workload": f"gdn_fused_step on an int8 ('vblock_int8') checkpoint, batch {B}, L={L}, {NL} layers, one "
+                    "ring cycle (flush re-quantises to int8); one-CTA-per-head kernel with the integer "
+                    "tensor-core readout; includes a position copy per layer"}
     # codec: [B, HV, V, K] float32 state (134 MB > L2)
     state = torch.randn(B, HV, KD, KD, generator=gen).mul_(0.05).to(device)
     codec = {}

@@ -129,9 +129,8 @@ namespace {
 const int DT_F32[] = {GDNR_F32};
 const int DT_I32[] = {GDNR_I32};
 const int DT_BF16[] = {GDNR_BF16};
-const int DT_E4M3[] = {GDNR_E4M3};
 const int DT_PAYLOAD[] = {GDNR_E4M3, GDNR_I8};
-const int DT_CK[] = {GDNR_E4M3, GDNR_F32};
+const int DT_CK[] = {GDNR_E4M3, GDNR_F32, GDNR_I8};
 const int DT_SCALE[] = {GDNR_F16, GDNR_F32};
 const int DT_ACT[] = {GDNR_BF16, GDNR_F32};
 const int DT_GATE[] = {GDNR_F32, GDNR_BF16, GDNR_F16};
@@ -166,8 +165,11 @@ int validate_state(const gdnr_tensor& ck, const gdnr_tensor& sc, const gdnr_tens
   CHECK(check_tensor(gr, "g_ring", 3, DT_GATE, 3, want_g));
   CHECK(check_tensor(br, "beta_ring", 3, DT_GATE, 3, want_g));
   const int64_t want_ck[4] = {B, HV, V, K};
-  CHECK(check_tensor(ck, "checkpoint", 4, DT_CK, 2, want_ck));
+  CHECK(check_tensor(ck, "checkpoint", 4, DT_CK, 3, want_ck));
   f32ck = ck.dtype == GDNR_F32;
+  p.ck_i8 = ck.dtype == GDNR_I8 ? 1 : 0;
+  if (p.ck_i8 && L > STEP2_MAX_L)
+    return set_error(GDNR_ERR_UNSUPPORTED, "INT8 checkpoint: ring length L=%lld above %d", (long long)L, STEP2_MAX_L);
   CHECK(check_inner_contiguous(kr, "k_ring"));
   CHECK(check_inner_contiguous(vr, "v_ring"));
   CHECK(check_inner_contiguous(ck, "checkpoint"));
@@ -378,7 +380,7 @@ int gdnr_packed_decode(const gdnr_packed_decode_args* a, void* stream) {
   bool f32ck = false;
   int group = 0;
   CHECK(validate_state(a->checkpoint, a->scale, a->k_ring, a->v_ring, a->g_ring, a->beta_ring, p, f32ck, group));
-  if (f32ck) return set_error(GDNR_ERR_UNSUPPORTED, "packed decode: E4M3 checkpoints only");
+  if (f32ck || p.ck_i8) return set_error(GDNR_ERR_UNSUPPORTED, "packed decode: E4M3 checkpoints only");
   const int32_t slots = p.B;
   CHECK(check_tensor(a->mixed_qkv, "mixed_qkv", 2, DT_ACT, 2, nullptr));
   const int64_t B = a->mixed_qkv.shape[0];

@@ -51,18 +51,10 @@ __global__ void __launch_bounds__(256) quantize_kernel(const __grid_constant__ C
   VScale vs;
   uint4 q;
   if (p.int8) {
-    const float s32 = am > 0.0f ? __fdiv_rn(am, 127.0f) : 1.0f;
-    vs.stored = __float2half_rn(s32);
-    vs.divisor = p.quant_rounded ? __half2float(vs.stored) : s32;
+    vs = vblock_scale_i8(am, p.quant_rounded);
     uint32_t w[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const float y = __fdiv_rn(x[i], vs.divisor);
-      sat += fabsf(y) > 127.0f ? 1u : 0u;
-      // NaN -> 0 (what the reference's float -> int8 cast gives on its host)
-      const float c = y != y ? 0.0f : fminf(fmaxf(rintf(y), -127.0f), 127.0f);
-      w[i >> 2] |= (uint32_t(__float2int_rn(c)) & 0xFFu) << (8 * (i & 3));
-    }
+    for (int i = 0; i < 16; ++i) w[i >> 2] |= quant_i8(x[i], vs.divisor, sat) << (8 * (i & 3));
     q = make_uint4(w[0], w[1], w[2], w[3]);
   } else {
     vs = vblock_scale(am, p.quant_rounded);

@@ -194,6 +194,27 @@ __device__ __forceinline__ VScale vblock_scale(float amax, int rounded_divisor) 
   return r;
 }
 
+// INT8 vblock scale ("vblock_int8", ref.py:44-47): amax / 127, 1 for a zero
+// (or NaN) amax, stored as f16; the divisor is the f32 value or, with
+// rounded_divisor, the stored f16 one.
+__device__ __forceinline__ VScale vblock_scale_i8(float amax, int rounded_divisor) {
+  const float s32 = (amax > 0.0f) ? __fdiv_rn(amax, 127.0f) : 1.0f;
+  VScale r;
+  r.stored = __float2half_rn(s32);
+  r.divisor = rounded_divisor ? __half2float(r.stored) : s32;
+  return r;
+}
+
+// INT8 code of x (ref.py:96-97): round-half-even of the IEEE quotient, clamped
+// to +-127; NaN gives 0 (the reference's float -> int8 cast on its host).
+// `sat` counts |x / divisor| > 127.
+__device__ __forceinline__ uint32_t quant_i8(float x, float divisor, uint32_t& sat) {
+  const float y = __fdiv_rn(x, divisor);
+  sat += fabsf(y) > 127.0f ? 1u : 0u;
+  const float c = y != y ? 0.0f : fminf(fmaxf(rintf(y), -127.0f), 127.0f);
+  return uint32_t(__float2int_rn(c)) & 0xFFu;
+}
+
 // x / divisor with IEEE division, then clamp to +-448 keeping NaN (torch.clamp
 // semantics, ref.py:99), returned as the pre-cast float.
 __device__ __forceinline__ float quant_normalize(float x, float divisor) {
@@ -412,6 +433,18 @@ __device__ __forceinline__ void mma16832_e4m3(float* d, const uint32_t* a, uint3
       "mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void mma16832_s8(int32_t* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// two int8 codes (low byte first) as f32 / f16x2 (exact: |code| <= 128)
+__device__ __forceinline__ float2 i8x2_to_f2(uint32_t w) {
+  return make_float2(float(int8_t(uint8_t(w))), float(int8_t(uint8_t(w >> 8))));
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {

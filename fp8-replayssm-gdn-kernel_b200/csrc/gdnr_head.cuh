@@ -18,6 +18,11 @@
 //        u_t = beta_t (v_t - r_t),  S_L = a_{n-1} S0 + W K,  W_t = u_t d_t
 //    (algebraically the token loop of ref.py:137-163), the readout, and the
 //    vblock32 re-quantisation (ref.py:40-106) written back in place.
+//  * I8 (template flag): the checkpoint holds int8 codes ("vblock_int8",
+//    ref.py:44-47, :96-97) instead of e4m3.  The readout then runs S_int8
+//    against T split into four int8 limbs on the integer tensor path (m16n8k32
+//    s8, exact s32 sums), with V^T c as a separate bf16 product; the flush
+//    reads the codes as f16 / f32 (exact) and re-quantises to int8.
 // a_t = prod_{m<=t} gamma_m, d_t = prod_{t<m<n} gamma_m, gamma_m = exp(g_m),
 // M[j][t] = prod_{j<m<=t} gamma_m (k_j . k_t).
 #pragma once
@@ -81,9 +86,26 @@ __device__ __forceinline__ void s0_afrag_f16(const uint8_t* s0, int rbase, int k
   a[3] = e4m3x2_to_f16x2(*reinterpret_cast<const uint16_t*>(p1 + 8 + 2 * t4));
 }
 
+// The same fragment from an int8 tile (codes are exact in f16)
+__device__ __forceinline__ void s0_afrag_i8f16(const uint8_t* s0, int rbase, int ks, int g8, int t4, uint32_t* a) {
+  const int r0 = rbase + g8, r1 = r0 + 8;
+  const uint8_t* p0 = s0 + uint32_t(r0) * 128u + 16u * uint32_t(ks ^ (r0 & 7));
+  const uint8_t* p1 = s0 + uint32_t(r1) * 128u + 16u * uint32_t(ks ^ (r1 & 7));
+  const uint32_t w[4] = {*reinterpret_cast<const uint16_t*>(p0 + 2 * t4), *reinterpret_cast<const uint16_t*>(p1 + 2 * t4),
+                         *reinterpret_cast<const uint16_t*>(p0 + 8 + 2 * t4),
+                         *reinterpret_cast<const uint16_t*>(p1 + 8 + 2 * t4)};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = i8x2_to_f2(w[i]);
+    a[i] = pack_f16x2(f.x, f.y);
+  }
+}
+
 // ============================================================== non-flush
 // Backward chain of one head in Gram form (one warp).  n: ring slots replayed.
-// Leaves in X: t8 (T as five e4m3 terms), cb (c as three bf16), misc[0] = 1/sigma.
+// Leaves in X: t8 (T as five e4m3 terms, or with I8 four int8 limbs), cb (c as
+// three bf16), misc[0] = 1/sigma.
+template <bool I8>
 __device__ __forceinline__ void head_chain(const HeadTile& T, const HeadScratch& X, int n, int lane) {
   const int g8 = lane >> 2, t4 = lane & 3;
   const uint16_t* kr_s = T.kr;
@@ -182,10 +204,33 @@ __device__ __forceinline__ void head_chain(const HeadTile& T, const HeadScratch&
     X.cb[16 + lane] = cmid;
     X.cb[32 + lane] = clo;
   }
-  // T -> 5 e4m3 terms: T sigma = sum_i term_i 16^-i, max |T sigma| in [128, 256)
   float m = fmaxf(fmaxf(fabsf(Tq[0]), fabsf(Tq[1])), fmaxf(fabsf(Tq[2]), fabsf(Tq[3])));
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if constexpr (I8) {
+    // T -> 4 int8 limbs: T sigma = sum_j limb_j 128^-j, max |T sigma| in [32, 64);
+    // x - rint(x) is exact, so every residual stays within +-64 after the x128
+    const float sig = pow2_scale_for(m) * (1.0f / 256.0f);
+    float x[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) x[i] = Tq[i] * sig;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint32_t w = 0u;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float r = rintf(x[i]);
+        w |= (uint32_t(__float2int_rn(r)) & 0xFFu) << (8 * i);
+        x[i] = (x[i] - r) * 128.0f;
+      }
+      *reinterpret_cast<uint32_t*>(X.t8 + j * T8STR + lane * 4) = w;
+    }
+#pragma unroll
+    for (int j = 4; j < 8; ++j) *reinterpret_cast<uint32_t*>(X.t8 + j * T8STR + lane * 4) = 0u;
+    if (lane == 0) X.misc[0] = 1.0f / sig;
+    return;
+  }
+  // T -> 5 e4m3 terms: T sigma = sum_i term_i 16^-i, max |T sigma| in [128, 256)
   const float sig = pow2_scale_for(m) * (1.0f / 64.0f);
   float x[4];
 #pragma unroll
@@ -231,16 +276,54 @@ __device__ __forceinline__ ReadoutFrags head_readout_frags(const HeadScratch& X,
   return f;
 }
 
+// With I8 the columns 0..3 hold S_int8 . limb_j (s8 MMA, s32) and 5..7 V^T . c
+// in a separate f32 accumulator.
+template <bool I8>
 __device__ __forceinline__ void head_readout_mtile(const HeadTile& T, const ReadoutFrags& f, int n, float wsc,
                                                    int rbase, int lane, float& o0, float& o1) {
   const int g8 = lane >> 2, t4 = lane & 3;
   const int VSTR = T.vstr;
   const uint16_t* vr_s = T.vr;
+  const int r0 = rbase + g8, r1 = r0 + 8;
+  if constexpr (I8) {
+    int32_t iacc[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      uint32_t a[4];
+      a[0] = *reinterpret_cast<const uint32_t*>(T.s0 + s0_off(r0, 2 * ks) + 4 * t4);
+      a[1] = *reinterpret_cast<const uint32_t*>(T.s0 + s0_off(r1, 2 * ks) + 4 * t4);
+      a[2] = *reinterpret_cast<const uint32_t*>(T.s0 + s0_off(r0, 2 * ks + 1) + 4 * t4);
+      a[3] = *reinterpret_cast<const uint32_t*>(T.s0 + s0_off(r1, 2 * ks + 1) + 4 * t4);
+      mma16832_s8(iacc, a, f.bt[ks][0], f.bt[ks][1]);
+    }
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    {
+      const int t0 = 2 * t4, t1 = 2 * t4 + 8;
+      uint32_t a[4];
+      a[0] = (t0 < n ? uint32_t(vr_s[t0 * VSTR + r0]) : 0u) | (t0 + 1 < n ? uint32_t(vr_s[(t0 + 1) * VSTR + r0]) << 16 : 0u);
+      a[1] = (t0 < n ? uint32_t(vr_s[t0 * VSTR + r1]) : 0u) | (t0 + 1 < n ? uint32_t(vr_s[(t0 + 1) * VSTR + r1]) << 16 : 0u);
+      a[2] = (t1 < n ? uint32_t(vr_s[t1 * VSTR + r0]) : 0u) | (t1 + 1 < n ? uint32_t(vr_s[(t1 + 1) * VSTR + r0]) << 16 : 0u);
+      a[3] = (t1 < n ? uint32_t(vr_s[t1 * VSTR + r1]) : 0u) | (t1 + 1 < n ? uint32_t(vr_s[(t1 + 1) * VSTR + r1]) << 16 : 0u);
+      mma16816_bf16(acc, a, f.rb0, f.rb1);
+    }
+    // limb weights: t4 = 0 -> limbs 0, 1; t4 = 1 -> limbs 2, 3; t4 >= 2 -> zero columns
+    // (the s32 sums stay below 2^24, so the conversion is exact)
+    const float wi0 = t4 == 0 ? wsc : (t4 == 1 ? wsc * (1.0f / 16384.0f) : 0.0f);
+    const float wi1 = t4 == 0 ? wsc * (1.0f / 128.0f) : (t4 == 1 ? wsc * (1.0f / 2097152.0f) : 0.0f);
+    o0 = fmaf(float(iacc[1]), wi1, float(iacc[0]) * wi0) + (acc[0] + acc[1]);
+    o1 = fmaf(float(iacc[3]), wi1, float(iacc[2]) * wi0) + (acc[2] + acc[3]);
+    o0 += __shfl_xor_sync(0xffffffffu, o0, 1);
+    o1 += __shfl_xor_sync(0xffffffffu, o1, 1);
+    o0 += __shfl_xor_sync(0xffffffffu, o0, 2);
+    o1 += __shfl_xor_sync(0xffffffffu, o1, 2);
+    o0 *= KSCALE_H;
+    o1 *= KSCALE_H;
+    return;
+  }
   // column weights: t4 = 0 -> terms 0,1; 1 -> terms 2,3; 2 -> term 4, ring; 3 -> ring, ring
   const float w0 = t4 == 0 ? wsc : (t4 == 1 ? wsc * (1.0f / 256.0f) : (t4 == 2 ? wsc * (1.0f / 65536.0f) : 1.0f));
   const float w1 = t4 == 0 ? wsc * (1.0f / 16.0f) : (t4 == 1 ? wsc * (1.0f / 4096.0f) : 1.0f);
   float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-  const int r0 = rbase + g8, r1 = r0 + 8;
 #pragma unroll
   for (int ks = 0; ks < 4; ++ks) {
     uint32_t a[4];
@@ -271,10 +354,10 @@ __device__ __forceinline__ void head_readout_mtile(const HeadTile& T, const Read
 
 // n: ring slots replayed (0..16); sc: the vblock scale of this warp's rows.
 // Writes X.ow[32 warp + i] = output row i of the warp's vblock (already * K^-1/2).
-template <class Sync>
+template <bool I8, class Sync>
 __device__ __forceinline__ void head_nonflush(const HeadTile& T, const HeadScratch& X, int n, float sc, int warp,
                                               int lane, Sync sync) {
-  if (warp == 0) head_chain(T, X, n, lane);
+  if (warp == 0) head_chain<I8>(T, X, n, lane);
   sync();
   const int g8 = lane >> 2, t4 = lane & 3;
   const ReadoutFrags f = head_readout_frags(X, lane);
@@ -283,7 +366,7 @@ __device__ __forceinline__ void head_nonflush(const HeadTile& T, const HeadScrat
 #pragma unroll
   for (int mt = 0; mt < 2; ++mt) {
     float o0, o1;
-    head_readout_mtile(T, f, n, wsc, 32 * warp + 16 * mt, lane, o0, o1);
+    head_readout_mtile<I8>(T, f, n, wsc, 32 * warp + 16 * mt, lane, o0, o1);
     if (t4 == 0) {
       ow[16 * mt + g8] = o0;
       ow[16 * mt + g8 + 8] = o1;
@@ -297,7 +380,7 @@ __device__ __forceinline__ void head_nonflush(const HeadTile& T, const HeadScrat
 // ck_tile_global (row 0 of this tile in the global checkpoint); the warp's
 // new scale goes to scale_ptr[sc_index] (f16 or f32 holding the f16 value).
 // gtid / nthreads: thread index within / size of the group owning the head.
-template <class Sync>
+template <bool I8, class Sync>
 __device__ __forceinline__ void head_flush(const HeadTile& T, const HeadScratch& X, int n, float sc, int quant_rounded,
                                            uint8_t* ck_tile_global, void* scale_ptr, int64_t sc_index, int sc_dt,
                                            int warp, int lane, int gtid, int nthreads, Sync sync) {
@@ -402,7 +485,10 @@ __device__ __forceinline__ void head_flush(const HeadTile& T, const HeadScratch&
 #pragma unroll
     for (int ks = 0; ks < 8; ++ks) {
       uint32_t a[4];
-      s0_afrag_f16(s0, rw0 + 16 * mt, ks, g8, t4, a);
+      if constexpr (I8)
+        s0_afrag_i8f16(s0, rw0 + 16 * mt, ks, g8, t4, a);
+      else
+        s0_afrag_f16(s0, rw0 + 16 * mt, ks, g8, t4, a);
       const int col = 16 * ks + 2 * t4;
 #pragma unroll
       for (int nt = 0; nt < 3; ++nt) {
@@ -503,9 +589,13 @@ __device__ __forceinline__ void head_flush(const HeadTile& T, const HeadScratch&
   for (int pass = 0; pass < 2; ++pass) {
     if (pass == 1) {
       amax = warp_max_nan(amax);
-      vs = vblock_scale(amax, quant_rounded);
-      rcp = __fdiv_rn(1.0f, vs.divisor);
-      fast = quant_exact_ok(vs.divisor, rcp);
+      if constexpr (I8) {
+        vs = vblock_scale_i8(amax, quant_rounded);
+      } else {
+        vs = vblock_scale(amax, quant_rounded);
+        rcp = __fdiv_rn(1.0f, vs.divisor);
+        fast = quant_exact_ok(vs.divisor, rcp);
+      }
     }
 #pragma unroll 2
     for (int nt = 0; nt < 16; ++nt) {
@@ -524,8 +614,13 @@ __device__ __forceinline__ void head_flush(const HeadTile& T, const HeadScratch&
           const int r = rw0 + 16 * mt + g8 + 8 * hf;
           const int cc = 8 * nt + 2 * t4;  // even column pair (cc, cc+1)
           const uint8_t* sp = s0 + s0_off(r, cc >> 4) + (cc & 15);
-          const uint32_t h2 = e4m3x2_to_f16x2(*reinterpret_cast<const uint16_t*>(sp));
-          const float2 sf = __half22float2(*reinterpret_cast<const __half2*>(&h2));
+          float2 sf;
+          if constexpr (I8) {
+            sf = i8x2_to_f2(*reinterpret_cast<const uint16_t*>(sp));
+          } else {
+            const uint32_t h2 = e4m3x2_to_f16x2(*reinterpret_cast<const uint16_t*>(sp));
+            sf = __half22float2(*reinterpret_cast<const __half2*>(&h2));
+          }
           x[(mt * 2 + hf) * 2] = fmaf(acc[2 * hf], dsc, asc * sf.x);
           x[(mt * 2 + hf) * 2 + 1] = fmaf(acc[2 * hf + 1], dsc, asc * sf.y);
         }
@@ -535,7 +630,14 @@ __device__ __forceinline__ void head_flush(const HeadTile& T, const HeadScratch&
         for (int i = 0; i < 8; ++i) amax = fmax_nan(amax, fabsf(x[i]));
       } else {
         uint32_t c[4];
-        quant_pairs_warp<4>(x, c, vs.divisor, rcp, quant_exact_kd(vs.divisor), fast);
+        if constexpr (I8) {
+          uint32_t sat = 0u;
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            c[i] = quant_i8(x[2 * i], vs.divisor, sat) | (quant_i8(x[2 * i + 1], vs.divisor, sat) << 8);
+        } else {
+          quant_pairs_warp<4>(x, c, vs.divisor, rcp, quant_exact_kd(vs.divisor), fast);
+        }
 #pragma unroll
         for (int mt = 0; mt < 2; ++mt)
 #pragma unroll

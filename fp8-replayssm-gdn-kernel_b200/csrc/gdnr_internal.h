@@ -69,10 +69,13 @@ struct StepParams {
   int32_t flush_hint;   // GDNR_FLUSH_*
   int32_t pdl;          // launch with programmatic stream serialization
   // packed decode: batch row b uses state slot sidx[b * si_s] of every state
-  // tensor (S slots; slot 0 is the null slot); null = the state is indexed by b
+  // tensor (S slots; an index <= 0 is the null slot); null = the state is indexed by b
   const int32_t* sidx;
   int64_t si_s;
   int32_t S;
+  // the checkpoint holds int8 codes ("vblock_int8"); launched on the
+  // one-CTA-per-head kernel (gdnr_step2.cu) only
+  int32_t ck_i8;
 };
 
 struct SmemLayout {
@@ -108,7 +111,7 @@ __host__ __device__ inline SmemLayout step_smem_layout(int G, int L, int rows, i
 constexpr uint32_t MAX_DYN_SMEM = 227u * 1024u;
 
 cudaError_t launch_step(const StepParams& p, bool fused, bool f32ck, int group, cudaStream_t stream);
-// B200 path for E4M3 checkpoints and rings of L <= 16 (one CTA per value head)
+// B200 path for E4M3 or INT8 checkpoints and rings of L <= 16 (one CTA per value head)
 cudaError_t launch_step2(const StepParams& p, bool fused, cudaStream_t stream);
 constexpr int STEP2_MAX_L = 16;
 // persistent warp-specialised path for the heads that do not flush (gdnr_step5.cu)

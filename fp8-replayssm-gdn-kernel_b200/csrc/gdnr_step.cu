@@ -417,6 +417,7 @@ cudaError_t launch_step(const StepParams& p, bool fused, bool f32ck, int group, 
   if (step5_eligible(p, fused, f32ck)) return launch_step5(p, fused, p.pdl != 0, stream);
   if (p.sidx) return cudaErrorNotSupported;  // slot indirection: the persistent kernel only
   if (!f32ck && p.L <= STEP2_MAX_L) return launch_step2(p, fused, stream);
+  if (p.ck_i8) return cudaErrorNotSupported;  // INT8 checkpoints: rings of L <= 16 only (checked by the API)
   if (fused) return f32ck ? launch_g<true, true>(p, group, stream) : launch_g<true, false>(p, group, stream);
   return f32ck ? launch_g<false, true>(p, group, stream) : launch_g<false, false>(p, group, stream);
 }

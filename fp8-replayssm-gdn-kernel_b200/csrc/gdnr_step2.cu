@@ -75,8 +75,9 @@ __device__ __forceinline__ bool cta_wait2(uint64_t* bar, uint32_t parity, uint32
   return __syncthreads_or(!ok) == 0;
 }
 
-template <bool FUSED>
-__global__ void __launch_bounds__(128, 6) step2_kernel(const __grid_constant__ StepParams p) {
+// I8: the checkpoint holds int8 codes ("vblock_int8"); see gdnr_head.cuh.
+template <bool FUSED, bool I8>
+__global__ void __launch_bounds__(128, I8 ? 4 : 6) step2_kernel(const __grid_constant__ StepParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int hv = blockIdx.x, b = blockIdx.y, z = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -240,38 +241,32 @@ __global__ void __launch_bounds__(128, 6) step2_kernel(const __grid_constant__ S
                       reinterpret_cast<float*>(smem + S.ow),
                       misc};
   if (!do_flush) {
-    head_nonflush(T, X, n, sc, warp, lane, CtaSync{});
+    head_nonflush<I8>(T, X, n, sc, warp, lane, CtaSync{});
   } else {
     uint8_t* ck_tile = static_cast<uint8_t*>(p.ck) + int64_t(b) * p.ck_sb + int64_t(hv) * p.ck_sh + int64_t(row0) * 128;
-    head_flush(T, X, n, sc, p.quant_rounded, ck_tile, p.sc, sc_idx, p.sc_dt, warp, lane, tid, blockDim.x, CtaSync{});
+    head_flush<I8>(T, X, n, sc, p.quant_rounded, ck_tile, p.sc, sc_idx, p.sc_dt, warp, lane, tid, blockDim.x, CtaSync{});
   }
   // ---- 12. output rows of this warp
   store_scalar(p.out, int64_t(b) * p.o_sb + int64_t(hv) * p.o_sh + int64_t(row0 + rw0 + lane) * p.o_sv, p.o_dt,
                ow[lane]);
 }
 
-cudaError_t launch_step2(const StepParams& p, bool fused, cudaStream_t stream) {
+template <bool FUSED, bool I8>
+static cudaError_t launch_step2_t(const StepParams& p, cudaStream_t stream) {
   const Smem2 s = step2_smem(p.L, p.rows);
-  dim3 grid(p.HV, p.B, 128 / p.rows);
-  if (fused) {
-    static int configured = 0;
-    if (int(s.total) > configured) {
-      cudaError_t e = cudaFuncSetAttribute(step2_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(s.total));
-      if (e != cudaSuccess) return e;
-      configured = int(s.total);
-    }
-    step2_kernel<true><<<grid, p.rows, s.total, stream>>>(p);
-  } else {
-    static int configured = 0;
-    if (int(s.total) > configured) {
-      cudaError_t e =
-          cudaFuncSetAttribute(step2_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(s.total));
-      if (e != cudaSuccess) return e;
-      configured = int(s.total);
-    }
-    step2_kernel<false><<<grid, p.rows, s.total, stream>>>(p);
+  static int configured = 0;  // largest dynamic smem size already allowed for this instance
+  if (int(s.total) > configured) {
+    cudaError_t e = cudaFuncSetAttribute(step2_kernel<FUSED, I8>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(s.total));
+    if (e != cudaSuccess) return e;
+    configured = int(s.total);
   }
+  step2_kernel<FUSED, I8><<<dim3(p.HV, p.B, 128 / p.rows), p.rows, s.total, stream>>>(p);
   return cudaGetLastError();
+}
+
+cudaError_t launch_step2(const StepParams& p, bool fused, cudaStream_t stream) {
+  if (p.ck_i8) return fused ? launch_step2_t<true, true>(p, stream) : launch_step2_t<false, true>(p, stream);
+  return fused ? launch_step2_t<true, false>(p, stream) : launch_step2_t<false, false>(p, stream);
 }
 
 }  // namespace gdnr

@@ -1885,7 +1885,7 @@ static bool s5_grid(const StepParams& p, int& grid, S5Layout& lay) {
 }
 
 bool step5_eligible(const StepParams& p, bool fused, bool f32ck) {
-  if (f32ck || p.L < 4 || p.L > STEP2_MAX_L) return false;
+  if (f32ck || p.ck_i8 || p.L < 4 || p.L > STEP2_MAX_L) return false;
   const int G = p.HV / p.H;
   if (G != 1 && G % 2 != 0) return false;
   if (p.ck_sb % 16 || p.ck_sh % 16 || reinterpret_cast<uintptr_t>(p.ck) % 16) return false;

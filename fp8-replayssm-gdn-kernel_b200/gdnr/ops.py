@@ -87,7 +87,8 @@ def gdn_replay_fp8(
 ) -> torch.Tensor:
     """Replay (and, where ``flush[b]``, rebuild + re-quantise in place).
 
-    checkpoint [B,HV,V,K] float8_e4m3fn (or float32: full-precision variant),
+    checkpoint [B,HV,V,K] float8_e4m3fn, int8 (the "vblock_int8" option,
+    rings of L <= 16) or float32 (full-precision variant),
     checkpoint_scale [B,HV,V/32] float16|float32, q [B,H,K], rings
     k [B,L,H,K] / v [B,L,HV,V] bf16, g/beta [B,L,HV], valid_len [B] int32,
     flush [B] bool.  Returns out [B,HV,V] in q's dtype unless ``out`` given.
@@ -410,8 +411,10 @@ def quantize_checkpoint(
 
     ``state`` [B,HV,V,K] float32 on CUDA.  ``compute_saturation`` reads the
     saturation count back (one synchronisation), like the reference's
-    ``.item()`` at ref.py:95.  INT8 checkpoints are a codec option: the replay
-    and step entry points take E4M3 (or float32) checkpoints.
+    ``.item()`` at ref.py:95.  An int8 payload also runs through
+    :func:`gdn_replay_fp8` and :func:`gdn_fused_step` (rings of L <= 16; the
+    flush re-quantises it to int8); the packed decode and the split replay
+    take E4M3 payloads only.
     """
     if granularity not in ("vblock", "vblock_int8") or tile_size != 32:
         raise ValueError("the GPU codec implements granularity 'vblock' / 'vblock_int8' with tile_size=32 only")

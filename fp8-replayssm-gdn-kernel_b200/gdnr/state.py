@@ -5,7 +5,8 @@ its kernels (prototype/gdn_replayssm_fp8_kernel.py:344-405 and
 prototype/bench_gdn_full_contract.py:113-135):
 
 * ``checkpoint`` [B,HV,V,K] float8_e4m3fn -- the FP8 snapshot at the start
-  of the current window (float32 for the full-precision variant);
+  of the current window (int8 codes for the "vblock_int8" option, float32 for
+  the full-precision variant);
 * ``scale`` [B,HV,V/32] -- one scale per 32 value rows (float16 as the
   reference stores it, or float32 holding the float16-rounded value);
 * the ring of the last L tokens: ``k`` [B,L,H,K] bf16, ``v`` [B,L,HV,V] bf16,
@@ -67,7 +68,8 @@ class ReplayState:
         if self.checkpoint.dtype == torch.float32:
             self.checkpoint.copy_(state)
             return
-        ops.quantize_checkpoint(state.float().contiguous(), payload=self.checkpoint, scale=self.scale,
+        gran = "vblock_int8" if self.checkpoint.dtype == torch.int8 else "vblock"
+        ops.quantize_checkpoint(state.float().contiguous(), gran, payload=self.checkpoint, scale=self.scale,
                                 scale_dtype=self.scale.dtype, quant_divisor=quant_divisor,
                                 compute_saturation=False)
 

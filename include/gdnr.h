@@ -82,7 +82,8 @@ typedef struct {
 
 /* ---- gdnr_replay: mirror of gdn_replay_fp8 ---------------------------- */
 typedef struct {
-  gdnr_tensor checkpoint; /* [B,HV,V,K] E4M3, or F32 for the full-precision variant; in/out */
+  gdnr_tensor checkpoint; /* [B,HV,V,K] E4M3, I8 ("vblock_int8" codes, L <= 16; the flush
+                             re-quantises to I8), or F32 for the full-precision variant; in/out */
   gdnr_tensor scale;      /* [B,HV,V/32] F16|F32 (absent for an F32 checkpoint); in/out */
   gdnr_tensor q;          /* [B,H,K] BF16|F32, already L2-normalised */
   gdnr_tensor k_ring;     /* [B,L,H,K] BF16 */
@@ -158,7 +159,7 @@ typedef struct {
   gdnr_tensor mixed_qkv, a, b, a_log, dt_bias; /* as gdnr_prep_args */
   gdnr_tensor pos;        /* [B] I32: slot of this token; the step flushes when pos == L-1 */
   gdnr_tensor pos_out;    /* optional [B] I32 (distinct from pos): receives (pos+1) % L */
-  gdnr_tensor checkpoint; /* [B,HV,V,K] E4M3 | F32, in/out */
+  gdnr_tensor checkpoint; /* [B,HV,V,K] E4M3 | I8 (L <= 16) | F32, in/out */
   gdnr_tensor scale;      /* [B,HV,V/32] F16|F32 (absent for F32 checkpoint), in/out */
   gdnr_tensor k_ring, v_ring, g_ring, beta_ring; /* in/out: slot pos is written */
   gdnr_tensor out;        /* [B,HV,V] BF16|F32 */

@@ -428,8 +428,9 @@ def prep(mixed_qkv, a, b, a_log, dt_bias, heads: int, key_dim: int, value_heads:
 class RingState:
     """Persistent per-sequence state of the replay scheme (kern.py:344-405 args).
 
-    payload [B,HV,V,K] e4m3 bytes (or float32 for the full-precision
-    variant), scale [B,HV,V/32] float16 (None for float32), rings
+    payload [B,HV,V,K] e4m3 bytes, int8 codes (the 'vblock_int8' option) or
+    float32 for the full-precision variant; scale [B,HV,V/32] float16 (None
+    for float32); rings
     k [B,L,H,K], v [B,L,HV,V], g/beta [B,L,HV] as float32 arrays holding
     values already rounded to their storage dtype.
     """
@@ -477,7 +478,8 @@ def replay_step(st: RingState, qn, pos, out_dtype="bf16", quant_divisor="oracle"
             if st.scale is None:
                 st.payload[i] = s_new[0]
             else:
-                qc = quantize_vblock32(s_new, divisor=quant_divisor)
+                # an int8 payload stays int8 (the 'vblock_int8' codec, ref.py:44-47, :96-97)
+                qc = quantize_vblock32(s_new, divisor=quant_divisor, int8=st.payload.dtype == np.int8)
                 st.payload[i] = qc.payload[0]
                 st.scale[i] = qc.scale[0]
     return _store_round(out, out_dtype)

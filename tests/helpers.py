@@ -84,3 +84,28 @@ def oracle_replay_out(state_f32, q, k, v, g, beta, valid):
         out[b] = o[0, -1]
         states[b] = s[0]
     return out, states
+
+
+def check_prep_and_sync(host, dev, mixed, a, b, a_log, dt_bias, pos, H, gate_name, q_out):
+    """Compare this step's prep outputs (ring slot ``pos``, q_out) with the
+    oracle's prep, then copy the device's slot into the host ring so that the
+    replay comparison runs on identical inputs.  Returns the device q."""
+    B, HV = a.shape
+    qn, kn, v, g, be = O.prep(mixed, a, b, a_log, dt_bias, H, 128, HV, 128, gate_dtype=gate_name)
+    qd = to_np(q_out)
+    # x/||x|| is rounded to bf16; a last-bit difference needs a value within
+    # ~1e-7 of a rounding midpoint
+    assert np.mean(qd != qn) < 1e-2 and np.allclose(qd, qn, rtol=8e-3, atol=1e-6)
+    for i in range(B):
+        p = pos[i]
+        kd = to_np(dev.k_ring[i, p])
+        assert np.mean(kd != kn[i]) < 1e-2 and np.allclose(kd, kn[i], rtol=8e-3, atol=1e-6)
+        np.testing.assert_array_equal(to_np(dev.v_ring[i, p]), v[i])
+        gtol = 1e-5 if gate_name == "f32" else 8e-3
+        np.testing.assert_allclose(to_np(dev.g_ring[i, p]), g[i], rtol=gtol, atol=1e-6)
+        np.testing.assert_allclose(to_np(dev.beta_ring[i, p]), be[i], rtol=gtol, atol=1e-6)
+        host.k_ring[i, p] = kd
+        host.v_ring[i, p] = v[i]
+        host.g_ring[i, p] = to_np(dev.g_ring[i, p])
+        host.beta_ring[i, p] = to_np(dev.beta_ring[i, p])
+    return qd

@@ -8,7 +8,8 @@ import torch
 
 import gdnr
 import oracle as O
-from helpers import TOL_F32_KERNEL, TOL_FULL_PRECISION, TOL_OUT_BF16, e4m3_dev, gate_params, raw_inputs, to_dev, to_np
+from helpers import TOL_F32_KERNEL, TOL_FULL_PRECISION, TOL_OUT_BF16, check_prep_and_sync, e4m3_dev, gate_params, \
+    raw_inputs, to_dev, to_np
 
 pytestmark = pytest.mark.gpu
 
@@ -33,31 +34,6 @@ def make_state(rng, B, H, HV, L, gate_dtype, scale_dtype, f32ck=False):
 
 def _gname(dt):
     return {torch.float32: "f32", torch.bfloat16: "bf16"}[dt]
-
-
-def check_prep_and_sync(host, dev, mixed, a, b, a_log, dt_bias, pos, H, gate_name, q_out):
-    """Compare this step's prep outputs (ring slot ``pos``, q_out) with the
-    oracle's prep, then copy the device's slot into the host ring so that the
-    replay comparison runs on identical inputs.  Returns the device q."""
-    B, HV = a.shape
-    qn, kn, v, g, be = O.prep(mixed, a, b, a_log, dt_bias, H, 128, HV, 128, gate_dtype=gate_name)
-    qd = to_np(q_out)
-    # x/||x|| is rounded to bf16; a last-bit difference needs a value within
-    # ~1e-7 of a rounding midpoint
-    assert np.mean(qd != qn) < 1e-2 and np.allclose(qd, qn, rtol=8e-3, atol=1e-6)
-    for i in range(B):
-        p = pos[i]
-        kd = to_np(dev.k_ring[i, p])
-        assert np.mean(kd != kn[i]) < 1e-2 and np.allclose(kd, kn[i], rtol=8e-3, atol=1e-6)
-        np.testing.assert_array_equal(to_np(dev.v_ring[i, p]), v[i])
-        gtol = 1e-5 if gate_name == "f32" else 8e-3
-        np.testing.assert_allclose(to_np(dev.g_ring[i, p]), g[i], rtol=gtol, atol=1e-6)
-        np.testing.assert_allclose(to_np(dev.beta_ring[i, p]), be[i], rtol=gtol, atol=1e-6)
-        host.k_ring[i, p] = kd
-        host.v_ring[i, p] = v[i]
-        host.g_ring[i, p] = to_np(dev.g_ring[i, p])
-        host.beta_ring[i, p] = to_np(dev.beta_ring[i, p])
-    return qd
 
 
 @pytest.mark.parametrize("heads", [(2, 4), (4, 4)])

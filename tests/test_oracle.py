@@ -145,9 +145,11 @@ def test_adjoint_replay_equals_forward():
         assert O.relative_l2(got[i], o[0, -1]) < 1e-5
 
 
-def test_fused_step_cycle_equals_replay_decode():
+@pytest.mark.parametrize("gran", ["vblock", "vblock_int8"])
+def test_fused_step_cycle_equals_replay_decode(gran):
     """Driving the full-contract step oracle over T tokens reproduces the
-    reference replay chain (ref.py:189-244) on the prepped inputs."""
+    reference replay chain (ref.py:189-244) on the prepped inputs, for the
+    E4M3 and the int8 checkpoint (the flush keeps the payload's format)."""
     rng = np.random.default_rng(3)
     B, T, H, HV, K, L = 2, 7, 1, 2, 128, 3
     mixed = O.bf16_round(rng.standard_normal((T, B, 2 * H * K + HV * K)).astype(np.float32))
@@ -156,7 +158,7 @@ def test_fused_step_cycle_equals_replay_decode():
     a_log = np.log(rng.uniform(1, 16, HV)).astype(np.float32)
     dt_bias = (0.5 * rng.standard_normal(HV)).astype(np.float32)
     s0 = (0.02 * rng.standard_normal((B, HV, K, K))).astype(np.float32)
-    q0 = O.quantize_checkpoint(s0, "vblock", 32)
+    q0 = O.quantize_checkpoint(s0, gran, 32)
     st = O.RingState(q0.payload.copy(), q0.scale.copy(), np.zeros((B, L, H, K), np.float32),
                      np.zeros((B, L, HV, K), np.float32), np.zeros((B, L, HV), np.float32),
                      np.zeros((B, L, HV), np.float32))
@@ -169,12 +171,13 @@ def test_fused_step_cycle_equals_replay_decode():
         qs.append(qn2); ks.append(kn); vs.append(v); gs.append(g); bs.append(be)
     stack = lambda xs: np.stack(xs, axis=1)
     ref_out, ref_state, _, _ = O.replay_decode(s0, stack(qs), stack(ks), stack(vs), stack(gs), stack(bs), L,
-                                               "vblock", 32)
+                                               gran, 32)
     assert O.relative_l2(np.stack(outs, 1), ref_out) < 1e-6
     # after T=7 tokens with L=3 the ring holds one token past the last flush at t=5
+    assert st.payload.dtype == q0.payload.dtype
     assert O.relative_l2(st.dequantized(), O.dequantize_checkpoint(O.quantize_checkpoint(
         O.replay_decode(s0, stack(qs)[:, :6], stack(ks)[:, :6], stack(vs)[:, :6], stack(gs)[:, :6],
-                        stack(bs)[:, :6], L, "vblock", 32)[1], "vblock", 32))) < 1e-6
+                        stack(bs)[:, :6], L, gran, 32)[1], gran, 32))) < 1e-6
 
 
 def test_prep_formula():
