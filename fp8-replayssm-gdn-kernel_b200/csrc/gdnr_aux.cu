@@ -230,24 +230,43 @@ struct Bf16StepParams {
   int32_t B, H, HV;
 };
 
-// grid (HV, B), 256 threads: 8 lanes x 16 columns per row, 32 rows per pass.
-__global__ void __launch_bounds__(256) bf16_step_kernel(const __grid_constant__ Bf16StepParams p) {
+// grid (HV, B), 256 threads: 8 lanes x 16 columns per row, 32 rows per pass,
+// 4 passes.  A thread issues the loads of all four of its rows (128 bytes)
+// before it computes the first one, and k / q sit in shared memory rather than
+// registers, so that three CTAs fit on an SM and keep enough of the state
+// stream in flight to run at HBM speed.
+constexpr int BF16_PASSES = 4;
+
+__global__ void __launch_bounds__(256, 3) bf16_step_kernel(const __grid_constant__ Bf16StepParams p) {
+  __shared__ __align__(16) float kq_s[2][128];
   const int hv = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
   const int h = hv / (p.HV / p.H);
-  const int c = tid & 7;
-  float kk[16], qq[16];
+  const int c = tid & 7, r0 = tid >> 3;
+  uint16_t* head = p.state + int64_t(b) * p.s_sb + int64_t(hv) * p.s_sh + c * 16;
+  uint4 w[BF16_PASSES][2];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    kk[i] = load_scalar(p.k, int64_t(b) * p.k_sb + int64_t(h) * p.k_sh + c * 16 + i, p.k_dt);
-    qq[i] = load_scalar(p.q, int64_t(b) * p.q_sb + int64_t(h) * p.q_sh + c * 16 + i, p.q_dt);
+  for (int j = 0; j < BF16_PASSES; ++j) {
+    const uint4* src = reinterpret_cast<const uint4*>(head + int64_t(r0 + 32 * j) * 128);
+    w[j][0] = src[0];
+    w[j][1] = src[1];
   }
+  float vv[BF16_PASSES];
+#pragma unroll
+  for (int j = 0; j < BF16_PASSES; ++j)
+    vv[j] = load_scalar(p.v, int64_t(b) * p.v_sb + int64_t(hv) * p.v_sh + int64_t(r0 + 32 * j) * p.v_sv, p.v_dt);
+  if (tid < 128)
+    kq_s[0][tid] = load_scalar(p.k, int64_t(b) * p.k_sb + int64_t(h) * p.k_sh + tid, p.k_dt);
+  else
+    kq_s[1][tid - 128] = load_scalar(p.q, int64_t(b) * p.q_sb + int64_t(h) * p.q_sh + tid - 128, p.q_dt);
   const float gam = expf(load_scalar(p.g, int64_t(b) * p.g_sb + int64_t(hv) * p.g_sh, p.g_dt));
   const float be = load_scalar(p.beta, int64_t(b) * p.be_sb + int64_t(hv) * p.be_sh, p.be_dt);
-  for (int r = tid >> 3; r < 128; r += 32) {
-    uint16_t* row = p.state + int64_t(b) * p.s_sb + int64_t(hv) * p.s_sh + int64_t(r) * 128 + c * 16;
-    const uint4 w0 = reinterpret_cast<const uint4*>(row)[0];
-    const uint4 w1 = reinterpret_cast<const uint4*>(row)[1];
-    const uint32_t ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+  __syncthreads();
+  const float4* kk4 = reinterpret_cast<const float4*>(kq_s[0] + c * 16);
+  const float4* qq4 = reinterpret_cast<const float4*>(kq_s[1] + c * 16);
+#pragma unroll
+  for (int j = 0; j < BF16_PASSES; ++j) {
+    const int r = r0 + 32 * j;
+    const uint32_t ws[8] = {w[j][0].x, w[j][0].y, w[j][0].z, w[j][0].w, w[j][1].x, w[j][1].y, w[j][1].z, w[j][1].w};
     float s[16];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -255,25 +274,39 @@ __global__ void __launch_bounds__(256) bf16_step_kernel(const __grid_constant__ 
       s[2 * i] = f.x * gam;
       s[2 * i + 1] = f.y * gam;
     }
+    float kk[16];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float4 k4 = kk4[i];
+      kk[4 * i] = k4.x;
+      kk[4 * i + 1] = k4.y;
+      kk[4 * i + 2] = k4.z;
+      kk[4 * i + 3] = k4.w;
+    }
     float d = 0.0f;
 #pragma unroll
     for (int i = 0; i < 16; ++i) d = fmaf(s[i], kk[i], d);
     d += __shfl_xor_sync(0xffffffffu, d, 1);
     d += __shfl_xor_sync(0xffffffffu, d, 2);
     d += __shfl_xor_sync(0xffffffffu, d, 4);
-    const float vv = load_scalar(p.v, int64_t(b) * p.v_sb + int64_t(hv) * p.v_sh + int64_t(r) * p.v_sv, p.v_dt);
-    const float corr = (vv - d) * be;
+    const float corr = (vv[j] - d) * be;
     float o = 0.0f;
     uint32_t wo[8];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      s[i] = fmaf(corr, kk[i], s[i]);
-      o = fmaf(s[i], qq[i], o);
+    for (int i = 0; i < 4; ++i) {
+      const float4 q4 = qq4[i];
+      const float qv[4] = {q4.x, q4.y, q4.z, q4.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        s[4 * i + e] = fmaf(corr, kk[4 * i + e], s[4 * i + e]);
+        o = fmaf(s[4 * i + e], qv[e], o);
+      }
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) wo[i] = uint32_t(f_to_bf16(s[2 * i])) | (uint32_t(f_to_bf16(s[2 * i + 1])) << 16);
-    reinterpret_cast<uint4*>(row)[0] = make_uint4(wo[0], wo[1], wo[2], wo[3]);
-    reinterpret_cast<uint4*>(row)[1] = make_uint4(wo[4], wo[5], wo[6], wo[7]);
+    uint4* dst = reinterpret_cast<uint4*>(head + int64_t(r) * 128);
+    dst[0] = make_uint4(wo[0], wo[1], wo[2], wo[3]);
+    dst[1] = make_uint4(wo[4], wo[5], wo[6], wo[7]);
     o += __shfl_xor_sync(0xffffffffu, o, 1);
     o += __shfl_xor_sync(0xffffffffu, o, 2);
     o += __shfl_xor_sync(0xffffffffu, o, 4);

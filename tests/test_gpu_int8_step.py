@@ -83,20 +83,27 @@ def test_int8_replay_flush_matches_oracle(cuda_device, divisor):
             assert np.array_equal(got_payload[b], ck.payload[b])
 
 
-def test_int8_fused_cycles_match_oracle(cuda_device):
+@pytest.mark.parametrize("heads,L,gate_dtype,scale_dtype", [
+    ((2, 4), 4, torch.float32, torch.float32),
+    ((2, 2), 3, torch.bfloat16, torch.float16),
+    ((1, 4), 8, torch.float32, torch.float16),
+])
+def test_int8_fused_cycles_match_oracle(cuda_device, heads, L, gate_dtype, scale_dtype):
     rng = np.random.default_rng(43)
-    H, HV, B, L, T = 2, 4, 4, 4, 10
+    (H, HV), B = heads, 4
+    T = 2 * L + 2
+    gname = "f32" if gate_dtype == torch.float32 else "bf16"
     a_log, dt_bias = gate_params(rng, HV)
     s0 = (0.02 * rng.standard_normal((B, HV, 128, 128))).astype(np.float32)
     q0 = O.quantize_checkpoint(s0, "vblock_int8", 32)
     host = O.RingState(q0.payload.copy(), q0.scale.copy(), np.zeros((B, L, H, 128), np.float32),
                        np.zeros((B, L, HV, 128), np.float32), np.zeros((B, L, HV), np.float32),
                        np.zeros((B, L, HV), np.float32))
-    dev = gdnr.ReplayState.allocate(B, H, HV, L, scale_dtype=torch.float32, gate_dtype=torch.float32,
+    dev = gdnr.ReplayState.allocate(B, H, HV, L, scale_dtype=scale_dtype, gate_dtype=gate_dtype,
                                     checkpoint_dtype=torch.int8)
     dev.load_state(to_dev(s0, torch.float32))
     np.testing.assert_array_equal(to_np(dev.checkpoint), q0.payload)  # the GPU int8 codec, bit-exact
-    pos = np.array([0, 1, 3, 2], np.int32)
+    pos = np.array([0, 1, L - 1, L // 2], np.int32)
     dev.pos.copy_(to_dev(pos, torch.int32))
     pos_next = torch.empty_like(dev.pos)
     flushes = 0
@@ -106,7 +113,7 @@ def test_int8_fused_cycles_match_oracle(cuda_device):
         q_out = torch.empty(B, H, 128, dtype=torch.bfloat16, device="cuda")
         dev.step(to_dev(mixed, torch.bfloat16), to_dev(a, torch.bfloat16), to_dev(b, torch.bfloat16),
                  to_dev(a_log, torch.float32), to_dev(dt_bias, torch.float32), out=out, pos_out=pos_next, q_out=q_out)
-        qd = check_prep_and_sync(host, dev, mixed, a, b, a_log, dt_bias, pos, H, "f32", q_out)
+        qd = check_prep_and_sync(host, dev, mixed, a, b, a_log, dt_bias, pos, H, gname, q_out)
         ref_out = O.replay_step(host, qd, pos, out_dtype="f32")
         assert O.relative_l2(to_np(out), ref_out) < TOL_F32_KERNEL, t
         flushed = pos == L - 1
