@@ -76,8 +76,13 @@ __device__ __forceinline__ bool cta_wait2(uint64_t* bar, uint32_t parity, uint32
 }
 
 // I8: the checkpoint holds int8 codes ("vblock_int8"); see gdnr_head.cuh.
+// CTAs per SM the register budget is sized for (6 x 128 threads: 80 registers; the
+// int8 variants then spill a few bytes in the flush, which costs less than the lower
+// occupancy of a larger budget -- 22 vs 26.5 us non-flush, 99 vs 108 us flush, same-box A/B)
+constexpr int S2_MIN_BLOCKS = 6;
+
 template <bool FUSED, bool I8>
-__global__ void __launch_bounds__(128, I8 ? 4 : 6) step2_kernel(const __grid_constant__ StepParams p) {
+__global__ void __launch_bounds__(128, S2_MIN_BLOCKS) step2_kernel(const __grid_constant__ StepParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int hv = blockIdx.x, b = blockIdx.y, z = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
