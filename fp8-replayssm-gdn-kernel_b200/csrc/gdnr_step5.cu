@@ -1,5 +1,7 @@
 // Persistent warp-specialised GDN decode step (sm_100a) for E4M3 checkpoints
-// with rings of 4 <= L <= 16: every head whose ring is not full.
+// with rings of 4 <= L <= 16: every head whose ring is not full.  INT8
+// checkpoints (template flag I8) run the variant without the flush path: the
+// team readout on the integer tensor path against T in int8 limbs.
 //
 // Work unit: the (up to) two value heads of one key head that share the key
 // ring and the query (G = HV/H value heads per key head; a unit holds
@@ -428,7 +430,10 @@ __device__ __forceinline__ uint32_t s5_t8_off(int h, int j, int lane) {
   return uint32_t((h * 8 + j) * T8STR + lane * 4);
 }
 
-template <int HPU, bool TC>
+// I8 (int8 checkpoint, team readout only): four int8 limbs per head instead,
+// T sigma = sum_j limb_j 128^-j with max |T sigma| in [32, 64) (x - rint(x) is
+// exact, so every residual times 128 stays within +-64), rows 4..7 zero.
+template <int HPU, bool TC, bool I8 = false>
 __device__ __forceinline__ void s5_tsplit(const float (*Tq)[4], uint8_t* t8, float* misc, int lane) {
   float m[HPU];
 #pragma unroll
@@ -438,6 +443,37 @@ __device__ __forceinline__ void s5_tsplit(const float (*Tq)[4], uint8_t* t8, flo
   for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
     for (int h = 0; h < HPU; ++h) m[h] = fmaxf(m[h], __shfl_xor_sync(0xffffffffu, m[h], o));
+  if constexpr (I8) {
+    static_assert(!TC, "int8 limbs feed the team readout only");
+    float x[HPU][4], sig[HPU];
+#pragma unroll
+    for (int h = 0; h < HPU; ++h) {
+      sig[h] = s5_pow2_scale(m[h]) * (1.0f / 256.0f);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) x[h][i] = Tq[h][i] * sig[h];
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+#pragma unroll
+      for (int h = 0; h < HPU; ++h) {
+        uint32_t w = 0u;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float r = rintf(x[h][i]);
+          w |= (uint32_t(__float2int_rn(r)) & 0xFFu) << (8 * i);
+          x[h][i] = (x[h][i] - r) * 128.0f;
+        }
+        *reinterpret_cast<uint32_t*>(t8 + s5_t8_off<TC>(h, j, lane)) = w;
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < HPU; ++h) {
+#pragma unroll
+      for (int j = 4; j < 8; ++j) *reinterpret_cast<uint32_t*>(t8 + s5_t8_off<TC>(h, j, lane)) = 0u;
+      if (lane == 0) misc[h * 4] = 1.0f / sig[h];
+    }
+    return;
+  }
   float x[HPU][4], sig[HPU];
 #pragma unroll
   for (int h = 0; h < HPU; ++h) {
@@ -654,7 +690,7 @@ __device__ __forceinline__ void s5_tloop(const uint8_t* kbuf, float wj, int n, f
 
 // The chain of one unit (one warp, both heads).  kbuf: the unit's key ring
 // (swizzled, slots < nmem loaded); res: this warp's result block.
-template <bool FUSED, int HPU, bool FLUSH>
+template <bool FUSED, int HPU, bool FLUSH, bool I8 = false>
 __device__ __forceinline__ S5Append s5_chain(const StepParams& p, const S5Unit& U, int code, const S5In& in,
                                              uint8_t* kbuf, uint8_t* res, const S5Layout& lay, int lane) {
   S5Append ap{};
@@ -933,14 +969,17 @@ __device__ __forceinline__ S5Append s5_chain(const StepParams& p, const S5Unit& 
   }
   s5_tloop<HPU>(kbuf, wj, n, T, lane);
   __syncwarp();  // q-split / Gram scratch (aliases t8) is dead from here on
-  s5_tsplit<HPU, s5_tc<HPU, FLUSH>()>(T, res + lay.t8, misc, lane);
+  s5_tsplit<HPU, s5_tc<HPU, FLUSH>(), I8>(T, res + lay.t8, misc, lane);
   return ap;
 }
 
 // Readout of MW m-tiles (rows rbase .. rbase + 16 MW - 1) of one head by one
 // warp: pre-scale o(row) = (S_fp8 . T) / sigma * scale(row) + V^T c into ost[row].
 // Lane sc_base + v of sc holds the scale of vblock v of these rows.
-template <int MW>
+// I8: the tile holds int8 codes and t8 four int8 limbs of T (s5_tsplit): the
+// tile product runs on the integer tensor path (exact s32 sums, below 2^24 so
+// they convert to f32 exactly) and the ring product into its own f32 accumulator.
+template <int MW, bool I8 = false>
 __device__ __forceinline__ void s5_readout(const uint8_t* ck_s, const uint8_t* vr_s, const uint8_t* t8,
                                            const uint16_t* cb, float inv_sig, float sc, int sc_base, int rbase,
                                            int nmem, float* ost, int lane) {
@@ -965,17 +1004,24 @@ __device__ __forceinline__ void s5_readout(const uint8_t* ck_s, const uint8_t* v
   for (int pr = 0; pr < MW / 2; ++pr) {
     const int rp = rbase + 32 * pr;
     float acc[2][4];
+    int32_t iacc[2][4];
 #pragma unroll
     for (int m = 0; m < 2; ++m)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) acc[m][i] = 0.0f;
+      for (int i = 0; i < 4; ++i) {
+        acc[m][i] = 0.0f;
+        iacc[m][i] = 0;
+      }
 #pragma unroll
     for (int ks = 0; ks < 4; ++ks) {
 #pragma unroll
       for (int m = 0; m < 2; ++m) {
         uint32_t a[4];
         s5_ldsm_x4(ck_addr + s0_off(rp + 16 * m + r8 + 8 * (mi & 1), 2 * ks + (mi >> 1)), a);
-        mma16832_e4m3(acc[m], a, bt[ks][0], bt[ks][1]);
+        if constexpr (I8)
+          mma16832_s8(iacc[m], a, bt[ks][0], bt[ks][1]);
+        else
+          mma16832_e4m3(acc[m], a, bt[ks][0], bt[ks][1]);
       }
     }
 #pragma unroll
@@ -990,12 +1036,25 @@ __device__ __forceinline__ void s5_readout(const uint8_t* ck_s, const uint8_t* v
     }
     // column weights: t4 = 0 -> terms 0,1; 1 -> terms 2,3; 2 -> term 4, ring; 3 -> ring, ring
     const float wsc = inv_sig * __shfl_sync(0xffffffffu, sc, sc_base + pr);
-    const float w0 = t4 == 0 ? wsc : (t4 == 1 ? wsc * (1.0f / 256.0f) : (t4 == 2 ? wsc * (1.0f / 65536.0f) : 1.0f));
-    const float w1 = t4 == 0 ? wsc * (1.0f / 16.0f) : (t4 == 1 ? wsc * (1.0f / 4096.0f) : 1.0f);
-    // v = (m0 row g8, m0 row g8+8, m1 row g8, m1 row g8+8), summed over the quad as a
-    // transpose-reduce: lane t4 ends with m-tile t4 & 1, row half t4 >> 1
-    const float v0 = fmaf(acc[0][1], w1, acc[0][0] * w0), v1 = fmaf(acc[0][3], w1, acc[0][2] * w0);
-    const float v2 = fmaf(acc[1][1], w1, acc[1][0] * w0), v3 = fmaf(acc[1][3], w1, acc[1][2] * w0);
+    float v0, v1, v2, v3;
+    if constexpr (I8) {
+      // limb weights: t4 = 0 -> limbs 0, 1; 1 -> limbs 2, 3; the ring columns (t4 >= 2) are in acc
+      const float w0 = t4 == 0 ? wsc : (t4 == 1 ? wsc * (1.0f / 16384.0f) : 0.0f);
+      const float w1 = t4 == 0 ? wsc * (1.0f / 128.0f) : (t4 == 1 ? wsc * (1.0f / 2097152.0f) : 0.0f);
+      v0 = fmaf(float(iacc[0][1]), w1, float(iacc[0][0]) * w0) + (acc[0][0] + acc[0][1]);
+      v1 = fmaf(float(iacc[0][3]), w1, float(iacc[0][2]) * w0) + (acc[0][2] + acc[0][3]);
+      v2 = fmaf(float(iacc[1][1]), w1, float(iacc[1][0]) * w0) + (acc[1][0] + acc[1][1]);
+      v3 = fmaf(float(iacc[1][3]), w1, float(iacc[1][2]) * w0) + (acc[1][2] + acc[1][3]);
+    } else {
+      const float w0 = t4 == 0 ? wsc : (t4 == 1 ? wsc * (1.0f / 256.0f) : (t4 == 2 ? wsc * (1.0f / 65536.0f) : 1.0f));
+      const float w1 = t4 == 0 ? wsc * (1.0f / 16.0f) : (t4 == 1 ? wsc * (1.0f / 4096.0f) : 1.0f);
+      // v = (m0 row g8, m0 row g8+8, m1 row g8, m1 row g8+8)
+      v0 = fmaf(acc[0][1], w1, acc[0][0] * w0);
+      v1 = fmaf(acc[0][3], w1, acc[0][2] * w0);
+      v2 = fmaf(acc[1][1], w1, acc[1][0] * w0);
+      v3 = fmaf(acc[1][3], w1, acc[1][2] * w0);
+    }
+    // summed over the quad as a transpose-reduce: lane t4 ends with m-tile t4 & 1, row half t4 >> 1
     const bool odd = t4 & 1;
     float x0 = odd ? v2 : v0, x1 = odd ? v3 : v1;
     x0 += __shfl_xor_sync(0xffffffffu, odd ? v0 : v2, 1);
@@ -1345,10 +1404,12 @@ __device__ __forceinline__ void s5_flush_task(const StepParams& p, uint8_t* smem
 }
 
 // SIDX: packed decode (state slots through StepParams::sidx)
-template <bool FUSED, int HPU, bool FLUSH, bool SIDX>
+// I8: int8 checkpoint codes ("vblock_int8"); the variant without the flush path only
+template <bool FUSED, int HPU, bool FLUSH, bool SIDX, bool I8 = false>
 __global__ void __launch_bounds__(S5_THREADS, 1)
     step5_kernel(const __grid_constant__ StepParams p, const __grid_constant__ CUtensorMap ck_map,
                  const __grid_constant__ CUtensorMap kr_map, const __grid_constant__ CUtensorMap vr_map) {
+  static_assert(!(I8 && (FLUSH || SIDX)), "int8 checkpoints: the non-flush, slot-free variant only");
   extern __shared__ __align__(1024) uint8_t smem[];
   constexpr bool TC = s5_tc<HPU, FLUSH>();
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1636,7 +1697,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       const int code = s5_code<FUSED>(in0.pos, in0.flag, L, FLUSH);
       const bool work = ok && !s5_skip(code);
       S5Append ap{};
-      if (work) ap = s5_chain<FUSED, HPU, FLUSH>(p, U, code, in0, kbuf, res, lay, lane);
+      if (work) ap = s5_chain<FUSED, HPU, FLUSH, I8>(p, U, code, in0, kbuf, res, lay, lane);
       // the T operand is read by the tensor cores (async proxy)
       if (TC) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
@@ -1812,7 +1873,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       const S5Unit U = s5_unit<SIDX>(bid + i * grid, p, G, geo);
       const uint8_t* res = smem + lay.res0 + ccw * lay.res_bytes;
       const float* misc = reinterpret_cast<const float*>(res + lay.misc) + head_r * 4;
-      s5_readout<MW>(sb + lay.ck + head_r * 16384, sb + lay.vr + head_r * 4096, res + lay.t8 + head_r * 8 * T8STR,
+      s5_readout<MW, I8>(sb + lay.ck + head_r * 16384, sb + lay.vr + head_r * 4096, res + lay.t8 + head_r * 8 * T8STR,
                      reinterpret_cast<const uint16_t*>(res + lay.cb + head_r * 96), misc[0], sc, sc_base, rbase,
                      s5_nmem(code), ost, lane);
       __syncwarp();
@@ -1885,7 +1946,10 @@ static bool s5_grid(const StepParams& p, int& grid, S5Layout& lay) {
 }
 
 bool step5_eligible(const StepParams& p, bool fused, bool f32ck) {
-  if (f32ck || p.ck_i8 || p.L < 4 || p.L > STEP2_MAX_L) return false;
+  if (f32ck || p.L < 4 || p.L > STEP2_MAX_L) return false;
+  // int8 checkpoints: the non-flush variant only (a flush-capable call runs the
+  // one-CTA-per-head kernel), and no slot indirection
+  if (p.ck_i8 && (p.flush_hint != GDNR_FLUSH_NONE || p.sidx)) return false;
   const int G = p.HV / p.H;
   if (G != 1 && G % 2 != 0) return false;
   if (p.ck_sb % 16 || p.ck_sh % 16 || reinterpret_cast<uintptr_t>(p.ck) % 16) return false;
@@ -1923,10 +1987,10 @@ static S5EncodeFn s5_encode_fn() {
   return fn;
 }
 
-template <bool FUSED, int HPU, bool FLUSH, bool SIDX = false>
+template <bool FUSED, int HPU, bool FLUSH, bool SIDX = false, bool I8 = false>
 static cudaError_t s5_launch(const StepParams& p, const CUtensorMap& ck, const CUtensorMap& kr,
                              const CUtensorMap& vr, int grid, uint32_t smem, bool pdl, cudaStream_t stream) {
-  auto kern = step5_kernel<FUSED, HPU, FLUSH, SIDX>;
+  auto kern = step5_kernel<FUSED, HPU, FLUSH, SIDX, I8>;
   static int configured = 0;
   if (int(smem) > configured) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
@@ -1982,6 +2046,14 @@ cudaError_t launch_step5(const StepParams& p, bool fused, bool pdl, cudaStream_t
   // skipped and reported); otherwise the flush-capable one
   const bool flush = p.flush_hint != GDNR_FLUSH_NONE;
   const uint32_t sm = lay.total;
+  if (p.ck_i8) {  // int8 checkpoints: GDNR_FLUSH_NONE steps only (step5_eligible)
+    if (flush || p.sidx) return cudaErrorNotSupported;
+    if (fused)
+      return g.hpu == 2 ? s5_launch<true, 2, false, false, true>(p, ck, kr, vr, grid, sm, pdl, stream)
+                        : s5_launch<true, 1, false, false, true>(p, ck, kr, vr, grid, sm, pdl, stream);
+    return g.hpu == 2 ? s5_launch<false, 2, false, false, true>(p, ck, kr, vr, grid, sm, pdl, stream)
+                      : s5_launch<false, 1, false, false, true>(p, ck, kr, vr, grid, sm, pdl, stream);
+  }
   if (fused && p.sidx) {
     if (g.hpu == 2)
       return flush ? s5_launch<true, 2, true, true>(p, ck, kr, vr, grid, sm, pdl, stream)

@@ -148,3 +148,68 @@ def test_int8_checkpoint_rejected_where_not_built(cuda_device):
             to_dev(a_log, torch.float32), to_dev(dt_bias, torch.float32), 128 ** -0.5, pool,
             torch.empty(2, 1, 4, 128, dtype=torch.bfloat16, device="cuda"),
             torch.tensor([1, 2], dtype=torch.int32, device="cuda"))
+
+
+@pytest.mark.parametrize("heads", [(2, 4), (2, 2)])
+def test_int8_replay_nonflush_persistent_matches_oracle(cuda_device, heads):
+    """flush_hint="none" runs the persistent kernel's int8 variant (integer
+    tensor-core team readout); "auto" runs the one-CTA-per-head kernel."""
+    H, HV = heads
+    B, L = 5, 16
+    d, ck, dev = setup_case(46, B, L, H=H, HV=HV)
+    valid = np.array([L, 1, 0, 9, 4], np.int32)
+    ref, _ = oracle_replay_out(O.dequantize_checkpoint(ck), d["q"], d["k"], d["v"], d["g"], d["beta"], valid)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    outs = {}
+    for hint in ("none", "auto"):
+        out = torch.empty(B, HV, 128, dtype=torch.float32, device="cuda")
+        gdnr.gdn_replay_fp8(dev["checkpoint"], dev["scale"], dev["q"], dev["k"], dev["v"], dev["g"], dev["beta"],
+                            to_dev(valid, torch.int32), torch.zeros(B, dtype=torch.bool, device="cuda"), out=out,
+                            flush_hint=hint, error_flag=err)
+        outs[hint] = to_np(out)
+        for b in range(B):
+            assert O.relative_l2(outs[hint][b], ref[b]) < TOL_F32_KERNEL, (hint, b)
+    assert int(err.item()) == 0
+    assert np.array_equal(to_np(dev["checkpoint"]), ck.payload)
+
+
+@pytest.mark.parametrize("heads", [(2, 4), (2, 2)])
+def test_int8_fused_persistent_cycles_match_oracle(cuda_device, heads):
+    """Ring cycles with every sequence at the same position: the non-flush steps
+    pass flush_hint="none" (the persistent kernel's int8 variant), the flush
+    step "auto" (the one-CTA-per-head kernel)."""
+    rng = np.random.default_rng(47)
+    (H, HV), B, L = heads, 4, 4
+    a_log, dt_bias = gate_params(rng, HV)
+    s0 = (0.02 * rng.standard_normal((B, HV, 128, 128))).astype(np.float32)
+    q0 = O.quantize_checkpoint(s0, "vblock_int8", 32)
+    host = O.RingState(q0.payload.copy(), q0.scale.copy(), np.zeros((B, L, H, 128), np.float32),
+                       np.zeros((B, L, HV, 128), np.float32), np.zeros((B, L, HV), np.float32),
+                       np.zeros((B, L, HV), np.float32))
+    dev = gdnr.ReplayState.allocate(B, H, HV, L, scale_dtype=torch.float32, gate_dtype=torch.float32,
+                                    checkpoint_dtype=torch.int8)
+    dev.load_state(to_dev(s0, torch.float32))
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    pos_next = torch.empty_like(dev.pos)
+    for t in range(2 * L + 1):
+        p = t % L
+        pos = np.full(B, p, np.int32)
+        dev.pos.copy_(to_dev(pos, torch.int32))
+        mixed, a, b = raw_inputs(rng, B, H, HV)
+        out = torch.empty(B, HV, 128, dtype=torch.float32, device="cuda")
+        q_out = torch.empty(B, H, 128, dtype=torch.bfloat16, device="cuda")
+        dev.step(to_dev(mixed, torch.bfloat16), to_dev(a, torch.bfloat16), to_dev(b, torch.bfloat16),
+                 to_dev(a_log, torch.float32), to_dev(dt_bias, torch.float32), out=out, pos_out=pos_next, q_out=q_out,
+                 error_flag=err, flush_hint="auto" if p == L - 1 else "none")
+        qd = check_prep_and_sync(host, dev, mixed, a, b, a_log, dt_bias, pos, H, "f32", q_out)
+        ref_out = O.replay_step(host, qd, pos, out_dtype="f32")
+        assert O.relative_l2(to_np(out), ref_out) < TOL_F32_KERNEL, t
+        if p == L - 1:
+            got_payload = to_np(dev.checkpoint)
+            got_scale = dev.scale.float().cpu().numpy()
+            for i in range(B):
+                assert np.mean(got_payload[i] != host.payload[i]) < TOL_CODE_MISMATCH
+                assert np.allclose(got_scale[i], host.scale[i].astype(np.float32), rtol=2e-3)
+            host.payload[:] = got_payload
+            host.scale[:] = got_scale.astype(np.float16)
+    assert int(err.item()) == 0
