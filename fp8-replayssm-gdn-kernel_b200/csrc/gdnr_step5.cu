@@ -481,7 +481,7 @@ __device__ __forceinline__ void s5_tsplit(const float (*Tq)[4], uint8_t* t8, flo
 #pragma unroll
     for (int i = 0; i < 4; ++i) x[h][i] = Tq[h][i] * sig[h];
   }
-#pragma unroll 1
+#pragma unroll
   for (int j = 0; j < 5; ++j) {
 #pragma unroll
     for (int h = 0; h < HPU; ++h) {
