@@ -1,22 +1,24 @@
-// The GDN decode step on an FP8 checkpoint + ring, B200 path for rings of
-// L <= 16 slots (the production windows 4/8/16).
+// The GDN decode step on an FP8 (E4M3) or INT8 checkpoint + ring, B200 path for
+// rings of L <= 16 that the persistent kernel (gdnr_step5.cu) does not take:
+// L < 4, rows or rings not 16-byte aligned, and the flush-capable calls on
+// INT8 checkpoints.
 //
 // One CTA owns one (sequence b, value head hv) and `rows` value rows
 // (128 = the whole head); warp w owns value rows [32w, 32w+32) -- exactly one
-// vblock, i.e. one FP8 scale.
+// vblock, i.e. one scale.
 //
 //  * The warp's 4 KiB of checkpoint is prefetched into registers with
 //    coalesced 16-byte loads issued first thing, then parked in shared memory
 //    in a 16-byte XOR swizzle (conflict-free tensor-core fragment reads).
 //  * The ring (k rows and this tile's v rows) arrives by bulk TMA copies into
 //    row-padded shared memory.
-//  * Non-flush: warp 0 runs the backward T-chain
+//  * Non-flush: warp 0 runs the backward T-chain in Gram form
 //    (prototype/gdn_replayssm_fp8_kernel.py:121-176); the readout
-//      o = scale (S_fp8 . T) + sum_t c_t v_t        (then * K^-1/2)
-//    is one tensor-core product per 16-row tile: S_fp8 (exact in f16) times
-//    [T_hi | T_lo] (T split into two power-of-two-scaled f16 halves), plus the
-//    ring term V^T [c_hi | c_mid | c_lo] as a bf16 product into separate
-//    accumulator columns.
+//      o = scale (S . T) + sum_t c_t v_t        (then * K^-1/2)
+//    is one tensor-core product per 16-row tile straight from the 8-bit tile:
+//    E4M3 against T split into five power-of-two-scaled e4m3 terms, INT8
+//    against four int8 limbs (integer MMA, exact s32 sums), plus V^T c as a
+//    bf16 product (gdnr_head.cuh).
 //  * Flush (ring full): the state rebuild runs in WY/Gram form on tensor
 //    cores (mma.sync m16n8k16, f32 accumulate):
 //      E = S0 [K;q]^T,  G = K K^T
@@ -26,8 +28,9 @@
 //    M[j][t] = prod_{j<m<=t} gamma_m G[j][t] -- algebraically the reference's
 //    token loop S <- gamma S; S += beta (v - S k) k^T (ref.py:137-163).  The
 //    E accumulators become, after the per-row recurrence, the A fragments of
-//    the S_L product in registers.  S_L is re-quantised per vblock
-//    (ref.py:40-106) and written back in place.
+//    the S_L product in registers.  S_L is re-quantised per vblock in the
+//    checkpoint's format (ref.py:40-106; int8: ref.py:44-47, :96-97) and
+//    written back in place.
 // In fused mode the prep stage (q/k L2 norm, gates, ring append,
 // kern.py:453-576) runs first and the new token joins this step's replay.
 #include "gdnr_device.cuh"
