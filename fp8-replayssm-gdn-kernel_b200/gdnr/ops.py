@@ -259,7 +259,9 @@ def gdn_fused_step(
     ``pos[b]``, replays slots ``0..pos[b]`` against the FP8 checkpoint, writes
     ``out`` [B,HV,V] (or [B,1,HV,V]), and when ``pos[b] == L-1`` rebuilds the
     state and re-quantises the checkpoint in place.  ``pos_out`` (optional,
-    distinct from ``pos``) receives ``(pos+1) % L``.
+    distinct from ``pos``) receives ``(pos+1) % L``.  The checkpoint is
+    float8_e4m3fn, int8 (the "vblock_int8" option, L <= 16: re-quantised to
+    int8 on a flush) or float32 (full precision, no scales).
 
     ``flush_hint``: "auto" (some sequences may be at ``L-1``: the
     flush-capable kernel decides per sequence on the device), "none" (no
