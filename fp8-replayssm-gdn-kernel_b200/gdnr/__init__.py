@@ -20,6 +20,7 @@ from .ops import (  # noqa: F401
     quantize_checkpoint,
     read_device_error,
 )
+from . import capture  # noqa: F401
 from .shard import ShardPlan, gather_shards, max_over_ranks, shard_range  # noqa: F401
 from .state import ReplayState  # noqa: F401
 
