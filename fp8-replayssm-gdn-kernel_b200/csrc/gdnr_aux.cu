@@ -503,11 +503,13 @@ int gdnr_replay_split_static(const gdnr_replay_split_static_args* a, void* strea
   if (a->k_ring.ndim != 4 || a->v_ring.ndim != 4)
     return set_error(GDNR_ERR_ARG, "k_ring and v_ring must be 4-D [B,L,H,K] / [B,L,HV,V]");
   const int64_t B = a->k_ring.shape[0], L = a->k_ring.shape[1], HV = a->v_ring.shape[2];
-  if (B < 0 || HV < 0 || B * HV > GDNR_SPLIT_STATIC_MAX_PAIRS)
+  if (B < 0 || HV < 0) return set_error(GDNR_ERR_ARG, "gdnr_replay_split_static: negative extent");
+  // each factor is bounded before the product is formed, so B*HV cannot overflow
+  if (B > GDNR_SPLIT_STATIC_MAX_PAIRS || HV > GDNR_SPLIT_STATIC_MAX_PAIRS || B * HV > GDNR_SPLIT_STATIC_MAX_PAIRS)
     return set_error(GDNR_ERR_UNSUPPORTED,
-                     "gdnr_replay_split_static: B*HV = %lld above the static scratch's %d (sequence, value head) "
-                     "pairs; use gdnr_replay_split with caller buffers",
-                     static_cast<long long>(B * HV), GDNR_SPLIT_STATIC_MAX_PAIRS);
+                     "gdnr_replay_split_static: B = %lld, HV = %lld exceed the static scratch's %d (sequence, value "
+                     "head) pairs; use gdnr_replay_split with caller buffers",
+                     static_cast<long long>(B), static_cast<long long>(HV), GDNR_SPLIT_STATIC_MAX_PAIRS);
   if (L < 1 || L > GDNR_SPLIT_STATIC_MAX_L)
     return set_error(GDNR_ERR_UNSUPPORTED, "gdnr_replay_split_static: ring length %lld outside [1, %d]",
                      static_cast<long long>(L), GDNR_SPLIT_STATIC_MAX_L);

@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+#include <mutex>
 #include <string>
 
 #include "../../include/gdnr.h"
@@ -109,6 +111,31 @@ __host__ __device__ inline SmemLayout step_smem_layout(int G, int L, int rows, i
 
 // Largest dynamic shared memory one CTA may use on sm_100 (227 KiB).
 constexpr uint32_t MAX_DYN_SMEM = 227u * 1024u;
+
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) acts on the current device
+// only, so the size a kernel has been allowed is cached per device ordinal;
+// one cache object per kernel instantiation.  Raising is serialised by a
+// mutex (the attribute is only ever raised, never lowered); the fast path is
+// one acquire load.
+struct DynSmemCache {
+  static constexpr int kMaxDevices = 64;
+  std::atomic<int> allowed[kMaxDevices] = {};
+  std::mutex mu;
+};
+
+inline cudaError_t ensure_dyn_smem(const void* func, int bytes, DynSmemCache& c) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const bool cached = dev >= 0 && dev < DynSmemCache::kMaxDevices;
+  if (cached && c.allowed[dev].load(std::memory_order_acquire) >= bytes) return cudaSuccess;
+  std::lock_guard<std::mutex> lock(c.mu);
+  if (cached && c.allowed[dev].load(std::memory_order_relaxed) >= bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return e;
+  if (cached) c.allowed[dev].store(bytes, std::memory_order_release);
+  return cudaSuccess;
+}
 
 cudaError_t launch_step(const StepParams& p, bool fused, bool f32ck, int group, cudaStream_t stream);
 // B200 path for E4M3 or INT8 checkpoints and rings of L <= 16 (one CTA per value head)

@@ -392,12 +392,9 @@ static cudaError_t launch_t(const StepParams& p, cudaStream_t stream) {
   const int esz = F32CK ? 4 : 1;
   const SmemLayout s = step_smem_layout(G, p.L, p.rows, esz);
   auto kern = step_kernel<FUSED, F32CK, G>;
-  static int configured = 0;  // largest dynamic smem size already allowed for this instance
-  if (int(s.total) > configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(s.total));
-    if (e != cudaSuccess) return e;
-    configured = int(s.total);
-  }
+  static DynSmemCache smem_cache;  // per device: dynamic smem already allowed for this instance
+  cudaError_t e = ensure_dyn_smem(reinterpret_cast<const void*>(kern), int(s.total), smem_cache);
+  if (e != cudaSuccess) return e;
   dim3 grid(p.H, p.B, 128 / p.rows);
   kern<<<grid, 256, s.total, stream>>>(p);
   return cudaGetLastError();

@@ -262,12 +262,9 @@ __global__ void __launch_bounds__(128, S2_MIN_BLOCKS) step2_kernel(const __grid_
 template <bool FUSED, bool I8>
 static cudaError_t launch_step2_t(const StepParams& p, cudaStream_t stream) {
   const Smem2 s = step2_smem(p.L, p.rows);
-  static int configured = 0;  // largest dynamic smem size already allowed for this instance
-  if (int(s.total) > configured) {
-    cudaError_t e = cudaFuncSetAttribute(step2_kernel<FUSED, I8>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(s.total));
-    if (e != cudaSuccess) return e;
-    configured = int(s.total);
-  }
+  static DynSmemCache smem_cache;  // per device: dynamic smem already allowed for this instance
+  cudaError_t e = ensure_dyn_smem(reinterpret_cast<const void*>(step2_kernel<FUSED, I8>), int(s.total), smem_cache);
+  if (e != cudaSuccess) return e;
   step2_kernel<FUSED, I8><<<dim3(p.HV, p.B, 128 / p.rows), p.rows, s.total, stream>>>(p);
   return cudaGetLastError();
 }

@@ -315,6 +315,27 @@ __device__ __noinline__ bool s5_wait_slow(uint64_t* bar, uint32_t parity, uint32
   return false;
 }
 
+// Abort path only: a bounded wait for an mbarrier phase that ignores *abort, so
+// that copies and tensor-core work this CTA has already issued are finished
+// before it releases its tensor memory or exits.
+__device__ __noinline__ bool s5_drain_wait(uint64_t* bar, uint32_t parity) {
+  const uint32_t a = smem_addr(bar);
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1; it < WAIT_LIMIT_ITERS; ++it) {
+    if (mbar_try_wait(a, parity)) return true;
+    if ((it & 63u) == 0 && globaltimer_ns() - t0 > WAIT_LIMIT_NS) return false;
+  }
+  return false;
+}
+
+// Abort path only: the stage loads of the last min(issued, S5_NS) units, the
+// only ones that can still be in flight (a stage is reloaded only after its
+// previous load was waited for, and no load is issued once *abort is set).
+__device__ __noinline__ void s5_drain_stages(uint64_t* full, int issued) {
+  for (int u = issued > S5_NS ? issued - S5_NS : 0; u < issued; ++u)
+    s5_drain_wait(&full[u % S5_NS], uint32_t((u / S5_NS) & 1));
+}
+
 __device__ __forceinline__ bool s5_wait(uint64_t* bar, uint32_t parity, uint32_t* err, volatile int* abort) {
   if (s5_test_wait(bar, parity)) return true;
   return s5_wait_slow(bar, parity, err, abort);
@@ -1315,6 +1336,22 @@ __device__ __forceinline__ void s5_st_release(uint32_t* p, uint32_t v) {
   asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_addr(p)), "r"(v) : "memory");
 }
 
+// Abort path only (tensor-memory readout): the scheduler publishes how many
+// unit commits it issued when it stops; the commit of the last one arrives
+// once every tensor-core operation of the CTA has completed.  Bounded waits
+// for both, ignoring *abort, before the tensor memory is released.
+__device__ __noinline__ void s5_drain_mma(uint64_t* mmab, const uint32_t* ncommit) {
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t n = s5_ld_acquire(ncommit);
+  for (uint32_t it = 1; n == 0xffffffffu && it < WAIT_LIMIT_ITERS; ++it) {
+    __nanosleep(64);
+    n = s5_ld_acquire(ncommit);
+    if ((it & 63u) == 0 && globaltimer_ns() - t0 > WAIT_LIMIT_NS) break;
+  }
+  if (n == 0xffffffffu || n == 0u) return;
+  s5_drain_wait(&mmab[(n - 1) % S5_NS], ((n - 1) / S5_NS) & 1u);
+}
+
 __device__ __forceinline__ void s5_add_release(uint32_t* p, uint32_t v) {
   asm volatile("red.release.cta.shared::cta.add.u32 [%0], %1;" ::"r"(smem_addr(p)), "r"(v) : "memory");
 }
@@ -1457,6 +1494,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       vdone[st] = 0u;
     }
     *abort = aligned ? 0 : 1;
+    reinterpret_cast<volatile int*>(smem + lay.tmem)[1] = -1;  // commits issued, published by the scheduler at exit
     fence_mbar_init();
     if (!aligned) atomicOr(p.err, GDNR_DEVERR_WAIT_TIMEOUT);
   }
@@ -1628,7 +1666,8 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       const uint64_t t0 = globaltimer_ns();
       for (uint32_t it = 0; (nl < nu || nm < nu) && it < WAIT_LIMIT_ITERS; ++it) {
         bool progress = false;
-        while (nl < nu && (nl < S5_NS || s5_test_wait(&empty[nl % S5_NS], uint32_t(((nl / S5_NS) - 1) & 1)))) {
+        while (nl < nu && (nl < S5_NS || s5_test_wait(&empty[nl % S5_NS], uint32_t(((nl / S5_NS) - 1) & 1))) &&
+               !*abort) {
           load_unit(nl++);
           progress = true;
         }
@@ -1659,14 +1698,20 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
         }
       }
       if (nl < nu || nm < nu) {
+        if (!*abort) atomicOr(p.err, GDNR_DEVERR_WAIT_TIMEOUT);
         *abort = 1;
-        atomicOr(p.err, GDNR_DEVERR_WAIT_TIMEOUT);
       }
+      // the readout's tensor-memory release waits for the last commit issued
+      s5_st_release(reinterpret_cast<uint32_t*>(smem + lay.tmem) + 1, uint32_t(nm));
+      if (*abort) s5_drain_stages(full, nl);
     } else {
-      for (int i = 0; i < nu; ++i) {
-        if (i >= S5_NS && !s5_wait(&empty[i % S5_NS], ((i / S5_NS) - 1) & 1, p.err, abort)) return;
-        load_unit(i);
+      int nl = 0;
+      for (; nl < nu; ++nl) {
+        if (nl >= S5_NS && !s5_wait(&empty[nl % S5_NS], ((nl / S5_NS) - 1) & 1, p.err, abort)) break;
+        if (*abort) break;  // read after the wait: a stage released under abort may still be loading
+        load_unit(nl);
       }
+      if (*abort) s5_drain_stages(full, nl);
     }
     return;
   }
@@ -1681,12 +1726,13 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
         // the key ring and result block are free once both readout warps of
         // this warp's previous unit are done with them
         ok = s5_warp_wait(&rbar[cw], uint32_t((k - 1) & 1), p.err, abort, lane);
+        if (!ok) break;  // abort: this warp issues no further loads
         // every lane's earlier generic accesses to kbuf, ordered before the
         // copy engine overwrites it
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
         if (lane == 0) {
-          const int nr = ok && U.s >= 0 ? nreq_k : 0;
+          const int nr = U.s >= 0 ? nreq_k : 0;
           mbar_arrive_expect_tx(&kfull[cw], uint32_t(nr) * box_bytes);
           for (int j = 0; j < nr; ++j)
             s5_tma5(kbuf + j * box_bytes, &kr_map, 0, 0, U.h, j * geo.rb, U.s, &kfull[cw]);
@@ -1694,6 +1740,11 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
         in0 = s5_fetch<FUSED, HPU, FLUSH>(p, U, lane);
       }
       ok = s5_warp_wait(&kfull[cw], k & 1, p.err, abort, lane) && ok;
+      if (!ok) {  // abort: the key-ring load of this unit may still be in flight
+        if (lane == 0) s5_drain_wait(&kfull[cw], uint32_t(k & 1));
+        __syncwarp();
+        break;
+      }
       const int code = s5_code<FUSED>(in0.pos, in0.flag, L, FLUSH);
       const bool work = ok && !s5_skip(code);
       S5Append ap{};
@@ -1806,7 +1857,9 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
     }
     // the last commit covers every MMA this CTA issued: complete before the
     // tensor memory is released
-    if (rw == 0 && nu > 0) s5_warp_wait(&mmab[(nu - 1) % S5_NS], uint32_t(((nu - 1) / S5_NS) & 1), p.err, abort, lane);
+    if (rw == 0 && nu > 0 &&
+        !s5_warp_wait(&mmab[(nu - 1) % S5_NS], uint32_t(((nu - 1) / S5_NS) & 1), p.err, abort, lane) && lane == 0)
+      s5_drain_mma(mmab, reinterpret_cast<const uint32_t*>(smem + lay.tmem) + 1);
     s5_tc_before_sync();
     asm volatile("bar.sync 1, %0;" ::"n"(32 * S5_NRW) : "memory");
     if (rw == 0) {
@@ -1991,12 +2044,9 @@ template <bool FUSED, int HPU, bool FLUSH, bool SIDX = false, bool I8 = false>
 static cudaError_t s5_launch(const StepParams& p, const CUtensorMap& ck, const CUtensorMap& kr,
                              const CUtensorMap& vr, int grid, uint32_t smem, bool pdl, cudaStream_t stream) {
   auto kern = step5_kernel<FUSED, HPU, FLUSH, SIDX, I8>;
-  static int configured = 0;
-  if (int(smem) > configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    if (e != cudaSuccess) return e;
-    configured = int(smem);
-  }
+  static DynSmemCache smem_cache;  // per device: dynamic smem already allowed for this instance
+  cudaError_t e = ensure_dyn_smem(reinterpret_cast<const void*>(kern), int(smem), smem_cache);
+  if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(S5_THREADS);
@@ -2077,3 +2127,58 @@ cudaError_t launch_step5(const StepParams& p, bool fused, bool pdl, cudaStream_t
 }
 
 }  // namespace gdnr
+
+// ---------------------------------------------------------------- bounded-wait self-test
+namespace gdnr {
+
+// One CTA, two warps, exercising the error path of the persistent kernel's
+// waits (s5_wait / s5_wait_slow, the code every wait of step5_kernel runs):
+// warp 0 holds 32 tensor-memory columns and waits on an mbarrier that nothing
+// ever arrives on, warp 1 waits on another one.  Warp 0's wait gives up after
+// WAIT_LIMIT_NS, records GDNR_DEVERR_WAIT_TIMEOUT and sets the CTA's abort
+// word; warp 1's wait then returns at its next poll of that word.  Warp 0
+// releases its tensor memory before the kernel returns.  report[0..3]: the two
+// waits' results (0 = gave up) and the nanoseconds each waited.
+__global__ void __launch_bounds__(64, 1) s5_wait_selftest_kernel(uint32_t* err, unsigned long long* report) {
+  __shared__ __align__(8) uint64_t bars[2];
+  __shared__ int abort_word;
+  __shared__ uint32_t tmem_addr;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    abort_word = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 32;" ::"r"(smem_addr(&tmem_addr))
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  volatile int* abort = &abort_word;
+  if (lane == 0) {
+    const uint64_t t0 = globaltimer_ns();
+    const bool ok = s5_wait(&bars[warp], 0u, err, abort);
+    const uint64_t t1 = globaltimer_ns();
+    report[warp] = ok ? 1ull : 0ull;
+    report[2 + warp] = t1 - t0;
+    if (warp == 1 && !ok) return;  // an early exit of one warp: the other still releases its tensor memory
+  }
+  if (warp == 0) {
+    __syncwarp();
+    s5_tc_before_sync();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 32;" ::"r"(tmem_addr) : "memory");
+  }
+}
+
+}  // namespace gdnr
+
+extern "C" int gdnr_selftest_wait_timeout(uint32_t* error_flag, unsigned long long* report, void* stream) {
+  using namespace gdnr;
+  if (!report) return set_error(GDNR_ERR_ARG, "report: null pointer");
+  uint32_t* err = error_flag ? error_flag : default_error_word();
+  if (!err) return set_error(GDNR_ERR_CUDA, "device error word unavailable");
+  s5_wait_selftest_kernel<<<1, 64, 0, static_cast<cudaStream_t>(stream)>>>(err, report);
+  return cuda_status(cudaGetLastError(), "gdnr_selftest_wait_timeout launch");
+}

@@ -140,6 +140,7 @@ SIGNATURES = {
     "gdnr_version": ([], ctypes.c_char_p),
     "gdnr_abi_version": ([], ctypes.c_int),
     "gdnr_read_device_error": ([_U32P, ctypes.c_int], ctypes.c_int),
+    "gdnr_selftest_wait_timeout": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
 }
 
 _lib = None
@@ -209,3 +210,14 @@ def tensor_desc(t: torch.Tensor | None, require_cuda: bool = True) -> Tensor:
 
 def stream_handle(device: torch.device | None = None) -> ctypes.c_void_p:
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def call(name: str, args: ctypes.Structure, device: torch.device) -> None:
+    """Run entry point ``name`` on ``device``'s current stream with that device
+    current (the library configures and launches on the current device)."""
+    fn = getattr(load(), name)
+    if device.index is None or device.index == torch.cuda.current_device():
+        check(fn(ctypes.byref(args), stream_handle(device)))
+        return
+    with torch.cuda.device(device):
+        check(fn(ctypes.byref(args), stream_handle(device)))

@@ -121,7 +121,7 @@ def gdn_replay_fp8(
     args.error_flag = _err_ptr(error_flag)
     args.flush_hint = _flush_hint(flush_hint)
     args.launch_flags = LAUNCH_PDL if pdl else 0
-    _lib.check(_lib.load().gdnr_replay(ctypes.byref(args), _lib.stream_handle(q.device)))
+    _lib.call("gdnr_replay", args, q.device)
     return out
 
 
@@ -166,7 +166,7 @@ def gdn_replay_fp8_split(
     args.coef = _lib.tensor_desc(coefficient_buffer)
     args.out = _lib.tensor_desc(_as_bhv(out))
     args.block_v = int(block_v)
-    _lib.check(_lib.load().gdnr_replay_split(ctypes.byref(args), _lib.stream_handle(q.device)))
+    _lib.call("gdnr_replay_split", args, q.device)
     return out
 
 
@@ -201,7 +201,7 @@ def gdn_replay_fp8_split_static(
     args.valid_len = _lib.tensor_desc(valid_len)
     args.out = _lib.tensor_desc(_as_bhv(out))
     args.block_v = int(block_v)
-    _lib.check(_lib.load().gdnr_replay_split_static(ctypes.byref(args), _lib.stream_handle(q.device)))
+    _lib.call("gdnr_replay_split_static", args, q.device)
     return out
 
 
@@ -229,7 +229,7 @@ def gdn_prep_ring(
                     ("beta_ring", beta_ring)):
         setattr(args, name, _lib.tensor_desc(t))
     args.error_flag = _err_ptr(error_flag)
-    _lib.check(_lib.load().gdnr_prep_ring(ctypes.byref(args), _lib.stream_handle(mixed_qkv.device)))
+    _lib.call("gdnr_prep_ring", args, mixed_qkv.device)
 
 
 def gdn_fused_step(
@@ -295,7 +295,7 @@ def gdn_fused_step(
     args.error_flag = _err_ptr(error_flag)
     args.flush_hint = _flush_hint(flush_hint)
     args.launch_flags = LAUNCH_PDL if pdl else 0
-    _lib.check(_lib.load().gdnr_fused_step(ctypes.byref(args), _lib.stream_handle(mixed_qkv.device)))
+    _lib.call("gdnr_fused_step", args, mixed_qkv.device)
     return out
 
 
@@ -335,6 +335,10 @@ def fused_recurrent_gated_delta_rule_packed_decode(
     no state is read or written for it and its ``out`` rows are set to zero,
     as the production op does; an index ``>= slots`` is treated the same way
     and reported in the device error word as ``GDNR_DEVERR_BAD_SLOT``.
+    The non-null indices of one call must be distinct, as in the production
+    contract (one batch row per sequence): two rows on the same slot would
+    both read-modify-write that slot's checkpoint, rings and position in the
+    same launch, and the result is undefined (nothing checks for it).
     ``out`` is ``[B, 1, HV, V]`` (or ``[B, HV, V]``).  q and k are always
     L2-normalised in the kernel and the output is scaled by ``K^-1/2``:
     ``use_qk_l2norm_in_kernel`` must be true and ``scale`` must be
@@ -366,7 +370,7 @@ def fused_recurrent_gated_delta_rule_packed_decode(
     args.error_flag = _err_ptr(error_flag)
     args.flush_hint = _flush_hint(flush_hint)
     args.launch_flags = LAUNCH_PDL if pdl else 0
-    _lib.check(_lib.load().gdnr_packed_decode(ctypes.byref(args), _lib.stream_handle(mixed_qkv.device)))
+    _lib.call("gdnr_packed_decode", args, mixed_qkv.device)
     st.pos.copy_(pos_next)
     return out
 
@@ -378,7 +382,7 @@ def gdn_bf16_step(state, q, k, v, g, beta) -> torch.Tensor:
     args = _lib.Bf16StepArgs()
     for name, t in (("state", state), ("q", q), ("k", k), ("v", v), ("g", g), ("beta", beta), ("out", out)):
         setattr(args, name, _lib.tensor_desc(t))
-    _lib.check(_lib.load().gdnr_bf16_step(ctypes.byref(args), _lib.stream_handle(q.device)))
+    _lib.call("gdnr_bf16_step", args, q.device)
     return out
 
 
@@ -434,7 +438,7 @@ def quantize_checkpoint(
     args.scale = _lib.tensor_desc(scale)
     args.quant_divisor = _divisor(quant_divisor)
     args.saturation_count = sat.data_ptr() if sat is not None else None
-    _lib.check(_lib.load().gdnr_quantize_vblock32(ctypes.byref(args), _lib.stream_handle(state.device)))
+    _lib.call("gdnr_quantize_vblock32", args, state.device)
     frac = float(sat.item()) / max(state.numel(), 1) if sat is not None else 0.0
     return QuantizedCheckpoint(payload, scale, granularity, 32, frac)
 
@@ -449,7 +453,7 @@ def dequantize_checkpoint(ckpt: QuantizedCheckpoint, out: torch.Tensor | None = 
     args.state = _lib.tensor_desc(out)
     args.payload = _lib.tensor_desc(ckpt.payload)
     args.scale = _lib.tensor_desc(ckpt.scale)
-    _lib.check(_lib.load().gdnr_dequantize_vblock32(ctypes.byref(args), _lib.stream_handle(out.device)))
+    _lib.call("gdnr_dequantize_vblock32", args, out.device)
     return out
 
 

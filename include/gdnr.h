@@ -182,7 +182,10 @@ int gdnr_fused_step(const gdnr_step_args* args, void* stream);
  * tensor.  An index <= 0 is the null slot (the serving engine's padding; the production
  * kernel's NULL_BLOCK_ID test, vLLM fused_recurrent.py:292-297): no state is read or written
  * for that row and its out rows are written as zeros, as the production op does.  An index
- * >= slots is treated the same way and reported as GDNR_DEVERR_BAD_SLOT.  q and k are
+ * >= slots is treated the same way and reported as GDNR_DEVERR_BAD_SLOT.  The non-null
+ * indices of one call must be distinct (one row per sequence, as in the production
+ * contract): two rows on one slot race on its state within the launch and the result is
+ * undefined; nothing checks for it.  q and k are
  * always L2-normalised in the kernel and the output is scaled by K^-1/2: the production
  * call's use_qk_l2norm_in_kernel and scale arguments must be 1 and K^-1/2.  The step is
  * gdnr_fused_step's (prep + ring append + replay, and the flush when a slot's pos is L-1);
@@ -241,6 +244,16 @@ int gdnr_abi_version(void);
 /* Library-owned device error word used when a call passes error_flag = NULL.
  * Reads it (synchronously, on the current device) and optionally clears it. */
 int gdnr_read_device_error(uint32_t* value, int clear);
+
+/* Diagnostic, no counterpart in the reference: one tiny launch that runs the
+ * persistent step kernel's bounded-wait code into its time limit (a barrier
+ * nothing arrives on, held with 32 tensor-memory columns allocated) and
+ * returns cleanly.  After it completes (about one second of GPU time), the
+ * error word has GDNR_DEVERR_WAIT_TIMEOUT set and report (device memory,
+ * 4 x u64) holds: both waits' results (0 = gave up), then the nanoseconds
+ * each waited; the second wait ends through the abort word the first one set.
+ * Used by the tests to show that a timed-out wait leaves the context usable. */
+int gdnr_selftest_wait_timeout(uint32_t* error_flag, unsigned long long* report, void* stream);
 
 #ifdef __cplusplus
 }

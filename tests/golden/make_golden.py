@@ -131,7 +131,8 @@ def make_recurrence(ref) -> dict:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True,
+                    help="root of a checkout of the reference project (its prototype/ directory is imported)")
     args = ap.parse_args()
     sys.path.insert(0, str(pathlib.Path(args.reference) / "prototype"))
     import gdn_replay_fp8_reference as ref  # noqa: E402  (the reference's own oracle)
