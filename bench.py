@@ -1,22 +1,39 @@
 #!/usr/bin/env python
 """Benchmark of the fused FP8-replay GDN decode step on B200.
 
-Workload (BASELINE config 3 at the metric's point, batch 64, L = 16): one
-*step* is one decode token through a stack of NL independent GDN layers,
-each a single ``gdn_fused_step`` launch (prep + ring append + replay, and the
-flush/re-quantisation on the L-th token of the ring cycle) at batch 64,
-H = 16, HV = 32, K = V = 128.  Steps walk the ring cycle, so the flush cost
-is amortised exactly as in the reference's cycle model
-(prototype/bench_gdn_full_contract.py:225-308).  NL layers x ~46 MB of state
-(> 2x the 126 MB L2) keep every launch reading its state from HBM.
+Headline workload (BASELINE config 3 at the metric's point, batch 64 per GPU,
+L = 16): one *step* is one decode token through a stack of NL independent GDN
+layers, each a single ``gdn_fused_step`` launch (prep + ring append + replay,
+and the flush / re-quantisation on the L-th token of the ring cycle) at
+batch 64, H = 16, HV = 32, K = V = 128.  The W warm-up steps end on a ring
+boundary, so the K timed steps walk the ring from position 0; ``value`` is
+cycle-exact: the per-position mean step times weighted so that the flush is
+exactly 1/L of the steps, whatever K is (K >= L), as in the reference's cycle
+model (prototype/bench_gdn_full_contract.py:225-308).  NL layers x ~46 MB of
+state (> 2x the 126 MB L2) keep every launch reading its state from HBM.
 
-The metric is decode steps.seq/s per GDN layer: (steps x NL x batch) / time.
+The metric is decode steps.seq/s per GDN layer: (NL x batch) / (cycle-mean
+time of one step).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Multi-GPU: one process per GPU (torchrun), each rank runs its own batch of
-64 sequences (weak scaling over independent sequence shards); no collective
-on the data path -- only the barrier and the max-over-ranks of the timing.
+Other keys of the JSON line (each measured the same way, one CUDA graph per
+ring position, CUDA events between replays):
+  sweep          BASELINE config 3: B in {1,4,16,64,256} x L in {4,8,16}
+  heterogeneous  B=64, L=16 with ring positions spread over 0..L-1 (1/L of the
+                 sequences flush on every step), default "auto" hint
+  config5        BASELINE config 5: 24 layers x 1024 sequences split over the
+                 ranks (strong scaling), 256 steps, per-rank times
+  comparators    the production op (vLLM FLA packed decode), the sm_100a bf16
+                 step, and the reference's own Triton kernels when a copy of
+                 the reference's prototype/ directory sits in baseline/_ref/
+  e2e            the public Python API with pinned host buffers, host<->device
+                 copies inside the timed region
+
+Multi-GPU: one process per GPU (torchrun); the headline runs batch 64 per
+rank (weak scaling over independent sequence shards), config5 splits a fixed
+job; no collective on the data path -- only barriers and the max over ranks
+of the timings.
 """
 
 from __future__ import annotations
@@ -38,7 +55,10 @@ sys.path.insert(0, str(ROOT))
 METRIC = "GDN decode steps·seq/s @batch64 L=16; achieved HBM GB/s vs B200 peak"
 UNIT = "steps·seq/s"
 H, HV, KD = 16, 32, 128
+W_MIXED = 2 * H * KD + HV * KD
 FALLBACK_HBM_GBS = 6650.0
+L2_BYTES = 126e6
+REF_DIR = ROOT / "baseline" / "_ref" / "prototype"  # optional copy of the reference's prototype/ (not committed)
 
 
 def parse_args():
@@ -53,10 +73,18 @@ def parse_args():
     ap.add_argument("--e2e-steps", type=int, default=64)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-core", action="store_true", help="skip the core-replay (config 2) measurement")
+    ap.add_argument("--no-core", action="store_true",
+                    help="skip the single-GPU extras (core replay, widened rows, comparators, sweep, heterogeneous)")
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-config5", action="store_true")
+    ap.add_argument("--config5-steps", type=int, default=256)
     ap.add_argument("--profile", type=int, default=None, metavar="POS",
                     help="profiling driver for ncu: a few untimed launches of one layer's step at ring position "
                          "POS (no timing, no JSON line)")
+    ap.add_argument("--profile-batch", type=int, default=None,
+                    help="batch of the --profile driver (default --batch)")
+    ap.add_argument("--profile-hetero", action="store_true",
+                    help="--profile with ring positions spread over 0..L-1 and the 'auto' hint")
     ap.add_argument("--checkpoint", choices=["e4m3", "int8"], default="e4m3",
                     help="checkpoint payload of the --profile driver (int8: the 'vblock_int8' option)")
     return ap.parse_args()
@@ -73,16 +101,22 @@ def measured_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def profile_traffic():
-    """dram bytes per launch of the step kernel from the committed ncu summary."""
+def profile_traffic_ratio():
+    """(dram bytes / algorithmic bytes, capture note) of the committed ncu summary
+    of the non-flush step kernel."""
     p = ROOT / "profiles" / "step5_kernel_b64_l16.md"
+    dram = alg = None
     try:
         for line in p.read_text().splitlines():
-            if line.startswith("dram_bytes_per_launch_cycle_avg"):
-                return int(float(line.split("=")[1].strip()))
+            if line.startswith("dram_bytes_per_launch_fill8"):
+                dram = float(line.split("=")[1].strip())
+            if line.startswith("algorithmic_bytes_per_launch_fill8"):
+                alg = float(line.split("=")[1].strip())
     except Exception:
         pass
-    return None
+    if dram and alg:
+        return dram / alg, "ncu capture at ring fill 8 (profiles/step5_kernel_b64_l16.md), scaled by algorithmic bytes"
+    return None, "no ncu capture"
 
 
 class ClockSampler:
@@ -183,6 +217,18 @@ def max_over_ranks(x: float, world: int) -> float:
     return reduce_max(x)
 
 
+def gather_over_ranks(x: float, world: int) -> list:
+    if world == 1:
+        return [x]
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([float(x)], dtype=torch.float64, device=torch.device("cuda", torch.cuda.current_device()))
+    out = [torch.zeros_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [float(o.item()) for o in out]
+
+
 def barrier(world: int):
     import torch
 
@@ -194,7 +240,7 @@ def barrier(world: int):
     torch.cuda.synchronize()
 
 
-# ---------------------------------------------------------------- CPU baseline (oracle port)
+# ---------------------------------------------------------------- CPU baseline and the reference arm
 
 def cpu_units(units_per_worker: int, workers: int, seed: int, ring_len: int):
     """Run the oracle port on `workers` spawned processes; returns (units, seconds)."""
@@ -230,22 +276,84 @@ def cpu_baseline(seed: int, ring_len: int, target_s: float = 15.0):
                       f"cycles incl. the flush) of the numpy oracle port of replay_decode, {wall:.1f} s wall"}
 
 
+def reference_torch_cpu(args):
+    """The reference's own CPU path, when a copy of its prototype/ sits in
+    baseline/_ref/: ``replay_decode`` of gdn_replay_fp8_reference.py
+    (ref.py:189-244: dequantise, replay the ring from the checkpoint with the
+    per-token recurrence, keep the last output, re-quantise when the ring is
+    full) at batch 64, H=16, HV=32, on all host threads.  One step = one decode
+    token of the batch; steps walk whole L-cycles.  Returns None without the copy."""
+    if not (REF_DIR / "gdn_replay_fp8_reference.py").exists():
+        return None
+    import torch
+
+    sys.path.insert(0, str(REF_DIR))
+    import gdn_replay_fp8_reference as ref  # noqa: E402  (the reference's own module)
+
+    threads = cpu_workers()
+    torch.set_num_threads(threads)
+    B, L = args.batch, args.ring
+    gen = torch.Generator().manual_seed(args.seed)
+    state = 0.02 * torch.randn(B, HV, KD, KD, generator=gen)
+
+    def inputs(T):
+        q = torch.nn.functional.normalize(torch.randn(B, T, H, KD, generator=gen), dim=-1)
+        k = torch.nn.functional.normalize(torch.randn(B, T, H, KD, generator=gen), dim=-1)
+        v = torch.randn(B, T, HV, KD, generator=gen)
+        g = -torch.rand(B, T, HV, generator=gen) * 0.1
+        beta = torch.sigmoid(torch.randn(B, T, HV, generator=gen))
+        return q, k, v, g, beta
+
+    # replay_decode(T tokens) runs all T steps of the chain; one cycle = L steps
+    q, k, v, g, beta = inputs(1)
+    t0 = time.perf_counter()
+    ref.replay_decode(state, q, k, v, g, beta, L, "vblock", 32)
+    one = time.perf_counter() - t0  # one step at fill 1: sizes the sample
+    cycles = 1
+    t0 = time.perf_counter()
+    q, k, v, g, beta = inputs(L * cycles)
+    ref.replay_decode(state, q, k, v, g, beta, L, "vblock", 32)
+    wall = time.perf_counter() - t0
+    steps = L * cycles
+    value = steps * B / wall
+    return {"value": value, "unit": UNIT, "cores": threads, "kind": "reference", "steps": steps,
+            "sample": f"the reference's replay_decode (gdn_replay_fp8_reference.py, torch on CPU, {threads} threads) "
+                      f"over {steps} decode steps (whole L={L} cycles incl. the flush) of batch {B}, H={H}, HV={HV}; "
+                      f"{wall:.1f} s wall (first step probe {one:.2f} s)"}
+
+
 def run_reference(args, world, rank):
-    """--impl reference: the reference's CPU implementation of the path (oracle port)."""
+    """--impl reference: the reference's CPU implementation of the path on the
+    host cores (its own replay_decode when baseline/_ref holds a copy of its
+    prototype/, else the numpy oracle port of it)."""
     if rank != 0:
         return
-    workers = cpu_workers()
-    # size each step's sample so the whole run stays within a few minutes:
-    # one unit per worker per step; cap total steps timed by the budget
-    budget_s = 150.0
-    probe_units, probe_wall = cpu_units(1, workers, args.seed, args.ring)
-    per_step = probe_wall if probe_wall > 0 else 0.05
-    steps = args.steps
-    units_per_step = workers
-    while steps * per_step > budget_s and steps > 1:
-        steps //= 2
-    t_units, t_wall = cpu_units(max(1, steps), workers, args.seed, args.ring)
-    value = t_units / t_wall
+    ref = None
+    try:
+        ref = reference_torch_cpu(args)
+    except Exception as e:  # a broken copy falls back to the port, with the reason
+        ref_err = f"{type(e).__name__}: {e}"[:200]
+    else:
+        ref_err = None
+    if ref is not None:
+        value, steps, ms = ref["value"], ref["steps"], 1e3 * args.batch / ref["value"]
+        cpu = {k: ref[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        cfg_batch, note = args.batch, "the reference's own torch replay_decode, imported from baseline/_ref"
+    else:
+        workers = cpu_workers()
+        budget_s = 150.0
+        _, probe_wall = cpu_units(1, workers, args.seed, args.ring)
+        per_step = probe_wall if probe_wall > 0 else 0.05
+        steps = args.steps
+        while steps * per_step > budget_s and steps > 1:
+            steps //= 2
+        t_units, t_wall = cpu_units(max(1, steps), workers, args.seed, args.ring)
+        value, ms, cfg_batch = t_units / t_wall, 1e3 * t_wall / max(1, steps), workers
+        cpu = {"value": value, "unit": UNIT, "cores": workers, "kind": "port",
+               "sample": f"{t_units} sequence-layer steps ({workers} sequences per step, {steps} steps) of the numpy "
+                         "oracle port of replay_decode"}
+        note = ("no copy of the reference's prototype/ in baseline/_ref" + (f" ({ref_err})" if ref_err else "") +
+                "; its CPU path (ref.py replay_decode) is timed through the repo's numpy restatement")
     line = {
         "impl": "reference",
         "metric": METRIC,
@@ -254,54 +362,78 @@ def run_reference(args, world, rank):
         "n_gpus": args.gpus,
         "steps": steps,
         "warmup": 1,
-        "ms_per_step": 1e3 * t_wall / max(1, steps),
+        "ms_per_step": ms,
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic (seeded, BASELINE config 1/3 distributions)",
-        "config": {"workload": f"config3 full-contract step, one GDN layer, L={args.ring}, CPU sample",
-                   "global_batch": units_per_step, "seq_len": args.ring, "parallelism": f"{workers} processes"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": workers, "kind": "port",
-                         "sample": f"{t_units} sequence-layer steps ({units_per_step} sequences per step, "
-                                   f"{steps} steps) of the numpy oracle port of replay_decode"},
+        "config": {"workload": f"one GDN layer's decode step (replay chain + flush every {args.ring}), L={args.ring}, "
+                               "CPU sample", "global_batch": cfg_batch, "seq_len": args.ring,
+                   "parallelism": f"{cpu['cores']} host threads"},
+        "cpu_baseline": cpu,
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "note": "the reference is a Python/Triton prototype that cannot be installed (no setup.py/pyproject); "
-                "its CPU path (ref.py replay_decode) is timed through the repo's numpy restatement",
+        "note": note,
     }
     print(json.dumps(line), flush=True)
 
 
-# ---------------------------------------------------------------- GPU arm
+# ---------------------------------------------------------------- workload construction
 
-def build_stack(args, device, rank: int = 0, world: int = 1, checkpoint_dtype=None):
-    """This rank's shard of the job: sequences ShardPlan(B * world, world).local(rank)
-    of every layer, each rank with its own seeded inputs and state (weak scaling)."""
-    import torch
+class LayerStack:
+    """NL independent GDN layers of B sequences each: one pooled decode state
+    (the layers are consecutive batch ranges of it) and resident raw inputs per
+    (layer, ring position), seeded per layer with the config-1 distributions
+    (q, k, v, a, b ~ N(0,1) bf16; A_log = log U(1,16); dt_bias ~ N(0,0.5);
+    state ~ N(0, 0.02) quantised to the checkpoint)."""
 
-    import gdnr
-    from gdnr import inputs as gin
-    from gdnr.shard import ShardPlan
+    def __init__(self, B, L, NL, seed_of, device, checkpoint_dtype=None, out_dtype=None):
+        import torch
 
-    B, L, NL = args.batch, args.ring, args.layers
-    shard = ShardPlan(B * world, world).local(rank)
-    assert len(shard) == B
-    layers, step_inputs = [], []
-    for li in range(NL):
-        st = gdnr.ReplayState.allocate(B, H, HV, L, device=device, scale_dtype=torch.float32,
-                                       gate_dtype=torch.float32,
-                                       checkpoint_dtype=checkpoint_dtype or torch.float8_e4m3fn)
-        raw = gin.raw_step_inputs(B, L, seed=(args.seed * 1000 + li) * 4096 + shard.start, device=device)
-        st.load_state(raw["state"])
-        layers.append({"state": st, "a_log": raw["a_log"], "dt_bias": raw["dt_bias"],
-                       "out": torch.empty(B, HV, KD, dtype=torch.bfloat16, device=device)})
-        # distinct raw inputs per (layer, ring position), resident in HBM
-        step_inputs.append([(raw["mixed_qkv"][:, s].contiguous(), raw["a"][:, s].contiguous(),
-                             raw["b"][:, s].contiguous()) for s in range(L)])
-        del raw
-    pos = [torch.full((B,), s, dtype=torch.int32, device=device) for s in range(L)]
-    err = torch.zeros(1, dtype=torch.int32, device=device)
-    return layers, step_inputs, pos, err
+        import gdnr
+
+        bf = torch.bfloat16
+        self.B, self.L, self.NL = B, L, NL
+        self.pool = gdnr.ReplayState.allocate(NL * B, H, HV, L, device=device, scale_dtype=torch.float32,
+                                              gate_dtype=torch.float32,
+                                              checkpoint_dtype=checkpoint_dtype or torch.float8_e4m3fn)
+        self.mixed = torch.empty(NL, L, B, W_MIXED, dtype=bf, device=device)
+        self.a = torch.empty(NL, L, B, HV, dtype=bf, device=device)
+        self.b = torch.empty(NL, L, B, HV, dtype=bf, device=device)
+        self.a_log = torch.empty(NL, HV, dtype=torch.float32, device=device)
+        self.dt_bias = torch.empty(NL, HV, dtype=torch.float32, device=device)
+        self.out = torch.empty(NL, B, HV, KD, dtype=out_dtype or bf, device=device)
+        self.views = []
+        for li in range(NL):
+            g = torch.Generator(device=device)
+            g.manual_seed(int(seed_of(li)))
+            self.mixed[li] = torch.randn(L, B, W_MIXED, generator=g, device=device)
+            self.a[li] = torch.randn(L, B, HV, generator=g, device=device)
+            self.b[li] = torch.randn(L, B, HV, generator=g, device=device)
+            self.a_log[li] = torch.log(1.0 + 15.0 * torch.rand(HV, generator=g, device=device))
+            self.dt_bias[li] = 0.5 * torch.randn(HV, generator=g, device=device)
+            sl = slice(li * B, (li + 1) * B)
+            p = self.pool
+            view = gdnr.ReplayState(p.checkpoint[sl], None if p.scale is None else p.scale[sl], p.k_ring[sl],
+                                    p.v_ring[sl], p.g_ring[sl], p.beta_ring[sl], p.pos[sl])
+            view.load_state(0.02 * torch.randn(B, HV, KD, KD, generator=g, device=device))
+            self.views.append(view)
+        # the shapes bench's e2e path consumes
+        self.layers = [{"state": self.views[li], "a_log": self.a_log[li], "dt_bias": self.dt_bias[li],
+                        "out": self.out[li]} for li in range(NL)]
+        self.step_inputs = [[(self.mixed[li, s], self.a[li, s], self.b[li, s]) for s in range(L)] for li in range(NL)]
+
+    def state_nbytes(self):
+        return self.pool.nbytes()
+
+    def launch(self, s, pos, hint, err=None):
+        """Every layer's fused step with this step's inputs of ring position s."""
+        import gdnr
+
+        for li, st in enumerate(self.views):
+            gdnr.gdn_fused_step(self.mixed[li, s], self.a[li, s], self.b[li, s], self.a_log[li], self.dt_bias[li], pos,
+                                st.checkpoint, st.scale, st.k_ring, st.v_ring, st.g_ring, st.beta_ring,
+                                out=self.out[li], error_flag=err, flush_hint=hint)
 
 
 def flush_hint_for(s: int, L: int) -> str:
@@ -310,38 +442,104 @@ def flush_hint_for(s: int, L: int) -> str:
     return "all" if s == L - 1 else "none"
 
 
-def launch_position(layers, step_inputs, pos, err, s):
-    import gdnr
+def uniform_positions(B, L, device):
+    import torch
 
-    L = len(pos)
-    for li, lay in enumerate(layers):
-        st = lay["state"]
-        mixed, a, b = step_inputs[li][s]
-        gdnr.gdn_fused_step(mixed, a, b, lay["a_log"], lay["dt_bias"], pos[s], st.checkpoint, st.scale, st.k_ring,
-                            st.v_ring, st.g_ring, st.beta_ring, out=lay["out"], error_flag=err,
-                            flush_hint=flush_hint_for(s, L))
+    return [torch.full((B,), s, dtype=torch.int32, device=device) for s in range(L)]
+
+
+def spread_positions(B, L, device):
+    """Step offset s: sequence b at ring position (b + s) % L (1/L of them flush)."""
+    import torch
+
+    base = torch.arange(B, dtype=torch.int32, device=device)
+    return [((base + s) % L).to(torch.int32) for s in range(L)]
+
+
+def capture_positions(fn, L, stream):
+    """One CUDA graph per ring position s of fn(s) (after one eager pass)."""
+    import torch
+
+    with torch.cuda.stream(stream):
+        for s in range(L):
+            fn(s)
+    torch.cuda.synchronize()
+    graphs = []
+    for s in range(L):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            fn(s)
+        graphs.append(g)
+    torch.cuda.synchronize()
+    return graphs
+
+
+def time_cycles(graphs, stream, cycles, warm=1):
+    """Mean device ms of each position's graph over `cycles` whole ring cycles
+    (events between consecutive replays on the launch stream)."""
+    import torch
+
+    L = len(graphs)
+    with torch.cuda.stream(stream):
+        for _ in range(warm):
+            for g in graphs:
+                g.replay()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(cycles * L + 1)]
+    with torch.cuda.stream(stream):
+        ev[0].record(stream)
+        for c in range(cycles):
+            for s, g in enumerate(graphs):
+                g.replay()
+                ev[c * L + s + 1].record(stream)
+    torch.cuda.synchronize()
+    per = [0.0] * L
+    for c in range(cycles):
+        for s in range(L):
+            per[s] += ev[c * L + s].elapsed_time(ev[c * L + s + 1]) / cycles
+    return per
+
+
+# ---------------------------------------------------------------- GPU arm
+
+def build_stack(args, device, rank: int = 0, world: int = 1, checkpoint_dtype=None, batch=None, layers=None):
+    """This rank's shard of the headline job: sequences ShardPlan(B * world,
+    world).local(rank) of every layer, each rank with its own seeded inputs and
+    state (weak scaling)."""
+    from gdnr.shard import ShardPlan
+
+    B = batch or args.batch
+    NL = layers or args.layers
+    shard = ShardPlan(B * world, world).local(rank)
+    assert len(shard) == B
+    return LayerStack(B, args.ring, NL, lambda li: (args.seed * 1000 + li) * 4096 + shard.start, device,
+                      checkpoint_dtype=checkpoint_dtype)
 
 
 def run_profile(args, local):
     """A few eager launches of one layer's fused step at one ring position (ncu target)."""
     import torch
 
-    args.layers = 1
     device = torch.device("cuda", local)
-    layers, step_inputs, pos, err = build_stack(
-        args, device, checkpoint_dtype=torch.int8 if args.checkpoint == "int8" else None)
-    s = args.profile % args.ring
+    B, L = args.profile_batch or args.batch, args.ring
+    stack = build_stack(args, device, batch=B, layers=1,
+                        checkpoint_dtype=torch.int8 if args.checkpoint == "int8" else None)
+    err = torch.zeros(1, dtype=torch.int32, device=device)
+    s = args.profile % L
+    if args.profile_hetero:
+        pos, hint = spread_positions(B, L, device)[s], "auto"
+    else:
+        pos, hint = uniform_positions(B, L, device)[s], flush_hint_for(s, L)
     for _ in range(3):
-        launch_position(layers, step_inputs, pos, err, s)
+        stack.launch(s, pos, hint, err)
     torch.cuda.synchronize()
-    print(f"profile: 3 launches at ring position {s}, device error word {int(err.item())}", flush=True)
+    print(f"profile: 3 launches at ring position {s} (batch {B}, hint {hint}), device error word {int(err.item())}",
+          flush=True)
 
 
 def run_ours(args, world, rank, local):
     import torch
 
-    import gdnr
-    from oracle import gdn_oracle as O
+    from gdnr import traffic
 
     device = torch.device("cuda", local)
     B, L, NL = args.batch, args.ring, args.layers
@@ -349,31 +547,20 @@ def run_ours(args, world, rank, local):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu_line = cpu_baseline(args.seed, L)  # spawn pool; GPU untouched so far
 
-    layers, step_inputs, pos, err = build_stack(args, device, rank, world)
+    stack = build_stack(args, device, rank, world)
+    err = torch.zeros(1, dtype=torch.int32, device=device)
+    pos = uniform_positions(B, L, device)
     stream = torch.cuda.Stream(device)
-    torch.cuda.synchronize()
-    # one graph per ring position: NL fused launches
-    graphs = []
-    with torch.cuda.stream(stream):
-        for s in range(L):  # eager pass: lazy loading + smem attribute before capture
-            launch_position(layers, step_inputs, pos, err, s)
-    torch.cuda.synchronize()
-    for s in range(L):
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=stream):
-            launch_position(layers, step_inputs, pos, err, s)
-        graphs.append(g)
-    torch.cuda.synchronize()
+    graphs = capture_positions(lambda s: stack.launch(s, pos[s], flush_hint_for(s, L), err), L, stream)
 
-    step_idx = 0
+    # warm-up steps end on a ring boundary: the timed steps start at position 0
+    step_idx = (-args.warmup) % L
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
             graphs[step_idx % L].replay()
             step_idx += 1
     barrier(world)
-    # one event between consecutive graph replays: per-position durations give
-    # each kernel's average launch time (non-flush positions -> the persistent
-    # step kernel; the flush position -> the flush kernel)
+    # one event between consecutive graph replays: per-position step times
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     positions = []
     sampler = ClockSampler(local)
@@ -387,43 +574,58 @@ def run_ours(args, world, rank, local):
                 evs[i + 1].record(stream)
         torch.cuda.synchronize()
     barrier(world)
-    ms = evs[0].elapsed_time(evs[-1])
-    ms_max = max_over_ranks(ms, world)
-    dev_err = int(err.item())
+    ms_window = evs[0].elapsed_time(evs[-1])
     step_ms = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
+    by_pos = {}
+    for p, t in zip(positions, step_ms):
+        by_pos.setdefault(p, []).append(t)
+    cycle_exact = len(by_pos) == L
+    if cycle_exact:  # each ring position weighted 1/L: the flush is exactly 1/L of the steps
+        ms_cycle_step = sum(statistics.fmean(by_pos[p]) for p in range(L)) / L
+    else:  # fewer timed steps than ring positions: the window as measured
+        ms_cycle_step = ms_window / args.steps
+    ms_step = max_over_ranks(ms_cycle_step, world)
+    ms_window_max = max_over_ranks(ms_window, world)
+    dev_err = int(err.item())
 
     launches = args.steps * NL
-    units = launches * B * world
-    value = units / (ms_max / 1e3)
-    # algorithmic bytes, averaged over the ring cycle actually timed
-    cyc = [O.algorithmic_bytes(B, p + 1, L, scale_bytes=4, gate_bytes=4, ab_bytes=2) for p in positions]
-    bytes_per_launch = sum(cyc) / len(cyc)
+    value = NL * B * world / (ms_step / 1e3)
     peak, peak_kind = measured_peak()
+    fill_bytes = {p: traffic.step_bytes(B, p + 1, L) for p in range(L)}
     kernels = {}
     for name, sel in (("step5_kernel<flush=false> (non-flush steps)", lambda p: p != L - 1),
                       ("step5_kernel<flush=true> (flush step)", lambda p: p == L - 1)):
-        idx = [i for i, p in enumerate(positions) if sel(p)]
-        if not idx:
+        ps = [p for p in by_pos if sel(p)]
+        if not ps:
             continue
-        t = sum(step_ms[i] for i in idx) / (len(idx) * NL) / 1e3
-        b = sum(cyc[i] for i in idx) / len(idx)
-        kernels[name] = {"launches": len(idx) * NL, "us_per_launch": t * 1e6, "algorithmic_bytes_per_launch": b,
-                         "achieved_GB_s": b / t / 1e9, "frac_of_peak": b / t / 1e9 / peak}
+        t = statistics.fmean(statistics.fmean(by_pos[p]) for p in ps) / NL / 1e3
+        b = statistics.fmean(fill_bytes[p] for p in ps)
+        kernels[name] = {"launches": sum(len(by_pos[p]) for p in ps) * NL, "us_per_launch": t * 1e6,
+                         "algorithmic_bytes_per_launch": b, "achieved_GB_s": b / t / 1e9,
+                         "frac_of_peak": b / t / 1e9 / peak}
     dom = max(kernels, key=lambda k: kernels[k]["launches"] * kernels[k]["us_per_launch"])
     achieved = kernels[dom]["achieved_GB_s"]
+    cyc_bytes = traffic.cycle_bytes(B, L)
+    ratio, traffic_note = profile_traffic_ratio()
 
     # ---- end to end through the public API with host buffers (pinned), per layer-step
-    e2e = run_e2e(args, layers, step_inputs, pos, stream, world) if args.e2e_steps > 0 else None
-
-    core = None
-    widened = None
-    if not args.no_core and world == 1:
-        core = run_core(args, device, stream)
-        widened = run_widened(args, device, stream)
-        widened["comparators"] = run_comparators(args, device, stream, 1e3 * ms_max / launches)
-
+    e2e = run_e2e(args, stack.layers, stack.step_inputs, pos, stream, world) if args.e2e_steps > 0 else None
     del graphs
     torch.cuda.synchronize()
+
+    extras = {}
+    if not args.no_core and world == 1:
+        extras["core_replay"] = run_core(args, device, stream)
+        extras["heterogeneous"] = run_heterogeneous(args, stack, device, stream, 1e3 * ms_step / NL)
+        extras.update(run_widened(args, device, stream))
+        extras["comparators"] = run_comparators(args, device, stream, 1e3 * ms_step / NL)
+        if not args.no_sweep:
+            extras["sweep"] = run_sweep(args, device, stream)
+    del stack
+    torch.cuda.empty_cache()
+    if not args.no_config5:
+        extras["config5"] = run_config5(args, world, rank, device, stream)
+
     if rank != 0:
         return
     line = {
@@ -433,8 +635,10 @@ def run_ours(args, world, rank, local):
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": ms_max / args.steps,
-        "us_per_layer_step": 1e3 * ms_max / launches,
+        "ms_per_step": ms_window_max / args.steps,
+        "us_per_layer_step": 1e3 * ms_step / NL,
+        "cycle_exact": cycle_exact,
+        "value_timed_window": NL * B * world * args.steps / (ms_window_max / 1e3),
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
@@ -442,11 +646,11 @@ def run_ours(args, world, rank, local):
         "data": "synthetic (seeded; BASELINE config 1/3 distributions; random state N(0,0.02))",
         "config": {
             "workload": f"config3 fused full-contract step (prep+ring append+replay, flush every {L}), "
-                        f"batch {B}/GPU, L={L}, cycle-amortised; one step = one token through {NL} independent "
-                        "GDN layers (one launch each)",
+                        f"batch {B}/GPU, L={L}, cycle-exact (each ring position weighted 1/L); one step = one token "
+                        f"through {NL} independent GDN layers (one launch each)",
             "global_batch": B * world, "seq_len": L, "parallelism": f"sequence-shard x{world} (no collective)",
             "heads": H, "value_heads": HV, "head_dim": KD, "layers": NL,
-            "l2": f"inputs larger than L2: {NL} layer states x {layers[0]['state'].nbytes() / 1e6:.1f} MB",
+            "l2": f"inputs larger than L2: {NL} layer states, {stack_bytes(B, L, NL) / 1e6:.0f} MB",
         },
         "gpu_launches": launches,
         "device_error_word": dev_err,
@@ -459,23 +663,166 @@ def run_ours(args, world, rank, local):
             "peak_kind": peak_kind,
             "unit": "GB/s",
             "frac": achieved / peak,
-            "traffic": profile_traffic(),
+            "traffic": None if ratio is None else ratio * kernels[dom]["algorithmic_bytes_per_launch"],
+            "traffic_source": traffic_note,
             "algorithmic_bytes_per_launch": kernels[dom]["algorithmic_bytes_per_launch"],
-            "note": "achieved = the kernel's algorithmic bytes per launch (averaged over the positions it ran) / "
-                    "its average launch time from CUDA events between graph replays on the launch stream",
+            "cycle": {"algorithmic_bytes_per_launch": cyc_bytes, "us_per_launch": 1e3 * ms_step / NL,
+                      "achieved": cyc_bytes / (ms_step / NL / 1e3) / 1e9,
+                      "frac": cyc_bytes / (ms_step / NL / 1e3) / 1e9 / peak},
+            "note": "achieved = the kernel's algorithmic bytes per launch (averaged over the ring positions it ran) / "
+                    "its average launch time from CUDA events between graph replays on the launch stream; cycle = "
+                    "the same over a whole ring cycle (flush included)",
         },
         "kernels": kernels,
-        "cycle_algorithmic_bytes_per_launch": bytes_per_launch,
+        "per_position_us_per_launch": [1e3 * statistics.fmean(by_pos[p]) / NL for p in sorted(by_pos)],
     }
     if e2e is not None:
         line["e2e"] = e2e
-    if core is not None:
-        line["core_replay"] = core
-    if widened is not None:
-        line.update(widened)
+    line.update(extras)
     if cpu_line is not None:
         line["cpu_baseline"] = cpu_line
     print(json.dumps(line), flush=True)
+
+
+def stack_bytes(B, L, NL):
+    from gdnr import traffic
+
+    return NL * traffic.state_bytes(B, L)
+
+
+def run_heterogeneous(args, stack, device, stream, uniform_us):
+    """The headline stack with ring positions spread evenly over 0..L-1 (step
+    offset s: sequence b at position (b + s) % L, so 1/L of the sequences flush
+    on every step), default "auto" hint; µs per layer-step over a cycle of offsets."""
+    import torch
+
+    B, L, NL = stack.B, stack.L, stack.NL
+    pos = spread_positions(B, L, device)
+    err = torch.zeros(1, dtype=torch.int32, device=device)
+    graphs = capture_positions(lambda s: stack.launch(s, pos[s], "auto", err), L, stream)
+    per = time_cycles(graphs, stream, cycles=4)
+    del graphs
+    us = 1e3 * statistics.fmean(per) / NL
+    return {"us_per_layer_step": us, "steps_seq_per_s": B / (us * 1e-6), "uniform_cycle_us_per_layer_step": uniform_us,
+            "ratio_to_uniform": us / uniform_us, "device_error_word": int(err.item()),
+            "workload": f"batch {B}, L={L}, {NL} layers, sequence b at ring position (b + s) % L on step s (1/L flush "
+                        "on every step), flush_hint 'auto', 4 cycles"}
+
+
+def run_sweep(args, device, stream):
+    """B in {1,4,16,64,256} x L in {4,8,16}, each cell a whole
+    ring cycle (fills 1..L, the flush on the last) with uniform positions, over
+    enough layer states to exceed 2x L2; plus the production op (vLLM FLA packed
+    decode) per batch, as the reference's speed-up table does
+    (bench_gdn_full_contract.py:225-308)."""
+    import torch
+
+    from gdnr import traffic
+
+    peak, _ = measured_peak()
+    cells = []
+    fla = {}
+    for B in (1, 4, 16, 64, 256):
+        for L in (4, 8, 16):
+            NL = max(1, min(512, math.ceil(2.2 * L2_BYTES / traffic.state_bytes(B, L))))
+            stack = LayerStack(B, L, NL, lambda li: (args.seed * 7919 + B * 131 + L) * 4096 + li, device)
+            pos = uniform_positions(B, L, device)
+            err = torch.zeros(1, dtype=torch.int32, device=device)
+            graphs = capture_positions(lambda s: stack.launch(s, pos[s], flush_hint_for(s, L), err), L, stream)
+            per = time_cycles(graphs, stream, cycles=4)
+            del graphs
+            us = 1e3 * statistics.fmean(per) / NL
+            cb = traffic.cycle_bytes(B, L)
+            cells.append({"batch": B, "ring": L, "layers": NL, "us_per_layer_step": us,
+                          "steps_seq_per_s": B / (us * 1e-6), "GB_s": cb / (us * 1e-6) / 1e9,
+                          "frac_of_peak": cb / (us * 1e-6) / 1e9 / peak,
+                          "us_nonflush": 1e3 * statistics.fmean(per[:-1]) / NL, "us_flush": 1e3 * per[-1] / NL,
+                          "device_error_word": int(err.item())})
+            del stack
+        fla[B] = fla_packed_decode_us(B, args.seed, device, stream)
+        for c in cells:
+            if c["batch"] == B and isinstance(fla[B], float):
+                c["production_us"] = fla[B]
+                c["speedup_vs_production"] = fla[B] / c["us_per_layer_step"]
+    return {"cells": cells, "workload": "gdn_fused_step cycle-averaged per layer-step (one CUDA graph per ring "
+                                        "position over >2x L2 of layer states); production_us: vLLM FLA packed decode "
+                                        "on a bf16 state pool, same batch"}
+
+
+def fla_packed_decode_us(B, seed, device, stream):
+    """µs per layer-step of the production operator (vLLM's FLA packed decode,
+    bf16 state pool of B + 1 slots, random slot order) over > 2x L2 of state."""
+    import torch
+
+    try:
+        from vllm.model_executor.layers.fla.ops.fused_recurrent import \
+            fused_recurrent_gated_delta_rule_packed_decode as fla_decode
+    except Exception as e:  # optional: the image may lack vLLM or Triton
+        return f"unavailable: {type(e).__name__}: {e}"[:200]
+    per_layer = (B + 1) * HV * KD * KD * 2
+    NL = max(1, min(512, math.ceil(2.2 * L2_BYTES / per_layer)))
+    gen = torch.Generator().manual_seed(seed + 23 + B)
+    pools = torch.zeros(NL, B + 1, HV, KD, KD, dtype=torch.bfloat16, device=device)
+    pools[:, 1:].normal_(0.0, 0.02)
+    mixed = torch.randn(NL, B, W_MIXED, device=device).to(torch.bfloat16)
+    a = torch.randn(NL, B, HV, device=device).to(torch.bfloat16)
+    b = torch.randn(NL, B, HV, device=device).to(torch.bfloat16)
+    a_log = torch.log(1.0 + 15.0 * torch.rand(HV, device=device))
+    dt_bias = 0.5 * torch.randn(HV, device=device)
+    out = torch.empty(NL, B, 1, HV, KD, dtype=torch.bfloat16, device=device)
+    idx = (torch.randperm(B, generator=gen) + 1).to(torch.int32).to(device)
+
+    def step(s=0):
+        for li in range(NL):
+            fla_decode(mixed[li], a[li], b[li], a_log, dt_bias, KD ** -0.5, pools[li], out[li], idx,
+                       use_qk_l2norm_in_kernel=True)
+    graphs = capture_positions(step, 1, stream)
+    per = time_cycles(graphs, stream, cycles=8)
+    del graphs, pools
+    return 1e3 * per[0] / NL
+
+
+def run_config5(args, world, rank, device, stream):
+    """a fixed job of 24 GDN layers x 1024 sequences, L=16,
+    split evenly over the ranks (strong scaling), config5_steps decode steps
+    (whole ring cycles, a flush every 16) after one warm-up cycle; each rank
+    times its own shard with CUDA events; value = all sequence-layer steps /
+    the slowest rank's time."""
+    import torch
+
+    from gdnr.shard import ShardPlan
+
+    GB_, NL, L = 1024, 24, 16
+    shard = ShardPlan(GB_, world).local(rank)
+    B = len(shard)
+    steps = max(L, (args.config5_steps + L - 1) // L * L)
+    stack = LayerStack(B, L, NL, lambda li: (args.seed * 1000003 + li) * 65536 + shard.start, device)
+    pos = uniform_positions(B, L, device)
+    err = torch.zeros(1, dtype=torch.int32, device=device)
+    graphs = capture_positions(lambda s: stack.launch(s, pos[s], flush_hint_for(s, L), err), L, stream)
+    with torch.cuda.stream(stream):
+        for s in range(L):
+            graphs[s].replay()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for i in range(steps):
+            graphs[i % L].replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = e0.elapsed_time(e1)
+    per_rank = gather_over_ranks(ms, world)
+    del graphs, stack
+    torch.cuda.empty_cache()
+    ms_max = max(per_rank)
+    return {"value": GB_ * NL * steps / (ms_max / 1e3), "unit": UNIT, "scaling": "strong", "n_gpus": world,
+            "sequences": GB_, "layers": NL, "ring": L, "steps": steps, "ms_max": ms_max,
+            "per_rank_ms": per_rank, "per_rank_sequences": [len(r) for r in ShardPlan(GB_, world).ranges],
+            "device_error_word": int(err.item()),
+            "workload": f"24 layers x 1024 sequences split over {world} GPU(s) (rank r owns a contiguous 1024/N "
+                        f"range), L=16, {steps} steps; per rank one CUDA graph per ring position; no collective"}
 
 
 def run_e2e(args, layers, step_inputs, pos, stream, world):
@@ -724,6 +1071,10 @@ def run_comparators(args, device, stream, ours_us):
     res["bf16_step_sm100a"] = {"us_per_layer_step": us, "state_GB_s": state_bytes / (us * 1e-6) / 1e9,
                                "speedup_of_ours": us / ours_us}
     del sets
+    res["triton_reference"] = run_triton_reference(args, device, stream)
+    tr = res["triton_reference"].get(f"L{args.ring}", {})
+    if "full_contract_us_per_layer_step" in tr:
+        tr["speedup_of_ours_full_contract"] = tr["full_contract_us_per_layer_step"] / ours_us
     try:
         from vllm.model_executor.layers.fla.ops.fused_recurrent import \
             fused_recurrent_gated_delta_rule_packed_decode as fla_decode
@@ -754,13 +1105,105 @@ def run_comparators(args, device, stream, ours_us):
     return res
 
 
+def run_triton_reference(args, device, stream):
+    """Same-box bar: the reference's own Triton kernels (gdn_prep_ring,
+    gdn_replay_fp8, gdn_replay_fp8_split of prototype/gdn_replayssm_fp8_kernel.py
+    :710, :344, :1129) as its stock wrappers launch them, when baseline/_ref/
+    holds a copy of the reference's prototype/ directory (it is not part of this
+    repository).  Batch 64, L in {4, 8, 16}, bf16 rings and fp16 scales as in the
+    reference's full-contract benchmark, over > 2x L2 of layer states, one CUDA
+    graph per ring position.  Per layer-step, amortised over a cycle like
+    bench_gdn_full_contract.py:225-308: core = (sum of the non-flush replays at
+    fills 1..L-1, best block_v of 32/64/128, + the flush at block_v 32) / L;
+    full = core + prep."""
+    if not (REF_DIR / "gdn_replayssm_fp8_kernel.py").exists():
+        return {"unavailable": "no copy of the reference's prototype/ in baseline/_ref"}
+    import torch
+
+    import gdnr
+    from gdnr import traffic
+
+    try:
+        sys.path.insert(0, str(REF_DIR))
+        import gdn_replayssm_fp8_kernel as rk  # noqa: E402  (the reference's own module)
+    except Exception as e:
+        return {"unavailable": f"{type(e).__name__}: {e}"[:200]}
+    bf = torch.bfloat16
+    B = args.batch
+    res = {"batch": B}
+    for L in (4, 8, 16):
+        NL = max(1, math.ceil(2.2 * L2_BYTES / traffic.state_bytes(B, L, scale_bytes=2, gate_bytes=2)))
+        gen = torch.Generator(device=device)
+        gen.manual_seed(args.seed * 97 + L)
+        lay = []
+        for li in range(NL):
+            ck = gdnr.quantize_checkpoint(0.02 * torch.randn(B, HV, KD, KD, generator=gen, device=device), "vblock",
+                                          scale_dtype=torch.float16, compute_saturation=False)
+            lay.append({
+                "ck": ck.payload, "sc": ck.scale,
+                "mixed": torch.randn(L, B, W_MIXED, generator=gen, device=device).to(bf),
+                "a": torch.randn(L, B, HV, generator=gen, device=device),
+                "b": torch.randn(L, B, HV, generator=gen, device=device),
+                "q": torch.empty(B, H, KD, dtype=bf, device=device),
+                "k": torch.zeros(B, L, H, KD, dtype=bf, device=device),
+                "v": torch.zeros(B, L, HV, KD, dtype=bf, device=device),
+                "g": torch.zeros(B, L, HV, dtype=bf, device=device),
+                "beta": torch.zeros(B, L, HV, dtype=bf, device=device),
+                "out": torch.empty(B, HV, KD, dtype=bf, device=device),
+                "tq": torch.empty(B, HV, KD, dtype=torch.float32, device=device),
+                "cf": torch.empty(B, HV, L, dtype=torch.float32, device=device),
+            })
+        a_log = torch.rand(HV, generator=gen, device=device)
+        dt_bias = torch.rand(HV, generator=gen, device=device) - 4.0
+        pos = uniform_positions(B, L, device)
+        valid = [torch.full((B,), s + 1, dtype=torch.int32, device=device) for s in range(L)]
+        no_flush = torch.zeros(B, dtype=torch.bool, device=device)
+        flush = torch.ones(B, dtype=torch.bool, device=device)
+
+        def prep(s):
+            for d in lay:
+                rk.gdn_prep_ring(d["mixed"][s], d["a"][s], d["b"][s], a_log, dt_bias, pos[s], d["q"], d["k"], d["v"],
+                                 d["g"], d["beta"])
+
+        def replay(s, block_v):
+            for d in lay:
+                rk.gdn_replay_fp8(d["ck"], d["sc"], d["q"], d["k"], d["v"], d["g"], d["beta"], valid[s],
+                                  flush if s == L - 1 else no_flush, block_v=block_v, out=d["out"])
+
+        def split(s):
+            for d in lay:
+                rk.gdn_replay_fp8_split(d["ck"], d["sc"], d["q"], d["k"], d["v"], d["g"], d["beta"], valid[s],
+                                        d["tq"], d["cf"], out=d["out"])
+        try:
+            prep_us = 1e3 * statistics.fmean(time_cycles(capture_positions(prep, L, stream), stream, 4)) / NL
+            nonflush = {}
+            for bv in (32, 64, 128):
+                per = time_cycles(capture_positions(lambda s, bv=bv: replay(s, bv), L - 1, stream), stream, 4)
+                nonflush[bv] = [1e3 * t / NL for t in per]
+            best = [min(nonflush[bv][i] for bv in nonflush) for i in range(L - 1)]
+            flush_us = 1e3 * time_cycles(capture_positions(lambda s: replay(L - 1, 32), 1, stream), stream, 4)[0] / NL
+            split_us = 1e3 * time_cycles(capture_positions(lambda s: split(L - 2), 1, stream), stream, 4)[0] / NL
+        except Exception as e:
+            res[f"L{L}"] = {"error": f"{type(e).__name__}: {e}"[:300]}
+            continue
+        core = (sum(best) + flush_us) / L
+        res[f"L{L}"] = {"layers": NL, "prep_us": prep_us, "replay_us_by_fill": best,
+                        "replay_us_full_ring_nonflush": best[-1], "flush_us": flush_us,
+                        "split_us_fill_L_minus_1": split_us, "core_us_per_layer_step": core,
+                        "full_contract_us_per_layer_step": core + prep_us,
+                        "best_block_v_by_fill": [min(nonflush, key=lambda bv: nonflush[bv][i]) for i in range(L - 1)]}
+        del lay
+        torch.cuda.empty_cache()
+    return res
+
+
 def run_core(args, device, stream):
     """core replay (non-flush) of a full L=16 ring, block-V sweep."""
     import torch
 
     import gdnr
     from gdnr import inputs as gin
-    from oracle import gdn_oracle as O
+    from gdnr import traffic
 
     B, L, NL = args.batch, args.ring, args.layers
     sets = []
@@ -771,7 +1214,7 @@ def run_core(args, device, stream):
                      torch.zeros(B, dtype=torch.bool, device=device),
                      torch.empty(B, HV, KD, dtype=torch.bfloat16, device=device)))
     res = {}
-    nbytes = O.algorithmic_bytes(B, L, L, scale_bytes=4, gate_bytes=4, fused=False)
+    nbytes = traffic.step_bytes(B, L, L, fused=False)
 
     def run():
         for ck, d, vl, fl, out in sets:

@@ -833,9 +833,13 @@ __device__ __forceinline__ S5Append s5_chain(const StepParams& p, const S5Unit& 
     const float4 v = gr4[4];
     kq = v.x + v.y + v.z;
   }
-  // ---- decays in log2 space per head (16-lane segment): Lg_t = sum_{m<=t} g_m log2(e),
-  // a_t = 2^Lg_t, d_t = 2^(Lg_{n-1} - Lg_t), M[t][j] = 2^(Lg_j - Lg_t) G[t][j]  (t < j)
-  float Lg = t < n ? g_own * S5_LOG2E : 0.0f;
+  // ---- decays in log2 space per head (16-lane segment), gl_m = g_m log2(e):
+  // a_t = 2^(sum_{m<=t} gl_m), and the ratios d_t = 2^(sum_{t<m<n} gl_m) and
+  // M[t][j] = 2^(sum_{t<m<=j} gl_m) G[t][j] (t < j) from running sums over (t, j]
+  // -- not as differences of two prefix sums, which would carry the rounding of
+  // the whole prefix (~|prefix| eps, large under strong decay) into every ratio.
+  const float gl = t < n ? g_own * S5_LOG2E : 0.0f;
+  float Lg = gl;
 #pragma unroll
   for (int o = 1; o < 16; o <<= 1) {
     const float up = __shfl_up_sync(0xffffffffu, Lg, o, 16);
@@ -843,6 +847,17 @@ __device__ __forceinline__ S5Append s5_chain(const StepParams& p, const S5Unit& 
   }
   const float Llast = __shfl_sync(0xffffffffu, Lg, 15, 16);  // slots >= n add nothing
   const float a_own = s5_ex2(Lg);
+  float em[16], dsum = 0.0f;
+  {
+    float run = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float gj = __shfl_sync(0xffffffffu, gl, j, 16);
+      if (j > t) run += gj;
+      em[j] = s5_ex2(run) * grow[j];  // used for j > t only
+      if (j == n - 1) dsum = run;
+    }
+  }
   if (FLUSH && s5_flush(code)) {
     // flush unit: hand the rebuild's inputs to the readout team (the T chain
     // is not needed: the flush output comes from the rebuilt state)
@@ -863,10 +878,10 @@ __device__ __forceinline__ S5Append s5_chain(const StepParams& p, const S5Unit& 
       float* nm = fh + S5_FN;
       const bool live = t < n, wr = e < HPU;
       const float bt = live ? beta_own : 0.0f;
-      const float dt = live ? s5_ex2(Llast - Lg) : 0.0f;
+      const float dt = live ? s5_ex2(dsum) : 0.0f;
 #pragma unroll
       for (int j = 0; j < 16; ++j) {  // row t of N
-        const float mj = s5_ex2(__shfl_sync(0xffffffffu, Lg, j, 16) - Lg) * grow[j];
+        const float mj = em[j];
         const float bj = __shfl_sync(0xffffffffu, bt, j, 16);
         if (wr) nm[t * 16 + j] = j > t ? (live ? mj * bj : 0.0f) : (j == t ? dt * kq : 0.0f);
       }
@@ -952,12 +967,9 @@ __device__ __forceinline__ S5Append s5_chain(const StepParams& p, const S5Unit& 
     return ap;
   }
   const float bsel = t < n ? beta_own : 0.0f;
-  float acc = t < n ? s5_ex2(Llast - Lg) * kq : 0.0f;
+  float acc = t < n ? s5_ex2(dsum) * kq : 0.0f;
   float cval = 0.0f;
   // ---- triangular solve, j = n-1 .. 0: c_j = beta_j (d_j kq_j - sum_{m>j} c_m M[j][m])
-  float em[16];
-#pragma unroll
-  for (int j = 0; j < 16; ++j) em[j] = s5_ex2(__shfl_sync(0xffffffffu, Lg, j, 16) - Lg) * grow[j];
   s5_solve(em, bsel, acc, cval, t);
   // ---- c -> [c_hi; c_mid; c_lo] bf16 over the slots read from memory (ring
   // columns of the readout); this token's own slot is a rank-one term

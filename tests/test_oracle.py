@@ -204,3 +204,16 @@ def test_algorithmic_bytes_match_documented_figures():
     cycle = sum(O.algorithmic_bytes(64, n, 16, scale_bytes=4) for n in range(1, 17))
     assert cycle == 705_466_368
     assert cycle // 16 == 44_091_648
+
+
+def test_package_byte_model_equals_oracle():
+    """gdnr.traffic (used by bench.py) and the oracle's byte model agree."""
+    from gdnr import traffic
+
+    for B in (1, 4, 64, 256):
+        for L in (4, 8, 16, 64):
+            for n in range(1, L + 1):
+                assert traffic.step_bytes(B, n, L) == O.algorithmic_bytes(B, n, L, scale_bytes=4, gate_bytes=4)
+                assert traffic.step_bytes(B, n, L, fused=False) == O.algorithmic_bytes(
+                    B, n, L, scale_bytes=4, gate_bytes=4, fused=False)
+    assert traffic.cycle_bytes(64, 16) == 44_091_648
