@@ -457,9 +457,12 @@ def spread_positions(B, L, device):
 
 
 def capture_positions(fn, L, stream):
-    """One CUDA graph per ring position s of fn(s) (after one eager pass)."""
+    """One CUDA graph per ring position s of fn(s) (after one eager pass).
+    Everything the default stream has enqueued (the inputs' initialisation)
+    completes first: the launches go to a side stream."""
     import torch
 
+    torch.cuda.synchronize()
     with torch.cuda.stream(stream):
         for s in range(L):
             fn(s)
@@ -725,7 +728,9 @@ def run_sweep(args, device, stream):
     for B in (1, 4, 16, 64, 256):
         for L in (4, 8, 16):
             NL = max(1, min(512, math.ceil(2.2 * L2_BYTES / traffic.state_bytes(B, L))))
+            print(f"bench: sweep cell B={B} L={L} ({NL} layers)", file=sys.stderr, flush=True)
             stack = LayerStack(B, L, NL, lambda li: (args.seed * 7919 + B * 131 + L) * 4096 + li, device)
+            torch.cuda.synchronize()
             pos = uniform_positions(B, L, device)
             err = torch.zeros(1, dtype=torch.int32, device=device)
             graphs = capture_positions(lambda s: stack.launch(s, pos[s], flush_hint_for(s, L), err), L, stream)
@@ -893,7 +898,9 @@ def run_e2e(args, layers, step_inputs, pos, stream, world):
             stream.wait_stream(s_in)
         stream.wait_stream(s_out)
 
-    # eager pass over the ring (warms up every path), then one graph per position
+    # eager pass over the ring (warms up every path), then one graph per position;
+    # the buffers above are initialised on the default stream: let that finish first
+    torch.cuda.synchronize()
     for s in range(L):
         with torch.cuda.stream(stream):
             step_body(s)
@@ -928,9 +935,11 @@ def run_e2e(args, layers, step_inputs, pos, stream, world):
 
 
 def _graph_us(fn, stream, reps):
-    """Mean device time of ``fn`` (captured once in a CUDA graph) over ``reps`` replays."""
+    """Mean device time of ``fn`` (captured once in a CUDA graph) over ``reps`` replays
+    (after the default stream's pending work, which initialises fn's inputs)."""
     import torch
 
+    torch.cuda.synchronize()
     with torch.cuda.stream(stream):
         fn()
     torch.cuda.synchronize()
@@ -1220,6 +1229,7 @@ def run_core(args, device, stream):
         for ck, d, vl, fl, out in sets:
             gdnr.gdn_replay_fp8(ck.payload, ck.scale, d["q"], d["k"], d["v"], d["g"], d["beta"], vl, fl, out=out,
                                 flush_hint="none")
+    torch.cuda.synchronize()  # the inputs above come from the default stream
     with torch.cuda.stream(stream):
         run()
     torch.cuda.synchronize()

@@ -584,9 +584,12 @@ __device__ __forceinline__ S5In s5_fetch(const StepParams& p, const S5Unit& U, i
   const int e = lane >> 4, t = lane & 15;
   const int hv = U.hv0 + (e < HPU ? e : 0);
   const int ts = t < p.L ? t : p.L - 1;
-  in.g = s5_ld_raw(p.gr, int64_t(U.s) * p.gr_sb + int64_t(ts) * p.gr_st + int64_t(hv) * p.gr_sh, p.gr_dt);
-  in.beta = s5_ld_raw(p.br, int64_t(U.s) * p.br_sb + int64_t(ts) * p.br_st + int64_t(hv) * p.br_sh, p.br_dt);
-  in.scr = FLUSH ? s5_ld_raw(p.sc, int64_t(U.s) * p.sc_sb + int64_t(hv) * p.sc_sh + int64_t(t & 3) * p.sc_sv, p.sc_dt)
+  // a null or bad slot (U.s < 0, packed decode) reads slot 0's gates and scales:
+  // the unit is skipped, the values are never used, and no load leaves the tensors
+  const int64_t sl = U.s < 0 ? 0 : U.s;
+  in.g = s5_ld_raw(p.gr, sl * p.gr_sb + int64_t(ts) * p.gr_st + int64_t(hv) * p.gr_sh, p.gr_dt);
+  in.beta = s5_ld_raw(p.br, sl * p.br_sb + int64_t(ts) * p.br_st + int64_t(hv) * p.br_sh, p.br_dt);
+  in.scr = FLUSH ? s5_ld_raw(p.sc, sl * p.sc_sb + int64_t(hv) * p.sc_sh + int64_t(t & 3) * p.sc_sv, p.sc_dt)
                  : 0u;
   if constexpr (FUSED) {
     const bool bf = p.mx_dt == GDNR_BF16;
@@ -1482,7 +1485,14 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
   uint64_t* mmab = reinterpret_cast<uint64_t*>(smem + lay.mmab);    // tensor-core readout of a stage done
   int* table = reinterpret_cast<int*>(smem + lay.table);
   uint32_t* tdone = reinterpret_cast<uint32_t*>(smem + lay.tdone);  // flush tasks done per unit (tensor-memory readout)
-  const bool aligned = (smem_addr(smem) & 1023u) == 0;  // swizzled TMA boxes need 1024-byte alignment
+  // self-check of the launch: the swizzled TMA boxes need 1024-byte alignment, and
+  // the layout must fit the dynamic shared memory the launch was given
+  uint32_t dyn_smem;
+  asm("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn_smem));
+  if ((smem_addr(smem) & 1023u) != 0 || lay.total > dyn_smem) {
+    if (tid == 0) atomicOr(p.err, GDNR_DEVERR_LAYOUT);
+    return;
+  }
   const uint32_t box_bytes = uint32_t(geo.rb) * 256u;
   const uint32_t ck_bytes = uint32_t(HPU) * 16384u;
 
@@ -1505,13 +1515,11 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       vword[st] = 0xffffffffu;
       vdone[st] = 0u;
     }
-    *abort = aligned ? 0 : 1;
+    *abort = 0;
     reinterpret_cast<volatile int*>(smem + lay.tmem)[1] = -1;  // commits issued, published by the scheduler at exit
     fence_mbar_init();
-    if (!aligned) atomicOr(p.err, GDNR_DEVERR_WAIT_TIMEOUT);
   }
   __syncthreads();
-  if (!aligned) return;
   // two-head units: the first readout warp allocates the readout's tensor
   // memory (released by the same warp at the end); the other readout warps see
   // the address after barrier 1

@@ -43,6 +43,7 @@ DEVERR_WAIT_TIMEOUT = 0x1
 DEVERR_BAD_POS = 0x2
 DEVERR_BAD_HINT = 0x4
 DEVERR_BAD_SLOT = 0x8
+DEVERR_LAYOUT = 0x10
 
 
 class Tensor(ctypes.Structure):

@@ -59,6 +59,8 @@ typedef enum {
 #define GDNR_DEVERR_BAD_POS 0x2u      /* fused step: pos[b] outside [0, L) */
 #define GDNR_DEVERR_BAD_HINT 0x4u     /* flush_hint NONE but a sequence's ring was full */
 #define GDNR_DEVERR_BAD_SLOT 0x8u     /* packed decode: state_indices[i] >= slots */
+#define GDNR_DEVERR_LAYOUT 0x10u      /* a kernel's shared memory did not fit its layout (a launch
+                                         configuration fault of the library): nothing was done */
 
 /* flush_hint: what the caller knows about which sequences flush in this call */
 #define GDNR_FLUSH_AUTO 0 /* unknown: every head is checked on the device */
