@@ -78,6 +78,13 @@ def parse_args():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-config5", action="store_true")
     ap.add_argument("--config5-steps", type=int, default=256)
+    ap.add_argument("--drift", action="store_true",
+                    help="BASELINE config 4 instead of the benchmark: drift of the FP8 replay chain vs an fp32 "
+                         "recurrence (one JSON line)")
+    ap.add_argument("--drift-steps", type=int, default=4096)
+    ap.add_argument("--drift-layers", type=int, default=4)
+    ap.add_argument("--drift-rings", default="4,16,64")
+    ap.add_argument("--drift-stride", type=int, default=256)
     ap.add_argument("--profile", type=int, default=None, metavar="POS",
                     help="profiling driver for ncu: a few untimed launches of one layer's step at ring position "
                          "POS (no timing, no JSON line)")
@@ -787,6 +794,106 @@ def fla_packed_decode_us(B, seed, device, stream):
     return 1e3 * per[0] / NL
 
 
+def run_drift(args, local):
+    """long-sequence drift of the FP8 checkpoint + replay
+    scheme against an fp32 per-token recurrence run alongside on the GPU, by the
+    reference's dual-chain method (prototype/qwen35_drift_study.py:341-379): the
+    true state evolves token by token in fp32; each arm (ring length L) keeps the
+    checkpoint + ring that gdn_fused_step maintains, its output is the kernel's,
+    and its reconstructed state (the recurrence from the dequantised checkpoint
+    over the ring, restarted from the kernel's re-quantised checkpoint at every
+    flush) is compared with the true state after every token.  Synthetic
+    inputs: q, k, v ~ N(0,1) bf16, A_log = 0 and a solved so that
+    alpha = exp(g) ~ U(0.9, 0.999), b ~ N(0,1), state ~ N(0, 0.02).  Both chains
+    consume the same prepped q, k, v, g, beta (the kernel's ring contents).
+    Reports mean / final state and output relative L2 per arm, a curve every
+    `--drift-stride` steps, and the steady-state µs per layer-step of each arm."""
+    import torch
+
+    import gdnr
+    from gdnr import inputs as gin
+
+    device = torch.device("cuda", local)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    NLy, B, T = args.drift_layers, args.batch, args.drift_steps
+    rings = [int(x) for x in args.drift_rings.split(",")]
+    NB = NLy * B  # the layers as independent batch ranges of one state
+    gen = torch.Generator(device=device)
+    gen.manual_seed(args.seed * 4099 + 4)
+    s0 = 0.02 * torch.randn(NB, HV, KD, KD, generator=gen, device=device)
+    truth = s0.clone()
+    arms = {}
+    for L in rings:
+        st = gdnr.ReplayState.allocate(NB, H, HV, L, device=device)
+        st.load_state(s0)
+        recon = gdnr.dequantize_checkpoint(gdnr.QuantizedCheckpoint(st.checkpoint, st.scale, "vblock", 32, 0.0)).clone()
+        arms[L] = {"state": st, "recon": recon, "sd": [], "od": [], "curve": []}
+    gates = gin.drift_gate_inputs(NB, T, HV, seed=args.seed * 4099 + 5, device=device)
+    a_log, dt_bias = gates["a_log"], gates["dt_bias"]
+    out = torch.empty(NB, HV, KD, dtype=torch.float32, device=device)
+    q_out = torch.empty(NB, H, KD, dtype=torch.bfloat16, device=device)  # q as the production step keeps it
+    nxt = torch.empty(NB, dtype=torch.int32, device=device)
+    scale = KD ** -0.5
+    G = HV // H
+
+    def rel(a, b):
+        return float(torch.linalg.vector_norm(a - b) / torch.linalg.vector_norm(b).clamp_min(1e-30))
+
+    def recur(S, q, k, v, g, beta):  # one fp32 token (ref.py:137-163), exact products
+        Sv = S.view(NB * HV, KD, KD)
+        Sv.mul_(torch.exp(g).view(-1, 1, 1))
+        kk = k.repeat_interleave(G, 1).reshape(NB * HV, KD, 1)
+        r = torch.bmm(Sv, kk)
+        u = (v.reshape(NB * HV, KD, 1) - r) * beta.reshape(NB * HV, 1, 1)
+        Sv.baddbmm_(u, kk.transpose(1, 2))
+        qq = q.repeat_interleave(G, 1).reshape(NB * HV, KD, 1)
+        return (torch.bmm(Sv, qq).view(NB, HV, KD) * scale)
+
+    for t in range(T):
+        mixed = torch.randn(NB, W_MIXED, generator=gen, device=device).to(torch.bfloat16)
+        a = gates["a"][:, t].contiguous()
+        b = torch.randn(NB, HV, generator=gen, device=device)
+        true_o = None
+        for L, arm in arms.items():
+            st = arm["state"]
+            p = t % L
+            st.step(mixed, a, b, a_log, dt_bias, out=out, q_out=q_out, pos_out=nxt)
+            q = q_out.float()
+            k = st.k_ring[:, p].float()
+            v = st.v_ring[:, p].float()
+            g = st.g_ring[:, p].float()
+            be = st.beta_ring[:, p].float()
+            if true_o is None:  # every arm prepped the same token: the truth consumes it once
+                true_o = recur(truth, q, k, v, g, be)
+            recur(arm["recon"], q, k, v, g, be)
+            if p == L - 1:  # flush: the reconstruction restarts from the kernel's re-quantised checkpoint
+                arm["recon"].copy_(gdnr.dequantize_checkpoint(
+                    gdnr.QuantizedCheckpoint(st.checkpoint, st.scale, "vblock", 32, 0.0)))
+            arm["sd"].append(rel(arm["recon"], truth))
+            arm["od"].append(rel(out, true_o))
+            if t % args.drift_stride == 0 or t == T - 1:
+                arm["curve"].append([t, round(arm["sd"][-1], 6), round(arm["od"][-1], 6)])
+            st.pos.copy_(nxt)
+    res = {"metric": "drift (relative L2 vs an fp32 per-token recurrence)", "layers": NLy, "batch": B, "steps": T,
+           "alpha": [0.9, 0.999], "arms": {}}
+    # steady-state time per layer-step of each arm: NLy layers of B sequences, one cycle
+    stream = torch.cuda.Stream(device)
+    for L, arm in arms.items():
+        stack = LayerStack(B, L, NLy, lambda li: args.seed * 7 + li, device)
+        pos = uniform_positions(B, L, device)
+        graphs = capture_positions(lambda s: stack.launch(s, pos[s], flush_hint_for(s, L)), L, stream)
+        per = time_cycles(graphs, stream, cycles=max(1, 64 // L))
+        del graphs, stack
+        sd, od = arm["sd"], arm["od"]
+        res["arms"][f"L{L}"] = {
+            "state_drift_mean": statistics.fmean(sd), "state_drift_final": sd[-1],
+            "output_drift_mean": statistics.fmean(od), "output_drift_final": od[-1],
+            "us_per_layer_step": 1e3 * statistics.fmean(per) / NLy,
+            "kernel": "step5_kernel (persistent)" if L <= 16 else "step_kernel (CUDA cores, rings of L > 16)",
+            "curve_step_state_output": arm["curve"]}
+    print(json.dumps(res), flush=True)
+
+
 def run_config5(args, world, rank, device, stream):
     """a fixed job of 24 GDN layers x 1024 sequences, L=16,
     split evenly over the ranks (strong scaling), config5_steps decode steps
@@ -1264,6 +1371,8 @@ def main():
             run_reference(args, world, rank)
         elif args.profile is not None:
             run_profile(args, local)
+        elif args.drift:
+            run_drift(args, local)
         else:
             run_ours(args, world, rank, local)
     finally:

@@ -40,6 +40,7 @@
 namespace gdnr {
 
 constexpr int S5_NS = 4;    // checkpoint / value-ring stages
+constexpr int S5_PF = 4;    // units beyond the stages kept prefetched into L2
 constexpr int S5_NCW = 7;   // chain warps
 constexpr int S5_NRW = 8;   // readout warps
 constexpr int S5_TEAM = S5_NRW / S5_NS;  // readout warps per stage
@@ -396,6 +397,9 @@ __device__ __forceinline__ int s5_nmem(int code) { return (code >> 8) & 0xff; }
 __device__ __forceinline__ bool s5_skip(int code) { return (code >> 16) & 1; }
 // bit 17: the unit flushes here (rebuild + re-quantisation in this kernel)
 __device__ __forceinline__ bool s5_flush(int code) { return (code >> 17) & 1; }
+// Table entries also carry, in bits 24-31, the CTA-local index of the unit they
+// describe (units bid + index * gridDim.x); entry i is the i-th unit processed.
+__device__ __forceinline__ int s5_uidx(int entry) { return int(uint32_t(entry) >> 24); }
 
 // A unit: batch row b, key head h, pair pp of its value heads (first value head
 // hv0); s: the row's state slot -- b, or under packed decode state_indices[b],
@@ -1621,7 +1625,28 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       atomicOr(p.err, GDNR_DEVERR_BAD_HINT);
     if (!FUSED && s5_skip(code) && p.flush_hint == GDNR_FLUSH_NONE && U.h == 0 && U.pp == 0)
       atomicOr(p.err, GDNR_DEVERR_BAD_HINT);
-    table[ti] = code;
+    raw0 = code;
+  }
+  // Processing order.  In the tensor-memory variant, when every unit of the CTA has
+  // a chain warp of its own (nu <= S5_NCW, so the chain phases impose no order)
+  // and no checkpoint was requested ahead by the PDL prologue, the flush units go
+  // first: their vblock tasks then overlap the other units' chains instead of
+  // trailing the CTA's last readout.  The units' entries are then all in the
+  // last warp (ti = 31 - lane).  Otherwise unit order.
+  if (ti < 32 && warp == (S5_THREADS / 32) - 1) {
+    int at = ti;
+    if (TC && nu <= S5_NCW && !p.pdl) {
+      const uint32_t vm = __ballot_sync(0xffffffffu, ti < nu);
+      const uint32_t fm = __ballot_sync(0xffffffffu, ti < nu && s5_flush(raw0));
+      const uint32_t gt = lane == 31 ? 0u : (0xffffffffu << (lane + 1));  // the units before this one
+      at = (ti < nu && s5_flush(raw0)) ? __popc(fm & gt) : __popc(fm) + __popc(vm & ~fm & gt);
+    }
+    if (ti < nu) {
+      table[at] = raw0 | (ti << 24);
+      tdone[at] = 0u;
+    }
+  } else if (ti < nu) {
+    table[ti] = raw0 | (ti << 24);
     tdone[ti] = 0u;
   }
   // The table is for the producer and the readout warps: the readout warps
@@ -1638,11 +1663,12 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
   if (warp == 0) {
     // =================== producer / scheduler ===================
     if (lane != 0) return;
-    // stage loads of unit i (stage i % S5_NS, free once its previous unit is read out)
+    // stage loads of entry i (stage i % S5_NS, free once its previous unit is read out)
+    int pf_next = S5_NS;  // next entry to prefetch into L2
     auto load_unit = [&](int i) {
       const int s = i % S5_NS;
       const int code = table[i];
-      const S5Unit U = s5_unit<SIDX>(bid + i * grid, p, G, geo);
+      const S5Unit U = s5_unit<SIDX>(bid + s5_uidx(code) * grid, p, G, geo);
       uint8_t* sb = smem + lay.stage0 + s * lay.stage_bytes;
       const bool skip = s5_skip(code);
       const int nreq = skip ? 0 : (s5_nmem(code) + geo.rb - 1) / geo.rb;
@@ -1653,13 +1679,14 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
 #pragma unroll
         for (int e = 0; e < HPU; ++e)
           s5_tma5(sb + lay.vr + e * 4096 + j * box_bytes, &vr_map, 0, 0, U.hv0 + e, j * geo.rb, U.s, &full[s]);
-      if (i == S5_NS - 1) {
-        // the units that wait for a free stage: their tiles and rings into L2 now,
-        // so that their stage loads later are served from L2
-        for (int u = S5_NS; u < nu; ++u) {
-          const int cu = table[u];
+      if (i >= S5_NS - 1) {
+        // the next S5_PF units waiting for a free stage: their tiles and rings into
+        // L2 now, so that their stage loads later are served from L2 (a bounded
+        // window: prefetching every remaining unit of a large batch would overrun L2)
+        for (; pf_next < nu && pf_next <= i + S5_PF; ++pf_next) {
+          const int cu = table[pf_next];
           if (s5_skip(cu)) continue;
-          const S5Unit V = s5_unit<SIDX>(bid + u * grid, p, G, geo);
+          const S5Unit V = s5_unit<SIDX>(bid + s5_uidx(cu) * grid, p, G, geo);
           s5_prefetch4(&ck_map, 0, 0, V.hv0, V.s);
           const int nr = (s5_nmem(cu) + geo.rb - 1) / geo.rb;
           for (int j = 0; j < nr; ++j)
@@ -1691,11 +1718,12 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
           load_unit(nl++);
           progress = true;
         }
+        const int um = nm < nl ? s5_uidx(table[nm]) : 0;  // the entry's unit: chain warp um % S5_NCW
         if (nm < nl && s5_test_wait(&full[nm % S5_NS], uint32_t((nm / S5_NS) & 1)) &&
-            s5_test_wait(&cbar[nm % S5_NCW], uint32_t((nm / S5_NCW) & 1))) {
+            s5_test_wait(&cbar[um % S5_NCW], uint32_t((um / S5_NCW) & 1))) {
           const int su = nm % S5_NS, cu = table[nm];
           if (!(FLUSH && s5_flush(cu)) && !s5_skip(cu)) {
-            const uint8_t* res = smem + lay.res0 + (nm % S5_NCW) * lay.res_bytes;
+            const uint8_t* res = smem + lay.res0 + (um % S5_NCW) * lay.res_bytes;
             const uint8_t* sbu = smem + lay.stage0 + su * lay.stage_bytes;
             s5_tc_after_sync();
 #pragma unroll
@@ -1796,14 +1824,15 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
     for (int i = 0; i < nu; ++i) {
       const int s = i % S5_NS;
       const uint32_t par = (i / S5_NS) & 1;
-      const int ccw = i % S5_NCW, k = i / S5_NCW;
       const int code = table[i];
-      const float sc_pref = s5_cvt(__shfl_sync(0xffffffffu, scl_raw, i & 31), p.sc_dt);
+      const int ui = s5_uidx(code);  // the unit of entry i (flush units may come first)
+      const int ccw = ui % S5_NCW, k = ui / S5_NCW;
+      const float sc_pref = s5_cvt(__shfl_sync(0xffffffffu, scl_raw, ui & 31), p.sc_dt);
       bool ok = s5_warp_wait(&full[s], par, p.err, abort, lane);
       ok = s5_warp_wait(&cbar[ccw], uint32_t(k & 1), p.err, abort, lane) && ok;
       const bool flush = FLUSH && s5_flush(code);
       uint8_t* sb = smem + lay.stage0 + s * lay.stage_bytes;
-      const S5Unit U = s5_unit<SIDX>(bid + i * grid, p, G, geo);
+      const S5Unit U = s5_unit<SIDX>(bid + ui * grid, p, G, geo);
       const bool mma = ok && !flush && !s5_skip(code);
       const uint8_t* res = smem + lay.res0 + ccw * lay.res_bytes;
       // V^T c over the slots read from memory (no tensor memory needed yet)
@@ -1843,7 +1872,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
         }
       } else if (mma) {
         float sc = sc_pref;
-        if (i >= 32)
+        if (ui >= 32)
           sc = load_scalar(p.sc, int64_t(U.s) * p.sc_sb + int64_t(U.hv0 + head_r) * p.sc_sh + int64_t(qd) * p.sc_sv,
                            p.sc_dt);
         const float* misc = reinterpret_cast<const float*>(res + lay.misc) + head_r * 4;
