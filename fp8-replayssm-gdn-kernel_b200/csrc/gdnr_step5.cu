@@ -102,7 +102,7 @@ __host__ __device__ inline S5Geo s5_geo(int H, int HV, int L) {
 //        doubles as the chain's q-split / Gram scratch before T is written)
 //   [ost: 128 floats] x S5_NRW
 struct S5Layout {
-  uint32_t full, empty, kfull, cbar, rbar, abort, vword, vdone, mmab, tmem, table, tdone;
+  uint32_t full, empty, kfull, cbar, rbar, abort, vword, vdone, mmab, tmem, table, tdone, gwords;
   uint32_t stage0, stage_bytes, ck, vr;
   uint32_t kbuf0;
   uint32_t res0, res_bytes, t8, cb, cf, misc, vnew;
@@ -126,6 +126,9 @@ __host__ __device__ inline S5Layout s5_layout(const S5Geo& g, int max_units, boo
   s.tmem = smem_take(o, 16);
   s.table = smem_take(o, uint32_t(max_units) * 4u);
   s.tdone = smem_take(o, uint32_t(max_units) * 4u);
+  // readout groups (tensor-memory variant): [0] flush entries, [1] claim counter,
+  // [2..7] per group a double-buffered claimed rank, [8..15] the claimable entries
+  s.gwords = smem_take(o, 16u * 4u);
   o = (o + 1023u) & ~1023u;
   s.stage0 = o;
   s.ck = 0;
@@ -181,6 +184,16 @@ __device__ __forceinline__ void s5_arrive(uint64_t* bar) {
 
 // Relaxed arrive / add, for releases that only end reads whose values have
 // already been consumed (nothing to order behind them).
+// Arrivals counting `n` (a readout group of 4 warps owes the 8 arrivals of a unit
+// that all 8 readout warps would otherwise make).
+__device__ __forceinline__ void s5_arrive_n(uint64_t* bar, uint32_t n) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(n) : "memory");
+}
+
+__device__ __forceinline__ void s5_arrive_relaxed_n(uint64_t* bar, uint32_t n) {
+  asm volatile("mbarrier.arrive.relaxed.cta.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(n) : "memory");
+}
+
 __device__ __forceinline__ void s5_arrive_relaxed(uint64_t* bar) {
   asm volatile("mbarrier.arrive.relaxed.cta.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
@@ -278,6 +291,20 @@ __device__ __forceinline__ void s5_tmem_ld16(uint32_t taddr, uint32_t* r) {
       "%15}, [%16];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
         "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// 32 consecutive 32-bit columns of this thread's tensor-memory lane (32x32b shape)
+__device__ __forceinline__ void s5_tmem_ld32(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr)
       : "memory");
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
@@ -1576,22 +1603,24 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
   // scale of the warp's head and vblock.  One-head units (teams): lane l holds
   // team unit l / (2 HPU), vblock l % (2 HPU) of the warp's rows.
   constexpr int VBW = 2 * HPU;  // vblocks per readout warp and unit (teams)
-  constexpr int SC_UNITS = TC ? 32 : 32 / VBW;
+  constexpr int SC_UNITS = 32 / VBW;  // team readout: units with a prefetched scale
   uint32_t scl_raw = 0u;
   const int rw = warp - 1 - S5_NCW;
   const int team = rw / S5_TEAM, mem = rw % S5_TEAM;
   const int head_r = TC ? (rw >> 2) : (HPU == 2 ? mem : 0);
   const int rbase = HPU == 2 ? 0 : 64 * mem;
   if (warp > S5_NCW) {
-    int i = TC ? lane : team + S5_NS * (lane / VBW);
-    i = i < nu ? i : 0;
-    const S5Unit U = s5_unit<SIDX>(bid + i * grid, p, G, geo);
-    const int vb = TC ? (warp & 3) : rbase / VBLOCK + lane % VBW;
-    scl_raw = s5_ld_raw(p.sc, int64_t(U.s < 0 ? 0 : U.s) * p.sc_sb + int64_t(U.hv0 + head_r) * p.sc_sh + int64_t(vb) * p.sc_sv,
-                        p.sc_dt);
-    if (TC) {  // the zero rows of the tensor-core T operands
+    if constexpr (TC) {  // the zero rows of the tensor-core T operands
       reinterpret_cast<uint32_t*>(smem + lay.zb)[tid - 32 * (1 + S5_NCW)] = 0u;
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    } else {
+      int i = team + S5_NS * (lane / VBW);
+      i = i < nu ? i : 0;
+      const S5Unit U = s5_unit<SIDX>(bid + i * grid, p, G, geo);
+      const int vb = rbase / VBLOCK + lane % VBW;
+      scl_raw = s5_ld_raw(p.sc, int64_t(U.s < 0 ? 0 : U.s) * p.sc_sb + int64_t(U.hv0 + head_r) * p.sc_sh +
+                                    int64_t(vb) * p.sc_sv,
+                          p.sc_dt);
     }
   }
   // ring positions of this CTA's units for the producer and the readout, read
@@ -1633,13 +1662,44 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
   // first: their vblock tasks then overlap the other units' chains instead of
   // trailing the CTA's last readout.  The units' entries are then all in the
   // last warp (ti = 31 - lane).  Otherwise unit order.
+  // Claim mode (tensor-memory variant, every unit with a chain warp of its own, no
+  // PDL prologue): the flush units take entries whose stage no later entry reuses
+  // (the last entries of the first round of stages, then the last entries), so
+  // that their long rebuild holds no stage another unit waits for; the other
+  // units fill the remaining entries in order, and readout groups claim those in
+  // order (the chain warps 1..4, whose single units are done early, forming a
+  // third group).  All the CTA's units are then in the last warp (ti = 31 - lane).
+  const bool claim = TC && nu <= S5_NCW && !p.pdl;
   if (ti < 32 && warp == (S5_THREADS / 32) - 1) {
     int at = ti;
-    if (TC && nu <= S5_NCW && !p.pdl) {
-      const uint32_t vm = __ballot_sync(0xffffffffu, ti < nu);
-      const uint32_t fm = __ballot_sync(0xffffffffu, ti < nu && s5_flush(raw0));
-      const uint32_t gt = lane == 31 ? 0u : (0xffffffffu << (lane + 1));  // the units before this one
-      at = (ti < nu && s5_flush(raw0)) ? __popc(fm & gt) : __popc(fm) + __popc(vm & ~fm & gt);
+    if (claim) {
+      const uint32_t fu = __brev(__ballot_sync(0xffffffffu, ti < nu && s5_flush(raw0)));  // bit ti: unit ti flushes
+      const int nf = __popc(fu);
+      uint32_t fp = 0u;  // entries of the flush units
+      int cnt = 0;
+      const int first_round = nu < S5_NS ? nu : S5_NS;
+      for (int q = first_round - 1; q >= 0 && q + S5_NS >= nu && cnt < nf; --q, ++cnt) fp |= 1u << q;
+      for (int q = nu - 1; q >= 0 && cnt < nf; --q)
+        if (!((fp >> q) & 1u)) {
+          fp |= 1u << q;
+          ++cnt;
+        }
+      const bool fl = ti < nu && ((fu >> ti) & 1u);
+      // k-th flush unit -> k-th flush entry; k-th other unit -> k-th other entry
+      const int k = __popc((fl ? fu : ~fu) & ((1u << ti) - 1u));
+      const uint32_t pool = fl ? fp : (~fp & ((1u << nu) - 1u));
+      int seen = -1;
+      for (int q = 0; q < 32 && seen < k; ++q)
+        if ((pool >> q) & 1u) {
+          ++seen;
+          at = q;
+        }
+      uint32_t* gw = reinterpret_cast<uint32_t*>(smem + lay.gwords);
+      if (ti < nu && !fl) gw[8 + k] = uint32_t(at);  // claimable entries, in order
+      if (lane == 0) {
+        gw[0] = uint32_t(nf);
+        gw[1] = 0u;  // next claimable entry (rank)
+      }
     }
     if (ti < nu) {
       table[at] = raw0 | (ti << 24);
@@ -1656,6 +1716,8 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
   if (warp > S5_NCW) {
     asm volatile("bar.arrive 2, %0;" ::"n"(32 * (1 + S5_NRW)) : "memory");
     asm volatile("bar.sync 1, %0;" ::"n"(32 * S5_NRW) : "memory");
+    // the chain warps of the third readout group read the table after their chains
+    if (claim) asm volatile("bar.arrive 10, %0;" ::"n"(32 * (S5_NRW + 4)) : "memory");
   } else if (warp == 0) {
     asm volatile("bar.sync 2, %0;" ::"n"(32 * (1 + S5_NRW)) : "memory");
   }
@@ -1706,9 +1768,6 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       // a stage's next load needs all readout warps to release it first.
       // Nothing here blocks: loads and readouts progress as stages free up and
       // chains finish.
-      s5_tc_after_sync();
-      const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + lay.tmem);
-      const uint32_t zb = smem_addr(smem + lay.zb);
       int nl = 0, nm = 0;
       const uint64_t t0 = globaltimer_ns();
       for (uint32_t it = 0; (nl < nu || nm < nu) && it < WAIT_LIMIT_ITERS; ++it) {
@@ -1718,25 +1777,16 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
           load_unit(nl++);
           progress = true;
         }
-        const int um = nm < nl ? s5_uidx(table[nm]) : 0;  // the entry's unit: chain warp um % S5_NCW
-        if (nm < nl && s5_test_wait(&full[nm % S5_NS], uint32_t((nm / S5_NS) & 1)) &&
-            s5_test_wait(&cbar[um % S5_NCW], uint32_t((um / S5_NCW) & 1))) {
-          const int su = nm % S5_NS, cu = table[nm];
-          if (!(FLUSH && s5_flush(cu)) && !s5_skip(cu)) {
-            const uint8_t* res = smem + lay.res0 + (um % S5_NCW) * lay.res_bytes;
-            const uint8_t* sbu = smem + lay.stage0 + su * lay.stage_bytes;
-            s5_tc_after_sync();
-#pragma unroll
-            for (int h = 0; h < 2; ++h)
-#pragma unroll
-              for (int ks = 0; ks < 4; ++ks) {
-                const uint32_t bs = smem_addr(res + lay.t8 + h * 1024) + 256 * ks;
-                s5_umma_e4m3(tmem + uint32_t(su * 32 + h * 16),
-                             s5_desc_sw128(smem_addr(sbu + lay.ck + h * 16384) + 32 * ks), s5_desc_cm(bs, 128, zb - bs),
-                             ks > 0 ? 1u : 0u);
-              }
+        // flush entries: their commit (no MMAs: it arrives at once, keeping mmab's
+        // phases one per entry) once their stage has landed; every other entry's
+        // MMAs and commit are issued by the readout group that takes it
+        // (tc_group_entry), several entries at a time
+        while (nm < nl) {
+          const int cu = table[nm];
+          if (FLUSH && s5_flush(cu)) {
+            if (!s5_test_wait(&full[nm % S5_NS], uint32_t((nm / S5_NS) & 1))) break;
+            s5_umma_commit(&mmab[nm % S5_NS]);
           }
-          s5_umma_commit(&mmab[su]);
           ++nm;
           progress = true;
         }
@@ -1763,6 +1813,142 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
     }
     return;
   }
+
+  // ---- tensor-memory readout of one entry that does not flush, by one warp of a
+  // readout group (4 warps, one per tensor-memory lane quarter qd = warp % 4): both
+  // heads of the rows 32 qd .. 32 qd + 31.  The scheduler thread has issued the
+  // entry's MMAs (five T terms per head into stage s's 32 columns: head h at
+  // 16 h); per row: the terms' weighted sum, V^T c over the ring slots, this
+  // token's own slot, K^-1/2, one store per head.  The group owes the unit's 8
+  // stage and chain-result arrivals: 2 per warp.
+  auto tc_group_entry = [&](int i, int code) {
+    const int s = i % S5_NS;
+    const uint32_t par = (i / S5_NS) & 1;
+    const int ui = s5_uidx(code);
+    const int ccw = ui % S5_NCW, k = ui / S5_NCW;
+    const int qd = warp & 3, row = 32 * qd + lane;
+    const S5Unit U = s5_unit<SIDX>(bid + ui * grid, p, G, geo);
+    const bool skip = s5_skip(code);
+    // this quarter's vblock scale of both heads, issued before the waits
+    uint32_t scr[2] = {0u, 0u};
+    if (!skip) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+        scr[h] = s5_ld_raw(p.sc, int64_t(U.s) * p.sc_sb + int64_t(U.hv0 + h) * p.sc_sh + int64_t(qd) * p.sc_sv,
+                           p.sc_dt);
+    }
+    bool ok = s5_warp_wait(&full[s], par, p.err, abort, lane);
+    ok = s5_warp_wait(&cbar[ccw], uint32_t(k & 1), p.err, abort, lane) && ok;
+    const bool mma = ok && !skip;
+    const uint8_t* sb = smem + lay.stage0 + s * lay.stage_bytes;
+    const uint8_t* res = smem + lay.res0 + ccw * lay.res_bytes;
+    // the group's first thread issues the entry's readout on the tensor cores -- per
+    // head 4 x tcgen05.mma (M = 128 rows, N = 16: the five T terms and zeros, K =
+    // 32) from the stage tile and the chain's T operand into the stage's 32 columns
+    // -- and its commit (one per entry, also without MMAs, so that mmab[s]
+    // completes one phase per entry of the stage)
+    const bool leader = (warp & 3) == 0 && lane == 0;
+    if (leader) {
+      if (mma) {
+        s5_tc_after_sync();
+        const uint32_t tm = *reinterpret_cast<volatile uint32_t*>(smem + lay.tmem);
+        const uint32_t zb = smem_addr(smem + lay.zb);
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            const uint32_t bs = smem_addr(res + lay.t8 + h * 1024) + 256 * ks;
+            s5_umma_e4m3(tm + uint32_t(s * 32 + h * 16), s5_desc_sw128(smem_addr(sb + lay.ck + h * 16384) + 32 * ks),
+                         s5_desc_cm(bs, 128, zb - bs), ks > 0 ? 1u : 0u);
+          }
+      }
+      s5_umma_commit(&mmab[s]);
+    }
+    float ov[2] = {0.0f, 0.0f};
+    if (mma) {
+      // V^T c: all 16 slots loaded unconditionally (the region is always
+      // allocated), the slots >= nmem (stale or unloaded data) selected away
+      const int nmem = s5_nmem(code);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint8_t* vr = sb + lay.vr + h * 4096;
+        const float4* cf = reinterpret_cast<const float4*>(res + lay.cf) + h * 4;
+        uint16_t vraw[16];
+#pragma unroll
+        for (int t = 0; t < 16; ++t) vraw[t] = *reinterpret_cast<const uint16_t*>(vr + s5_ring_off(t, row));
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 c4 = cf[q];
+          const float cq[4] = {c4.x, c4.y, c4.z, c4.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int t = 4 * q + j;
+            ov[h] = fmaf(cq[j], t < nmem ? bf16_to_f(vraw[t]) : 0.0f, ov[h]);
+          }
+        }
+        if constexpr (FUSED) {
+          const float* misc = reinterpret_cast<const float*>(res + lay.misc) + h * 4;
+          ov[h] = fmaf(misc[1], bf16_to_f(reinterpret_cast<const uint16_t*>(res + lay.vnew + h * 256)[row]), ov[h]);
+        }
+      }
+    }
+    const bool mok = s5_warp_wait(&mmab[s], par, p.err, abort, lane);
+    // abort: the MMAs this thread issued finish before the tensor memory is released
+    if (!mok && leader) s5_drain_wait(&mmab[s], par);
+    float o[2] = {0.0f, 0.0f};
+    if (mma) {
+      s5_tc_after_sync();
+      const uint32_t tm = *reinterpret_cast<volatile uint32_t*>(smem + lay.tmem);
+      uint32_t d[32];
+      s5_tmem_ld32(tm + (uint32_t(32 * qd) << 16) + uint32_t(s * 32), d);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const float* misc = reinterpret_cast<const float*>(res + lay.misc) + h * 4;
+        float ot = __uint_as_float(d[16 * h + 4]) * (1.0f / 16.0f);
+        ot = (ot + __uint_as_float(d[16 * h + 3])) * (1.0f / 16.0f);
+        ot = (ot + __uint_as_float(d[16 * h + 2])) * (1.0f / 16.0f);
+        ot = (ot + __uint_as_float(d[16 * h + 1])) * (1.0f / 16.0f);
+        ot = ot + __uint_as_float(d[16 * h]);
+        o[h] = mok ? fmaf(ot, misc[0] * s5_cvt(scr[h], p.sc_dt), ov[h]) : 0.0f;
+      }
+    }
+    // release the stage and the chain's results before the output stores: every
+    // read of them has been consumed, so relaxed releases suffice after an MMA
+    s5_tc_before_sync();
+    __syncwarp();
+    if (lane == 0) {
+      if (mma) {
+        s5_arrive_relaxed_n(&empty[s], 2u);
+        s5_arrive_relaxed_n(&rbar[ccw], 2u);
+      } else {
+        s5_arrive_n(&empty[s], 2u);
+        s5_arrive_n(&rbar[ccw], 2u);
+      }
+    }
+    if (mma) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+        store_scalar(p.out, int64_t(U.b) * p.o_sb + int64_t(U.hv0 + h) * p.o_sh + int64_t(row) * p.o_sv, p.o_dt,
+                     o[h] * KSCALE_H);
+    }
+  };
+  // Claim mode: the group's first warp claims the next entry after the flush
+  // entries (a shared counter), the group syncs on a named barrier of its own and
+  // reads the claim (double-buffered, so that a claim is never overwritten before
+  // the whole group has read it); a claim past the last entry ends the loop.
+  auto tc_claim_loop = [&](int grp) {
+    uint32_t* gw = reinterpret_cast<uint32_t*>(smem + lay.gwords);
+    const int ncl = nu - int(gw[0]);
+    for (int round = 0;; ++round) {
+      volatile uint32_t* slot = gw + 2 + 2 * grp + (round & 1);
+      if ((warp & 3) == 0 && lane == 0) *slot = atomicAdd(&gw[1], 1u);
+      asm volatile("bar.sync %0, %1;" ::"r"(12 + grp), "n"(128) : "memory");
+      const int r = int(*slot);
+      if (r >= ncl) break;
+      const int i = int(gw[8 + r]);
+      tc_group_entry(i, table[i]);
+    }
+  };
 
   if (chain_warp) {
     // =================== chain warps ===================
@@ -1803,99 +1989,60 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       if (lane == 0) s5_arrive(&cbar[cw]);
       if (work) s5_append<FUSED, HPU>(p, U, code, ap, lane);
     }
+    if constexpr (TC) {
+      // claim mode: chain warps 1..4 (lane quarters 1, 2, 3, 0) are readout group 2
+      if (claim && warp <= 4) {
+        asm volatile("bar.sync 10, %0;" ::"n"(32 * (S5_NRW + 4)) : "memory");
+        s5_tc_after_sync();
+        tc_claim_loop(2);
+        s5_tc_before_sync();
+        asm volatile("bar.sync 11, %0;" ::"n"(32 * (S5_NRW + 4)) : "memory");
+      }
+    }
     return;
   }
 
   if constexpr (TC) {
     // =================== readout through tensor memory ===================
-    // Every unit is read out by all S5_NRW warps; warp w takes head head_r and the
-    // 32 rows 32 (w % 4) .. of it (the tensor-memory lanes a warp may access).  The
-    // scheduler thread (producer) has issued the unit's MMAs; per lane and row:
-    // the five terms' weighted sum, V^T c over the ring slots, this token's own
-    // slot, K^-1/2, one store.  Every unit's commit is waited for (also of flush
-    // and skipped units, which have none to read) so that the waits stay in step
-    // with mmab's phases.
+    // Flush entries are read out by all S5_NRW readout warps, one vblock task each
+    // (warp w: head w / 4, rows 32 (w % 4) ..); the other entries by readout groups
+    // of 4 warps, one per tensor-memory lane quarter, both heads (tc_group_entry):
+    // group 0 = readout warps 0..3, group 1 = 4..7, and in claim mode group 2 =
+    // chain warps 1..4 once their chains are done.  Claim mode (flush entries
+    // first): after the flush entries, the groups claim the remaining entries in
+    // order, so that a group that is free takes the next one.  Otherwise groups 0
+    // and 1 alternate over the non-flush entries in order.
     s5_tc_after_sync();
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + lay.tmem);
-    const int qd = warp & 3, row = 32 * qd + lane;
+    const int qd = warp & 3;
     // this warp's flush stash: its lane quarter, 128 columns (two warps share a quarter)
     const uint32_t stash = tmem + (uint32_t(32 * qd) << 16) + S5_TM_STASH + 128u * uint32_t(rw >> 2);
     float* ost = reinterpret_cast<float*>(smem + lay.ost0 + rw * 512);
-    for (int i = 0; i < nu; ++i) {
+    auto flush_entry = [&](int i) {
       const int s = i % S5_NS;
       const uint32_t par = (i / S5_NS) & 1;
       const int code = table[i];
-      const int ui = s5_uidx(code);  // the unit of entry i (flush units may come first)
+      const int ui = s5_uidx(code);
       const int ccw = ui % S5_NCW, k = ui / S5_NCW;
-      const float sc_pref = s5_cvt(__shfl_sync(0xffffffffu, scl_raw, ui & 31), p.sc_dt);
       bool ok = s5_warp_wait(&full[s], par, p.err, abort, lane);
       ok = s5_warp_wait(&cbar[ccw], uint32_t(k & 1), p.err, abort, lane) && ok;
-      const bool flush = FLUSH && s5_flush(code);
       uint8_t* sb = smem + lay.stage0 + s * lay.stage_bytes;
       const S5Unit U = s5_unit<SIDX>(bid + ui * grid, p, G, geo);
-      const bool mma = ok && !flush && !s5_skip(code);
-      const uint8_t* res = smem + lay.res0 + ccw * lay.res_bytes;
-      // V^T c over the slots read from memory (no tensor memory needed yet)
-      float ov = 0.0f;
-      if (mma) {
-        const float* cf = reinterpret_cast<const float*>(res + lay.cf) + head_r * 16;
-        const uint8_t* vr = sb + lay.vr + head_r * 4096;
-        const int nmem = s5_nmem(code);
-        float vt[16];
-#pragma unroll
-        for (int t = 0; t < 16; ++t)  // slots >= nmem hold stale or unloaded data
-          vt[t] = t < nmem ? bf16_to_f(*reinterpret_cast<const uint16_t*>(vr + s5_ring_off(t, row))) : 0.0f;
-#pragma unroll
-        for (int t = 0; t < 16; ++t) ov = fmaf(cf[t], vt[t], ov);
-        if constexpr (FUSED) {
-          const float* misc = reinterpret_cast<const float*>(res + lay.misc) + head_r * 4;
-          ov = fmaf(misc[1], bf16_to_f(reinterpret_cast<const uint16_t*>(res + lay.vnew + head_r * 256)[row]), ov);
-        }
+      s5_warp_wait(&mmab[s], par, p.err, abort, lane);  // keeps the commits in step (none issued for it)
+      // The unit's 4 x 2 vblock tasks, one per readout warp (task rw), then one
+      // tensor-map store by the warp whose acquire-release increment of the unit's
+      // done count completes it (the other tasks' released rows are visible to
+      // it); the others release the stage now (it is reloaded only after all have).
+      static_assert(4 * HPU == S5_NRW, "one flush task per readout warp");
+      int last = 0;
+      if (ok) {
+        s5_flush_task<FUSED, HPU>(p, smem, lay, U, s, ccw, code, rw, ost, stash, lane);
+        if (lane == 0 && s5_add_acq_rel(&tdone[i], 1u) == uint32_t(S5_NRW - 1)) last = 1;
       }
-      const bool mok = s5_warp_wait(&mmab[s], par, p.err, abort, lane);
-      if (flush) {
-        // The unit's 4 x 2 vblock tasks, one per readout warp (task rw), then
-        // one tensor-map store by the warp whose acquire-release increment of
-        // the unit's done count completes it (the other tasks' released rows
-        // are visible to it); the others release the stage now (it is reloaded
-        // only after all have).
-        static_assert(4 * HPU == S5_NRW, "one flush task per readout warp");
-        int last = 0;
-        if (ok) {
-          s5_flush_task<FUSED, HPU>(p, smem, lay, U, s, ccw, code, rw, ost, stash, lane);
-          if (lane == 0 && s5_add_acq_rel(&tdone[i], 1u) == uint32_t(S5_NRW - 1)) last = 1;
-        }
-        if (__shfl_sync(0xffffffffu, last, 0) && lane == 0 && *abort == 0) {
-          s5_tma_store4(&ck_map, sb + lay.ck, 0, 0, U.hv0, U.s);
-          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-          asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-        }
-      } else if (mma) {
-        float sc = sc_pref;
-        if (ui >= 32)
-          sc = load_scalar(p.sc, int64_t(U.s) * p.sc_sb + int64_t(U.hv0 + head_r) * p.sc_sh + int64_t(qd) * p.sc_sv,
-                           p.sc_dt);
-        const float* misc = reinterpret_cast<const float*>(res + lay.misc) + head_r * 4;
-        s5_tc_after_sync();
-        uint32_t d[16];
-        s5_tmem_ld16(tmem + (uint32_t(32 * qd) << 16) + uint32_t(s * 32 + head_r * 16), d);
-        float ot = __uint_as_float(d[4]) * (1.0f / 16.0f);
-        ot = (ot + __uint_as_float(d[3])) * (1.0f / 16.0f);
-        ot = (ot + __uint_as_float(d[2])) * (1.0f / 16.0f);
-        ot = (ot + __uint_as_float(d[1])) * (1.0f / 16.0f);
-        ot = ot + __uint_as_float(d[0]);
-        const float o = mok ? fmaf(ot, misc[0] * sc, ov) : 0.0f;
-        // release the stage and the chain's results before the output store: every
-        // read of them has been consumed, so relaxed releases suffice
-        s5_tc_before_sync();
-        __syncwarp();
-        if (lane == 0) {
-          s5_arrive_relaxed(&empty[s]);
-          s5_arrive_relaxed(&rbar[ccw]);
-        }
-        store_scalar(p.out, int64_t(U.b) * p.o_sb + int64_t(U.hv0 + head_r) * p.o_sh + int64_t(row) * p.o_sv, p.o_dt,
-                     o * KSCALE_H);
-        continue;
+      if (__shfl_sync(0xffffffffu, last, 0) && lane == 0 && *abort == 0) {
+        s5_tma_store4(&ck_map, sb + lay.ck, 0, 0, U.hv0, U.s);
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
       }
       s5_tc_before_sync();
       __syncwarp();
@@ -1903,14 +2050,34 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
         s5_arrive(&empty[s]);
         s5_arrive(&rbar[ccw]);
       }
+    };
+    const int g = rw >> 2;
+    if (claim) {
+      for (int i = 0; i < nu; ++i)
+        if (FLUSH && s5_flush(table[i])) flush_entry(i);
+      tc_claim_loop(g);
+    } else {
+      int rank = 0;
+      for (int i = 0; i < nu; ++i) {
+        const int code = table[i];
+        if (FLUSH && s5_flush(code)) {
+          flush_entry(i);
+        } else {
+          if ((rank & 1) == g) tc_group_entry(i, code);
+          ++rank;
+        }
+      }
     }
     // the last commit covers every MMA this CTA issued: complete before the
-    // tensor memory is released
+    // tensor memory is released (and the third group is done with it)
     if (rw == 0 && nu > 0 &&
         !s5_warp_wait(&mmab[(nu - 1) % S5_NS], uint32_t(((nu - 1) / S5_NS) & 1), p.err, abort, lane) && lane == 0)
       s5_drain_mma(mmab, reinterpret_cast<const uint32_t*>(smem + lay.tmem) + 1);
     s5_tc_before_sync();
-    asm volatile("bar.sync 1, %0;" ::"n"(32 * S5_NRW) : "memory");
+    if (claim)
+      asm volatile("bar.sync 11, %0;" ::"n"(32 * (S5_NRW + 4)) : "memory");
+    else
+      asm volatile("bar.sync 1, %0;" ::"n"(32 * S5_NRW) : "memory");
     if (rw == 0) {
       s5_tc_after_sync();
       asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(S5_TMEM_COLS) : "memory");
