@@ -20,10 +20,11 @@
 //    form) -- for both heads of the unit at once.  A unit's chain needs only
 //    its key ring (4 KB, loaded by the chain warp's own TMA), so all chains of
 //    the SM run while the checkpoints are still streaming in.
-//  * readout team (S5_NRW warps): consumes the stages in order; each warp
-//    reads out 32 * hpu / 2 rows of the unit on tensor cores: S_fp8 . T as an
-//    e4m3 MMA against T split into five e4m3 terms, V^T c as a bf16 MMA into
-//    the spare accumulator columns, plus this token's value row (rank one).
+//  * readout (S5_NRW warps): consumes the stages in order; in the variant
+//    without the flush path each warp reads out one 32-row vblock of every unit
+//    (both heads of a unit at once) on tensor cores: S_fp8 . T as an e4m3 MMA
+//    against T split into five e4m3 terms, V^T c as a bf16 MMA into the spare
+//    accumulator columns, plus this token's value row (rank one).
 //
 // Units whose ring is full (flush) take the same stages: their chain warp
 // hands the decayed Gram matrix and gates to the readout team, whose warps
@@ -56,9 +57,19 @@ template <int HPU, bool FLUSH>
 __host__ __device__ constexpr bool s5_tc() {
   return HPU == 2 && FLUSH;
 }
+// Readout of the variant without the flush path ("vblock readout"): every
+// readout warp takes one 32-row vblock of a unit (warp w: head w / 4, rows
+// 32 (w % 4) ..), so that a unit is read out by 4 x hpu warps at once (one-head
+// units: two groups of 4 warps alternate over the units) and stages free up
+// one unit at a time.  The team readout (S5_TEAM warps per stage, four units
+// at a time) stays for the flush-capable variant with one-head units.
+template <bool FLUSH>
+__host__ __device__ constexpr bool s5_vb() {
+  return !FLUSH;
+}
 template <int HPU, bool FLUSH>
 __host__ __device__ constexpr int s5_rpu() {  // readout warps per unit
-  return s5_tc<HPU, FLUSH>() ? S5_NRW : S5_TEAM;
+  return s5_tc<HPU, FLUSH>() ? S5_NRW : (s5_vb<FLUSH>() ? 4 * HPU : S5_TEAM);
 }
 // Tensor memory of the tensor-memory readout: columns 0..127 the readout's
 // accumulators (stages x heads x 16); from S5_TM_STASH, 128 columns per readout
@@ -1599,20 +1610,27 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
     asm volatile("bar.sync 3, %0;" ::"n"(32 * (1 + S5_NCW)) : "memory");
   }
   // readout warps: vblock scales of their first units, raw until used.
-  // Two-head units (every readout warp reads every unit): lane l holds unit l's
-  // scale of the warp's head and vblock.  One-head units (teams): lane l holds
-  // team unit l / (2 HPU), vblock l % (2 HPU) of the warp's rows.
+  // Vblock readout: lane l holds unit l's scale of the warp's head and vblock.
+  // One-head units (teams): lane l holds team unit l / (2 HPU), vblock l % (2 HPU)
+  // of the warp's rows.
+  constexpr bool VB = s5_vb<FLUSH>();
   constexpr int VBW = 2 * HPU;  // vblocks per readout warp and unit (teams)
-  constexpr int SC_UNITS = 32 / VBW;  // team readout: units with a prefetched scale
+  constexpr int SC_UNITS = VB ? 32 : 32 / VBW;  // units with a prefetched scale
   uint32_t scl_raw = 0u;
   const int rw = warp - 1 - S5_NCW;
   const int team = rw / S5_TEAM, mem = rw % S5_TEAM;
-  const int head_r = TC ? (rw >> 2) : (HPU == 2 ? mem : 0);
-  const int rbase = HPU == 2 ? 0 : 64 * mem;
+  const int head_r = (TC || VB) ? (HPU == 2 ? (rw >> 2) : 0) : (HPU == 2 ? mem : 0);
+  const int rbase = VB ? 32 * (rw & 3) : (HPU == 2 ? 0 : 64 * mem);
   if (warp > S5_NCW) {
     if constexpr (TC) {  // the zero rows of the tensor-core T operands
       reinterpret_cast<uint32_t*>(smem + lay.zb)[tid - 32 * (1 + S5_NCW)] = 0u;
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    } else if constexpr (VB) {
+      const int i = lane < nu ? lane : 0;
+      const S5Unit U = s5_unit<SIDX>(bid + i * grid, p, G, geo);
+      scl_raw = s5_ld_raw(p.sc, int64_t(U.s < 0 ? 0 : U.s) * p.sc_sb + int64_t(U.hv0 + head_r) * p.sc_sh +
+                                    int64_t(rw & 3) * p.sc_sv,
+                          p.sc_dt);
     } else {
       int i = team + S5_NS * (lane / VBW);
       i = i < nu ? i : 0;
@@ -2082,6 +2100,65 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       s5_tc_after_sync();
       asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(S5_TMEM_COLS) : "memory");
     }
+  } else if constexpr (VB) {
+  // =================== vblock readout ===================
+  // Warp w reads out rows 32 (w % 4) .. of head w / 4 of every unit (two-head
+  // units), or of every other unit (one-head units: group w / 4 takes the units
+  // i = w / 4 (mod 2)); the unit's 4 x hpu warps release its stage and chain
+  // results as they finish.
+  constexpr int NG = S5_NRW / (4 * HPU);  // readout groups
+  float* ost = reinterpret_cast<float*>(smem + lay.ost0 + rw * 512);
+  const float sc_pre = s5_cvt(scl_raw, p.sc_dt);
+  for (int i = NG == 1 ? 0 : (rw >> 2); i < nu; i += NG) {
+    const int s = i % S5_NS;
+    const int ccw = i % S5_NCW, k = i / S5_NCW;
+    const int code = table[i];
+    float sc = sc_pre;
+    int sc_base = i;
+    if (i >= SC_UNITS) {  // beyond the prefetched units
+      sc = 1.0f;
+      sc_base = 0;
+      if (!s5_skip(code)) {
+        const S5Unit U = s5_unit<SIDX>(bid + i * grid, p, G, geo);
+        sc = load_scalar(p.sc, int64_t(U.s) * p.sc_sb + int64_t(U.hv0 + head_r) * p.sc_sh + int64_t(rw & 3) * p.sc_sv,
+                         p.sc_dt);
+      }
+    }
+    bool ok = s5_warp_wait(&full[s], (i / S5_NS) & 1, p.err, abort, lane);
+    ok = s5_warp_wait(&cbar[ccw], uint32_t(k & 1), p.err, abort, lane) && ok;
+    uint8_t* sb = smem + lay.stage0 + s * lay.stage_bytes;
+    if (ok && !s5_skip(code)) {
+      const S5Unit U = s5_unit<SIDX>(bid + i * grid, p, G, geo);
+      const uint8_t* res = smem + lay.res0 + ccw * lay.res_bytes;
+      const float* misc = reinterpret_cast<const float*>(res + lay.misc) + head_r * 4;
+      s5_readout<2, I8>(sb + lay.ck + head_r * 16384, sb + lay.vr + head_r * 4096, res + lay.t8 + head_r * 8 * T8STR,
+                        reinterpret_cast<const uint16_t*>(res + lay.cb + head_r * 96), misc[0], sc, sc_base, rbase,
+                        s5_nmem(code), ost, lane);
+      __syncwarp();
+      // this token's own slot (fused) as a rank-one term, K^-1/2, one row per lane
+      float o = ost[lane];
+      if (FUSED) {
+        const uint16_t* vnew = reinterpret_cast<const uint16_t*>(res + lay.vnew + head_r * 256) + rbase;
+        o = fmaf(misc[1], bf16_to_f(vnew[lane]), o);
+      }
+      __syncwarp();
+      // every read of the stage and the chain's results has returned its value (all
+      // of them feed o, which every lane holds after the warp barrier): relaxed
+      // arrivals suffice
+      if (lane == 0) {
+        s5_arrive_relaxed(&empty[s]);
+        s5_arrive_relaxed(&rbar[ccw]);
+      }
+      store_scalar(p.out, int64_t(U.b) * p.o_sb + int64_t(U.hv0 + head_r) * p.o_sh + int64_t(rbase + lane) * p.o_sv,
+                   p.o_dt, o * KSCALE_H);
+    } else {
+      __syncwarp();
+      if (lane == 0) {
+        s5_arrive(&empty[s]);
+        s5_arrive(&rbar[ccw]);
+      }
+    }
+  }
   } else {
   // =================== readout teams ===================
   // Team j (2 warps) reads out the units of stage j in order; with two heads
