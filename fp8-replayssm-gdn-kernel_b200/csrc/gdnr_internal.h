@@ -78,6 +78,9 @@ struct StepParams {
   // the checkpoint holds int8 codes ("vblock_int8"); launched on the
   // one-CTA-per-head kernel (gdnr_step2.cu) only
   int32_t ck_i8;
+  // persistent step without the flush path: the gate rings are read by TMA
+  // (set by its launcher when their layout allows)
+  int32_t gtma;
 };
 
 struct SmemLayout {

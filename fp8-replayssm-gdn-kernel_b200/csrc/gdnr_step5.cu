@@ -119,6 +119,7 @@ struct S5Layout {
   uint32_t res0, res_bytes, t8, cb, cf, misc, vnew;
   uint32_t qb, gram;  // chain scratch inside res (aliases t8)
   uint32_t ost0, zb;
+  uint32_t gbuf0;  // variant without the flush path: per chain warp, its unit's gate rings (g, beta; 256 B each)
   uint32_t total;
 };
 
@@ -166,6 +167,7 @@ __host__ __device__ inline S5Layout s5_layout(const S5Geo& g, int max_units, boo
   s.ost0 = o;
   o += S5_NRW * 512u;
   s.zb = smem_take(o, 1024u);  // zeros: rows 8..15 of every T operand (N = 16)
+  s.gbuf0 = smem_take(o, flush ? 0u : S5_NCW * 512u);
   s.total = o;
   return s;
 }
@@ -221,6 +223,18 @@ __device__ __forceinline__ void s5_tma4(void* dst, const CUtensorMap* map, int c
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_addr(bar))
       : "memory");
 }
+
+__device__ __forceinline__ void s5_tma3(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// Heads per 16-byte row of a gate-ring tensor-map box (the box starts at a
+// multiple of it, the TMA alignment rule for the innermost coordinate)
+__device__ __forceinline__ int s5_gate_hb(int dtype) { return dtype == GDNR_F32 ? 4 : 8; }
 
 __device__ __forceinline__ void s5_tma5(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3, int c4,
                                         uint64_t* bar) {
@@ -629,8 +643,12 @@ __device__ __forceinline__ S5In s5_fetch(const StepParams& p, const S5Unit& U, i
   // a null or bad slot (U.s < 0, packed decode) reads slot 0's gates and scales:
   // the unit is skipped, the values are never used, and no load leaves the tensors
   const int64_t sl = U.s < 0 ? 0 : U.s;
-  in.g = s5_ld_raw(p.gr, sl * p.gr_sb + int64_t(ts) * p.gr_st + int64_t(hv) * p.gr_sh, p.gr_dt);
-  in.beta = s5_ld_raw(p.br, sl * p.br_sb + int64_t(ts) * p.br_st + int64_t(hv) * p.br_sh, p.br_dt);
+  if (!FLUSH && p.gtma) {  // in shared memory (gate-ring TMA with the key ring)
+    in.g = in.beta = 0u;
+  } else {
+    in.g = s5_ld_raw(p.gr, sl * p.gr_sb + int64_t(ts) * p.gr_st + int64_t(hv) * p.gr_sh, p.gr_dt);
+    in.beta = s5_ld_raw(p.br, sl * p.br_sb + int64_t(ts) * p.br_st + int64_t(hv) * p.br_sh, p.br_dt);
+  }
   in.scr = FLUSH ? s5_ld_raw(p.sc, sl * p.sc_sb + int64_t(hv) * p.sc_sh + int64_t(t & 3) * p.sc_sv, p.sc_dt)
                  : 0u;
   if constexpr (FUSED) {
@@ -758,7 +776,8 @@ __device__ __forceinline__ void s5_tloop(const uint8_t* kbuf, float wj, int n, f
 // (swizzled, slots < nmem loaded); res: this warp's result block.
 template <bool FUSED, int HPU, bool FLUSH, bool I8 = false>
 __device__ __forceinline__ S5Append s5_chain(const StepParams& p, const S5Unit& U, int code, const S5In& in,
-                                             uint8_t* kbuf, uint8_t* res, const S5Layout& lay, int lane) {
+                                             uint8_t* kbuf, const uint8_t* gbuf, uint8_t* res, const S5Layout& lay,
+                                             int lane) {
   S5Append ap{};
   const int g8 = lane >> 2, t4 = lane & 3;
   const int e = lane >> 4, t = lane & 15;
@@ -766,7 +785,19 @@ __device__ __forceinline__ S5Append s5_chain(const StepParams& p, const S5Unit& 
   uint16_t* qb = reinterpret_cast<uint16_t*>(res + lay.t8 + lay.qb);
   float* gram = reinterpret_cast<float*>(res + lay.t8 + lay.gram);
   float* misc = reinterpret_cast<float*>(res + lay.misc);
-  float g_own = s5_cvt(in.g, p.gr_dt), beta_own = s5_cvt(in.beta, p.br_dt);  // gates of (head e, slot t)
+  uint32_t graw = in.g, braw = in.beta;
+  if (!FLUSH && p.gtma) {
+    // the gate-ring boxes: slot-major rows of 16 bytes, heads from hv0 rounded down
+    const int ts = t < p.L ? t : p.L - 1;
+    const int hv = U.hv0 + (e < HPU ? e : 0);
+    const int ig = ts * s5_gate_hb(p.gr_dt) + (hv & (s5_gate_hb(p.gr_dt) - 1));
+    const int ib = ts * s5_gate_hb(p.br_dt) + (hv & (s5_gate_hb(p.br_dt) - 1));
+    graw = p.gr_dt == GDNR_F32 ? reinterpret_cast<const uint32_t*>(gbuf)[ig]
+                               : uint32_t(reinterpret_cast<const uint16_t*>(gbuf)[ig]);
+    braw = p.br_dt == GDNR_F32 ? reinterpret_cast<const uint32_t*>(gbuf + 256)[ib]
+                               : uint32_t(reinterpret_cast<const uint16_t*>(gbuf + 256)[ib]);
+  }
+  float g_own = s5_cvt(graw, p.gr_dt), beta_own = s5_cvt(braw, p.br_dt);  // gates of (head e, slot t)
   float qv[4];
   if constexpr (FUSED) {
     const int pos = nmem;
@@ -1502,7 +1533,8 @@ __device__ __forceinline__ void s5_flush_task(const StepParams& p, uint8_t* smem
 template <bool FUSED, int HPU, bool FLUSH, bool SIDX, bool I8 = false>
 __global__ void __launch_bounds__(S5_THREADS, 1)
     step5_kernel(const __grid_constant__ StepParams p, const __grid_constant__ CUtensorMap ck_map,
-                 const __grid_constant__ CUtensorMap kr_map, const __grid_constant__ CUtensorMap vr_map) {
+                 const __grid_constant__ CUtensorMap kr_map, const __grid_constant__ CUtensorMap vr_map,
+                 const __grid_constant__ CUtensorMap gr_map, const __grid_constant__ CUtensorMap br_map) {
   static_assert(!(I8 && (FLUSH || SIDX)), "int8 checkpoints: the non-flush, slot-free variant only");
   extern __shared__ __align__(1024) uint8_t smem[];
   constexpr bool TC = s5_tc<HPU, FLUSH>();
@@ -1592,14 +1624,23 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
   const bool chain_warp = warp >= 1 && warp <= S5_NCW;
   const int nreq_k = (L + geo.rb - 1) / geo.rb;
   uint8_t* kbuf = smem + lay.kbuf0 + (chain_warp ? cw : 0) * 4096;
+  uint8_t* gbuf = smem + lay.gbuf0 + (chain_warp ? cw : 0) * 512;
+  // gate rings of unit U with its key ring (variant without the flush path)
+  const bool gtma = !FLUSH && p.gtma;
+  const uint32_t gate_bytes = gtma ? 2u * 16u * uint32_t(L) : 0u;
+  auto issue_gates = [&](const S5Unit& U) {
+    s5_tma3(gbuf, &gr_map, U.hv0 & ~(s5_gate_hb(p.gr_dt) - 1), 0, U.s, &kfull[cw]);
+    s5_tma3(gbuf + 256, &br_map, U.hv0 & ~(s5_gate_hb(p.br_dt) - 1), 0, U.s, &kfull[cw]);
+  };
   S5In in0;
   if (chain_warp) {
     const int i0 = cw < nu ? cw : 0;
     const S5Unit U = s5_unit<SIDX>(bid + i0 * grid, p, G, geo);
     if (lane == 0) {
       const int nr = cw < nu && U.s >= 0 ? nreq_k : 0;
-      mbar_arrive_expect_tx(&kfull[cw], uint32_t(nr) * box_bytes);
+      mbar_arrive_expect_tx(&kfull[cw], uint32_t(nr) * box_bytes + (nr > 0 ? gate_bytes : 0u));
       for (int j = 0; j < nr; ++j) s5_tma5(kbuf + j * box_bytes, &kr_map, 0, 0, U.h, j * geo.rb, U.s, &kfull[cw]);
+      if (gtma && nr > 0) issue_gates(U);
     }
     in0 = s5_fetch<FUSED, HPU, FLUSH>(p, U, lane);
     // the key rings and these loads go out first; the producer starts the
@@ -1985,9 +2026,10 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
         __syncwarp();
         if (lane == 0) {
           const int nr = U.s >= 0 ? nreq_k : 0;
-          mbar_arrive_expect_tx(&kfull[cw], uint32_t(nr) * box_bytes);
+          mbar_arrive_expect_tx(&kfull[cw], uint32_t(nr) * box_bytes + (nr > 0 ? gate_bytes : 0u));
           for (int j = 0; j < nr; ++j)
             s5_tma5(kbuf + j * box_bytes, &kr_map, 0, 0, U.h, j * geo.rb, U.s, &kfull[cw]);
+          if (gtma && nr > 0) issue_gates(U);
         }
         in0 = s5_fetch<FUSED, HPU, FLUSH>(p, U, lane);
       }
@@ -2000,7 +2042,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       const int code = s5_code<FUSED>(in0.pos, in0.flag, L, FLUSH);
       const bool work = ok && !s5_skip(code);
       S5Append ap{};
-      if (work) ap = s5_chain<FUSED, HPU, FLUSH, I8>(p, U, code, in0, kbuf, res, lay, lane);
+      if (work) ap = s5_chain<FUSED, HPU, FLUSH, I8>(p, U, code, in0, kbuf, gbuf, res, lay, lane);
       // the T operand is read by the tensor cores (async proxy)
       if (TC) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
@@ -2335,7 +2377,8 @@ static S5EncodeFn s5_encode_fn() {
 
 template <bool FUSED, int HPU, bool FLUSH, bool SIDX = false, bool I8 = false>
 static cudaError_t s5_launch(const StepParams& p, const CUtensorMap& ck, const CUtensorMap& kr,
-                             const CUtensorMap& vr, int grid, uint32_t smem, bool pdl, cudaStream_t stream) {
+                             const CUtensorMap& vr, const CUtensorMap& gm, const CUtensorMap& bm, int grid,
+                             uint32_t smem, bool pdl, cudaStream_t stream) {
   auto kern = step5_kernel<FUSED, HPU, FLUSH, SIDX, I8>;
   static DynSmemCache smem_cache;  // per device: dynamic smem already allowed for this instance
   cudaError_t e = ensure_dyn_smem(reinterpret_cast<const void*>(kern), int(smem), smem_cache);
@@ -2350,7 +2393,7 @@ static cudaError_t s5_launch(const StepParams& p, const CUtensorMap& ck, const C
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, kern, p, ck, kr, vr);
+  return cudaLaunchKernelEx(&cfg, kern, p, ck, kr, vr, gm, bm);
 }
 
 cudaError_t launch_step5(const StepParams& p, bool fused, bool pdl, cudaStream_t stream) {
@@ -2385,6 +2428,30 @@ cudaError_t launch_step5(const StepParams& p, bool fused, bool pdl, cudaStream_t
   };
   if (ring_map(&kr, p.kr, p.H, p.kr_sh, p.kr_st, p.kr_sb) != CUDA_SUCCESS) return cudaErrorInvalidValue;
   if (ring_map(&vr, p.vr, p.HV, p.vr_sh, p.vr_st, p.vr_sb) != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  // gate rings [slots][L][HV] (heads contiguous) for the variant without the flush
+  // path: a box of 16 bytes of heads x L slots per ring, read by TMA with the key ring
+  StepParams q = p;
+  CUtensorMap gm, bm;
+  memset(&gm, 0, sizeof(gm));
+  memset(&bm, 0, sizeof(bm));
+  q.gtma = 0;
+  if (p.flush_hint == GDNR_FLUSH_NONE) {
+    auto gate_map = [&](CUtensorMap* m, void* base, int dt, int64_t s_slot, int64_t s_b, int64_t s_head) {
+      const int esz = dt == GDNR_F32 ? 4 : 2, hb = 16 / esz;
+      if (s_head != 1 || p.HV < hb || reinterpret_cast<uintptr_t>(base) % 16 || (s_slot * esz) % 16 ||
+          (s_b * esz) % 16)
+        return false;
+      const cuuint64_t dims[3] = {cuuint64_t(p.HV), cuuint64_t(p.L), cuuint64_t(nst)};
+      const cuuint64_t strides[2] = {cuuint64_t(s_slot * esz), cuuint64_t(s_b * esz)};
+      const cuuint32_t box[3] = {cuuint32_t(hb), cuuint32_t(p.L), 1};
+      const cuuint32_t es[3] = {1, 1, 1};
+      return enc(m, esz == 4 ? CU_TENSOR_MAP_DATA_TYPE_UINT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, base, dims, strides,
+                 box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    };
+    q.gtma = gate_map(&gm, p.gr, p.gr_dt, p.gr_st, p.gr_sb, p.gr_sh) &&
+             gate_map(&bm, p.br, p.br_dt, p.br_st, p.br_sb, p.br_sh);
+  }
   // GDNR_FLUSH_NONE: the variant without the flush path (flushing units are
   // skipped and reported); otherwise the flush-capable one
   const bool flush = p.flush_hint != GDNR_FLUSH_NONE;
@@ -2392,31 +2459,31 @@ cudaError_t launch_step5(const StepParams& p, bool fused, bool pdl, cudaStream_t
   if (p.ck_i8) {  // int8 checkpoints: GDNR_FLUSH_NONE steps only (step5_eligible)
     if (flush || p.sidx) return cudaErrorNotSupported;
     if (fused)
-      return g.hpu == 2 ? s5_launch<true, 2, false, false, true>(p, ck, kr, vr, grid, sm, pdl, stream)
-                        : s5_launch<true, 1, false, false, true>(p, ck, kr, vr, grid, sm, pdl, stream);
-    return g.hpu == 2 ? s5_launch<false, 2, false, false, true>(p, ck, kr, vr, grid, sm, pdl, stream)
-                      : s5_launch<false, 1, false, false, true>(p, ck, kr, vr, grid, sm, pdl, stream);
+      return g.hpu == 2 ? s5_launch<true, 2, false, false, true>(q, ck, kr, vr, gm, bm, grid, sm, pdl, stream)
+                        : s5_launch<true, 1, false, false, true>(q, ck, kr, vr, gm, bm, grid, sm, pdl, stream);
+    return g.hpu == 2 ? s5_launch<false, 2, false, false, true>(q, ck, kr, vr, gm, bm, grid, sm, pdl, stream)
+                      : s5_launch<false, 1, false, false, true>(q, ck, kr, vr, gm, bm, grid, sm, pdl, stream);
   }
   if (fused && p.sidx) {
     if (g.hpu == 2)
-      return flush ? s5_launch<true, 2, true, true>(p, ck, kr, vr, grid, sm, pdl, stream)
-                   : s5_launch<true, 2, false, true>(p, ck, kr, vr, grid, sm, pdl, stream);
-    return flush ? s5_launch<true, 1, true, true>(p, ck, kr, vr, grid, sm, pdl, stream)
-                 : s5_launch<true, 1, false, true>(p, ck, kr, vr, grid, sm, pdl, stream);
+      return flush ? s5_launch<true, 2, true, true>(q, ck, kr, vr, gm, bm, grid, sm, pdl, stream)
+                   : s5_launch<true, 2, false, true>(q, ck, kr, vr, gm, bm, grid, sm, pdl, stream);
+    return flush ? s5_launch<true, 1, true, true>(q, ck, kr, vr, gm, bm, grid, sm, pdl, stream)
+                 : s5_launch<true, 1, false, true>(q, ck, kr, vr, gm, bm, grid, sm, pdl, stream);
   }
   if (p.sidx) return cudaErrorNotSupported;  // packed decode: fused steps only
   if (fused) {
     if (g.hpu == 2)
-      return flush ? s5_launch<true, 2, true>(p, ck, kr, vr, grid, sm, pdl, stream)
-                   : s5_launch<true, 2, false>(p, ck, kr, vr, grid, sm, pdl, stream);
-    return flush ? s5_launch<true, 1, true>(p, ck, kr, vr, grid, sm, pdl, stream)
-                 : s5_launch<true, 1, false>(p, ck, kr, vr, grid, sm, pdl, stream);
+      return flush ? s5_launch<true, 2, true>(q, ck, kr, vr, gm, bm, grid, sm, pdl, stream)
+                   : s5_launch<true, 2, false>(q, ck, kr, vr, gm, bm, grid, sm, pdl, stream);
+    return flush ? s5_launch<true, 1, true>(q, ck, kr, vr, gm, bm, grid, sm, pdl, stream)
+                 : s5_launch<true, 1, false>(q, ck, kr, vr, gm, bm, grid, sm, pdl, stream);
   }
   if (g.hpu == 2)
-    return flush ? s5_launch<false, 2, true>(p, ck, kr, vr, grid, sm, pdl, stream)
-                 : s5_launch<false, 2, false>(p, ck, kr, vr, grid, sm, pdl, stream);
-  return flush ? s5_launch<false, 1, true>(p, ck, kr, vr, grid, sm, pdl, stream)
-               : s5_launch<false, 1, false>(p, ck, kr, vr, grid, sm, pdl, stream);
+    return flush ? s5_launch<false, 2, true>(q, ck, kr, vr, gm, bm, grid, sm, pdl, stream)
+                 : s5_launch<false, 2, false>(q, ck, kr, vr, gm, bm, grid, sm, pdl, stream);
+  return flush ? s5_launch<false, 1, true>(q, ck, kr, vr, gm, bm, grid, sm, pdl, stream)
+               : s5_launch<false, 1, false>(q, ck, kr, vr, gm, bm, grid, sm, pdl, stream);
 }
 
 }  // namespace gdnr
