@@ -318,6 +318,13 @@ __device__ __forceinline__ uint32_t quant_e4m3x2(float x0, float x1, float d, fl
   return f2_to_e4m3x2(y0, y1);
 }
 
+// The exact path of quant_pairs_warp, out of line: it is rare, and one copy of it
+// instead of one per pair keeps the re-quantisation loops small in the
+// instruction cache (flush step 69.6 -> 68.5 us at B = 64, L = 16).
+static __device__ __noinline__ uint32_t quant_e4m3x2_slow(float x0, float x1, float d, float rcp, uint32_t kd, bool ok) {
+  return quant_e4m3x2(x0, x1, d, rcp, kd, ok);
+}
+
 // e4m3 codes of RN(x / d) for NP pairs, the common case without a division and
 // without the per-element work of quant_exact.  y = RN(x * rcp) is within one
 // ulp of the IEEE quotient RN(x / d) (rcp = RN(1 / d) has relative error at
@@ -343,7 +350,7 @@ __device__ __forceinline__ void quant_pairs_warp(const float* x, uint32_t* c, fl
   if (__any_sync(0xffffffffu, amb != 0u)) {
 #pragma unroll
     for (int j = 0; j < NP; ++j)
-      if ((amb >> j) & 1u) c[j] = quant_e4m3x2(x[2 * j], x[2 * j + 1], d, rcp, kd, ok);
+      if ((amb >> j) & 1u) c[j] = quant_e4m3x2_slow(x[2 * j], x[2 * j + 1], d, rcp, kd, ok);
   }
 }
 
