@@ -1336,29 +1336,53 @@ def run_core(args, device, stream):
         for ck, d, vl, fl, out in sets:
             gdnr.gdn_replay_fp8(ck.payload, ck.scale, d["q"], d["k"], d["v"], d["g"], d["beta"], vl, fl, out=out,
                                 flush_hint="none")
-    torch.cuda.synchronize()  # the inputs above come from the default stream
-    with torch.cuda.stream(stream):
-        run()
-    torch.cuda.synchronize()
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g, stream=stream):
-        run()
-    reps = 50
-    with torch.cuda.stream(stream):
-        for _ in range(5):
-            g.replay()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(reps):
-            g.replay()
-        e1.record(stream)
-    torch.cuda.synchronize()
-    us = 1e3 * e0.elapsed_time(e1) / (reps * NL)
+
+    # gdn_replay_fp8_split (kern.py:1129-1235): precompute + apply launches, caller T / c
+    # buffers; and the variant without caller scratch (library-owned static buffers)
+    tq = torch.empty(B, HV, KD, dtype=torch.float32, device=device)
+    coef = torch.empty(B, HV, L, dtype=torch.float32, device=device)
+
+    def run_split():
+        for ck, d, vl, fl, out in sets:
+            gdnr.gdn_replay_fp8_split(ck.payload, ck.scale, d["q"], d["k"], d["v"], d["g"], d["beta"], vl, tq, coef,
+                                      out=out)
+
+    def run_split_static():
+        for ck, d, vl, fl, out in sets:
+            gdnr.gdn_replay_fp8_split_static(ck.payload, ck.scale, d["q"], d["k"], d["v"], d["g"], d["beta"], vl, out)
+
+    def graph_us(fn):
+        torch.cuda.synchronize()  # the inputs above come from the default stream
+        with torch.cuda.stream(stream):
+            fn()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            fn()
+        reps = 50
+        with torch.cuda.stream(stream):
+            for _ in range(5):
+                g.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(reps):
+                g.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        del g
+        return 1e3 * e0.elapsed_time(e1) / (reps * NL)
+
+    us = graph_us(run)
     res.update({"us_per_launch": us, "GB_s": nbytes / (us * 1e-6) / 1e9, "steps_seq_per_s": B / (us * 1e-6),
                 "frac_of_peak": nbytes / (us * 1e-6) / 1e9 / measured_peak()[0]})
-    del g
     res["algorithmic_bytes_per_launch"] = nbytes
     res["workload"] = "config2: gdn_replay_fp8 non-flush, B=64, full L=16 ring, f32 scales/gates"
+    us_split = graph_us(run_split)
+    us_static = graph_us(run_split_static)
+    res["split"] = {"us_per_call": us_split, "static_us_per_call": us_static,
+                    "ratio_to_fused_replay": us_split / us,
+                    "workload": "gdn_replay_fp8_split (precompute + apply, caller T [B,HV,K] / c [B,HV,L] f32 "
+                                "buffers) and gdn_replay_fp8_split_static (no caller scratch), same inputs"}
     return res
 
 
