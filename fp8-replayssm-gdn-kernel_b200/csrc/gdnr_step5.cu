@@ -67,9 +67,19 @@ template <bool FLUSH>
 __host__ __device__ constexpr bool s5_vb() {
   return !FLUSH;
 }
+#ifndef S5_VB_VPW
+#define S5_VB_VPW 2
+#endif
+// vblock readout: vblocks per warp and unit (two-head units: S5_VB_VPW, so that
+// 8 / S5_VB_VPW warps read a unit out and S5_VB_VPW units are in flight; one-head
+// units: 1, four warps per unit, two units in flight)
+template <int HPU>
+__host__ __device__ constexpr int s5_vpw() {
+  return HPU == 2 ? S5_VB_VPW : 1;
+}
 template <int HPU, bool FLUSH>
 __host__ __device__ constexpr int s5_rpu() {  // readout warps per unit
-  return s5_tc<HPU, FLUSH>() ? S5_NRW : (s5_vb<FLUSH>() ? 4 * HPU : S5_TEAM);
+  return s5_tc<HPU, FLUSH>() ? S5_NRW : (s5_vb<FLUSH>() ? 4 * HPU / s5_vpw<HPU>() : S5_TEAM);
 }
 // Tensor memory of the tensor-memory readout: columns 0..127 the readout's
 // accumulators (stages x heads x 16); from S5_TM_STASH, 128 columns per readout
@@ -1656,21 +1666,25 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
   // of the warp's rows.
   constexpr bool VB = s5_vb<FLUSH>();
   constexpr int VBW = 2 * HPU;  // vblocks per readout warp and unit (teams)
-  constexpr int SC_UNITS = VB ? 32 : 32 / VBW;  // units with a prefetched scale
+  constexpr int VPW = s5_vpw<HPU>();              // vblock readout: vblocks per warp and unit
+  constexpr int WPU = 4 * HPU / VPW;             // vblock readout: warps per unit
+  constexpr int SC_UNITS = VB ? 32 / VPW : 32 / VBW;  // units with a prefetched scale
   uint32_t scl_raw = 0u;
   const int rw = warp - 1 - S5_NCW;
   const int team = rw / S5_TEAM, mem = rw % S5_TEAM;
-  const int head_r = (TC || VB) ? (HPU == 2 ? (rw >> 2) : 0) : (HPU == 2 ? mem : 0);
-  const int rbase = VB ? 32 * (rw & 3) : (HPU == 2 ? 0 : 64 * mem);
+  const int vq = (rw % WPU) * VPW;  // vblock readout: the warp's first vblock of a unit (0..4 HPU - 1)
+  const int head_r = TC ? (HPU == 2 ? (rw >> 2) : 0) : (VB ? vq / 4 : (HPU == 2 ? mem : 0));
+  const int rbase = VB ? 32 * (vq % 4) : (HPU == 2 ? 0 : 64 * mem);
   if (warp > S5_NCW) {
     if constexpr (TC) {  // the zero rows of the tensor-core T operands
       reinterpret_cast<uint32_t*>(smem + lay.zb)[tid - 32 * (1 + S5_NCW)] = 0u;
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     } else if constexpr (VB) {
-      const int i = lane < nu ? lane : 0;
+      // lane l: unit l / VPW, the warp's vblock l % VPW
+      const int i = lane / VPW < nu ? lane / VPW : 0;
       const S5Unit U = s5_unit<SIDX>(bid + i * grid, p, G, geo);
       scl_raw = s5_ld_raw(p.sc, int64_t(U.s < 0 ? 0 : U.s) * p.sc_sb + int64_t(U.hv0 + head_r) * p.sc_sh +
-                                    int64_t(rw & 3) * p.sc_sv,
+                                    int64_t(rbase / VBLOCK + lane % VPW) * p.sc_sv,
                           p.sc_dt);
     } else {
       int i = team + S5_NS * (lane / VBW);
@@ -2144,25 +2158,26 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
     }
   } else if constexpr (VB) {
   // =================== vblock readout ===================
-  // Warp w reads out rows 32 (w % 4) .. of head w / 4 of every unit (two-head
-  // units), or of every other unit (one-head units: group w / 4 takes the units
-  // i = w / 4 (mod 2)); the unit's 4 x hpu warps release its stage and chain
-  // results as they finish.
-  constexpr int NG = S5_NRW / (4 * HPU);  // readout groups
+  // The readout warps form NG groups of WPU warps; group g reads out the units
+  // i = g (mod NG), warp q of a group the VPW vblocks (32 rows each) from vblock
+  // q VPW of the unit (heads in order); the unit's WPU warps release its stage
+  // and chain results as they finish.
+  constexpr int NG = S5_NRW / WPU;  // readout groups (units in flight)
   float* ost = reinterpret_cast<float*>(smem + lay.ost0 + rw * 512);
   const float sc_pre = s5_cvt(scl_raw, p.sc_dt);
-  for (int i = NG == 1 ? 0 : (rw >> 2); i < nu; i += NG) {
+  for (int i = rw / WPU; i < nu; i += NG) {
     const int s = i % S5_NS;
     const int ccw = i % S5_NCW, k = i / S5_NCW;
     const int code = table[i];
     float sc = sc_pre;
-    int sc_base = i;
-    if (i >= SC_UNITS) {  // beyond the prefetched units
+    int sc_base = i * VPW;
+    if (i >= SC_UNITS) {  // beyond the prefetched units: lane v < VPW holds vblock v
       sc = 1.0f;
       sc_base = 0;
-      if (!s5_skip(code)) {
+      if (lane < VPW && !s5_skip(code)) {
         const S5Unit U = s5_unit<SIDX>(bid + i * grid, p, G, geo);
-        sc = load_scalar(p.sc, int64_t(U.s) * p.sc_sb + int64_t(U.hv0 + head_r) * p.sc_sh + int64_t(rw & 3) * p.sc_sv,
+        sc = load_scalar(p.sc, int64_t(U.s) * p.sc_sb + int64_t(U.hv0 + head_r) * p.sc_sh +
+                                   int64_t(rbase / VBLOCK + lane) * p.sc_sv,
                          p.sc_dt);
       }
     }
@@ -2173,15 +2188,19 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       const S5Unit U = s5_unit<SIDX>(bid + i * grid, p, G, geo);
       const uint8_t* res = smem + lay.res0 + ccw * lay.res_bytes;
       const float* misc = reinterpret_cast<const float*>(res + lay.misc) + head_r * 4;
-      s5_readout<2, I8>(sb + lay.ck + head_r * 16384, sb + lay.vr + head_r * 4096, res + lay.t8 + head_r * 8 * T8STR,
-                        reinterpret_cast<const uint16_t*>(res + lay.cb + head_r * 96), misc[0], sc, sc_base, rbase,
-                        s5_nmem(code), ost, lane);
+      s5_readout<2 * VPW, I8>(sb + lay.ck + head_r * 16384, sb + lay.vr + head_r * 4096,
+                              res + lay.t8 + head_r * 8 * T8STR,
+                              reinterpret_cast<const uint16_t*>(res + lay.cb + head_r * 96), misc[0], sc, sc_base,
+                              rbase, s5_nmem(code), ost, lane);
       __syncwarp();
-      // this token's own slot (fused) as a rank-one term, K^-1/2, one row per lane
-      float o = ost[lane];
+      // this token's own slot (fused) as a rank-one term, K^-1/2, VPW rows per lane
+      float o[VPW];
+#pragma unroll
+      for (int r = 0; r < VPW; ++r) o[r] = ost[VPW * lane + r];
       if (FUSED) {
         const uint16_t* vnew = reinterpret_cast<const uint16_t*>(res + lay.vnew + head_r * 256) + rbase;
-        o = fmaf(misc[1], bf16_to_f(vnew[lane]), o);
+#pragma unroll
+        for (int r = 0; r < VPW; ++r) o[r] = fmaf(misc[1], bf16_to_f(vnew[VPW * lane + r]), o[r]);
       }
       __syncwarp();
       // every read of the stage and the chain's results has returned its value (all
@@ -2191,8 +2210,11 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
         s5_arrive_relaxed(&empty[s]);
         s5_arrive_relaxed(&rbar[ccw]);
       }
-      store_scalar(p.out, int64_t(U.b) * p.o_sb + int64_t(U.hv0 + head_r) * p.o_sh + int64_t(rbase + lane) * p.o_sv,
-                   p.o_dt, o * KSCALE_H);
+#pragma unroll
+      for (int r = 0; r < VPW; ++r)
+        store_scalar(p.out,
+                     int64_t(U.b) * p.o_sb + int64_t(U.hv0 + head_r) * p.o_sh + int64_t(rbase + VPW * lane + r) * p.o_sv,
+                     p.o_dt, o[r] * KSCALE_H);
     } else {
       __syncwarp();
       if (lane == 0) {
