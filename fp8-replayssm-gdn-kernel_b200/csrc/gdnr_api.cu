@@ -252,6 +252,43 @@ int pick_rows(int requested, int group, int L, bool f32ck, int& rows) {
 
 }  // namespace
 
+int gdnr::replay_split_step5(const gdnr_tensor& ck, const gdnr_tensor& sc, const gdnr_tensor& q, const gdnr_tensor& kr,
+                       const gdnr_tensor& vr, const gdnr_tensor& gr, const gdnr_tensor& br, const gdnr_tensor& vl,
+                       const gdnr_tensor& out, float* tq, const int64_t* tq_s, float* co, const int64_t* co_s,
+                       uint32_t* err, cudaStream_t st, int* done) {
+  *done = 0;
+  StepParams p;
+  memset(&p, 0, sizeof(p));
+  bool f32ck = false;
+  int group = 0;
+  CHECK(validate_state(ck, sc, kr, vr, gr, br, p, f32ck, group));
+  if (f32ck || tq_s[2] != 1) return GDNR_OK;
+  CHECK(validate_out(out, p));
+  p.q = q.data;
+  p.q_sb = q.stride[0];
+  p.q_sh = q.stride[1];
+  p.q_dt = q.dtype;
+  p.valid_len = static_cast<const int32_t*>(vl.data);
+  p.vl_s = vl.stride[0];
+  p.flush = nullptr;  // no flush input: every unit replays
+  p.rows = 128;
+  p.err = err ? err : default_error_word();
+  if (!p.err) return GDNR_OK;
+  p.flush_hint = GDNR_FLUSH_NONE;
+  p.tqo = tq;
+  p.tqo_sb = tq_s[0];
+  p.tqo_sh = tq_s[1];
+  p.coo = co;
+  p.coo_sb = co_s[0];
+  p.coo_sh = co_s[1];
+  p.coo_st = co_s[2];
+  if (!step5_eligible(p, false, false)) return GDNR_OK;
+  *done = 1;
+  if (p.B == 0) return GDNR_OK;
+  return cuda_status(launch_step5(p, false, false, st), "gdnr_replay_split launch");
+}
+
+
 extern "C" {
 
 const char* gdnr_last_error(void) { return g_last_error.c_str(); }

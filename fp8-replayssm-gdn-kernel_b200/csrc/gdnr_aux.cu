@@ -135,28 +135,38 @@ struct SplitParams {
 __global__ void __launch_bounds__(128) split_precompute_kernel(const __grid_constant__ SplitParams p) {
   const int h = blockIdx.x, b = blockIdx.y;
   const int j = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (j >= p.G) return;
-  const int hv = h * p.G + j;
+  const int hv = h * p.G + j;  // the block has 32 G threads
   int n = p.valid_len[int64_t(b) * p.vl_s];
   n = n < 0 ? 0 : (n > p.L ? p.L : n);
+  // the key head's ring rows (4 elements per lane; shared by the G warps) and each
+  // warp's betas and decays of slots t < n, all loaded before the backward chain so
+  // that the chain waits on no global load
+  __shared__ uint2 ks[MAX_L][32];
+  __shared__ float bs[MAX_G][MAX_L], gs[MAX_G][MAX_L];
+  for (int t = j; t < n; t += p.G) {
+    const uint16_t* kp = p.kr + int64_t(b) * p.kr_sb + int64_t(t) * p.kr_st + int64_t(h) * p.kr_sh + lane * 4;
+    ks[t][lane] = make_uint2(uint32_t(kp[0]) | (uint32_t(kp[1]) << 16), uint32_t(kp[2]) | (uint32_t(kp[3]) << 16));
+  }
+  for (int t = lane; t < n; t += 32) {
+    bs[j][t] = load_scalar(p.br, int64_t(b) * p.br_sb + int64_t(t) * p.br_st + int64_t(hv) * p.br_sh, p.br_dt);
+    gs[j][t] = expf(load_scalar(p.gr, int64_t(b) * p.gr_sb + int64_t(t) * p.gr_st + int64_t(hv) * p.gr_sh, p.gr_dt));
+  }
   float T[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) T[i] = load_scalar(p.q, int64_t(b) * p.q_sb + int64_t(h) * p.q_sh + lane * 4 + i, p.q_dt);
+  __syncthreads();
   for (int t = n - 1; t >= 0; --t) {
-    const uint16_t* kp = p.kr + int64_t(b) * p.kr_sb + int64_t(t) * p.kr_st + int64_t(h) * p.kr_sh + lane * 4;
-    float k[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) k[i] = bf16_to_f(kp[i]);
+    const uint2 kw = ks[t][lane];
+    const float2 k01 = bf16x2_to_f2(kw.x), k23 = bf16x2_to_f2(kw.y);
+    const float k[4] = {k01.x, k01.y, k23.x, k23.y};
     float d = T[0] * k[0];
     d = fmaf(T[1], k[1], d);
     d = fmaf(T[2], k[2], d);
     d = fmaf(T[3], k[3], d);
     d = warp_sum(d);
-    const float c =
-        load_scalar(p.br, int64_t(b) * p.br_sb + int64_t(t) * p.br_st + int64_t(hv) * p.br_sh, p.br_dt) * d;
+    const float c = bs[j][t] * d;
     if (lane == 0) p.coef[int64_t(b) * p.co_sb + int64_t(hv) * p.co_sh + int64_t(t) * p.co_st] = c;
-    const float gam =
-        expf(load_scalar(p.gr, int64_t(b) * p.gr_sb + int64_t(t) * p.gr_st + int64_t(hv) * p.gr_sh, p.gr_dt));
+    const float gam = gs[j][t];
 #pragma unroll
     for (int i = 0; i < 4; ++i) T[i] = gam * (T[i] - c * k[i]);
   }
@@ -168,40 +178,63 @@ __global__ void __launch_bounds__(128) split_precompute_kernel(const __grid_cons
 __global__ void __launch_bounds__(256) split_apply_kernel(const __grid_constant__ SplitParams p) {
   __shared__ float tq_s[128];
   __shared__ float cf_s[MAX_L];
+  __shared__ float sc_s[4];
+  __shared__ uint16_t vr_s[MAX_L][128];  // value-ring rows [z rows, (z + 1) rows) of every slot
   const int hv = blockIdx.x, b = blockIdx.y, z = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  int n = p.valid_len[int64_t(b) * p.vl_s];
-  n = n < 0 ? 0 : (n > p.L ? p.L : n);
-  if (tid < 128) tq_s[tid] = p.tq[int64_t(b) * p.tq_sb + int64_t(hv) * p.tq_sh + int64_t(tid) * p.tq_sk];
-  if (tid < n) cf_s[tid] = p.coef[int64_t(b) * p.co_sb + int64_t(hv) * p.co_sh + int64_t(tid) * p.co_st];
-  __syncthreads();
+  // Every load of the block goes out before the one barrier: the valid length,
+  // T, all L coefficients (those at t >= n are masked after the barrier), the four
+  // vblock scales, the value-ring rows of all L slots and each warp's checkpoint
+  // rows (at most 4 passes of 4 rows, 8 lanes per row).
+  const int nraw = p.valid_len[int64_t(b) * p.vl_s];
+  const float tqv = tid < 128 ? p.tq[int64_t(b) * p.tq_sb + int64_t(hv) * p.tq_sh + int64_t(tid) * p.tq_sk] : 0.0f;
+  const float cfv = tid < p.L ? p.coef[int64_t(b) * p.co_sb + int64_t(hv) * p.co_sh + int64_t(tid) * p.co_st] : 0.0f;
+  if (tid < 4) sc_s[tid] = load_scalar(p.sc, int64_t(b) * p.sc_sb + int64_t(hv) * p.sc_sh + int64_t(tid) * p.sc_sv, p.sc_dt);
+  for (int idx = tid; idx < p.L * p.rows; idx += 256) {
+    const int t = idx / p.rows, rr = idx - t * p.rows;
+    vr_s[t][rr] = p.vr[int64_t(b) * p.vr_sb + int64_t(t) * p.vr_st + int64_t(hv) * p.vr_sh + z * p.rows + rr];
+  }
+  constexpr int NP = 4;
   const int c = lane & 7;
+  const int rl0 = warp * 4 + (lane >> 3);  // row within the block's rows
+  const int npass = p.rows / 32;
+  uint4 w[NP];
+#pragma unroll
+  for (int k = 0; k < NP; ++k)
+    if (k < npass)
+      w[k] = *reinterpret_cast<const uint4*>(p.ck + int64_t(b) * p.ck_sb + int64_t(hv) * p.ck_sh +
+                                             int64_t(z * p.rows + rl0 + 32 * k) * 128 + c * 16);
+  const int n = nraw < 0 ? 0 : (nraw > p.L ? p.L : nraw);
+  if (tid < 128) tq_s[tid] = tqv;
+  if (tid < p.L) cf_s[tid] = tid < n ? cfv : 0.0f;
+  __syncthreads();
   float Tl[16];
 #pragma unroll
   for (int i = 0; i < 16; ++i) Tl[i] = tq_s[c * 16 + i];
-  // each warp pass covers 4 rows; rows [z*rows, (z+1)*rows)
-  for (int r = z * p.rows + warp * 4 + (lane >> 3); r < (z + 1) * p.rows; r += 32) {
-    const uint4 w = *reinterpret_cast<const uint4*>(p.ck + int64_t(b) * p.ck_sb + int64_t(hv) * p.ck_sh +
-                                                    int64_t(r) * 128 + c * 16);
+#pragma unroll
+  for (int k = 0; k < NP; ++k) {
+    if (k >= npass) break;
+    const int rl = rl0 + 32 * k, r = z * p.rows + rl;
     float f[16];
-    e4m3x4_to_f4(w.x, f);
-    e4m3x4_to_f4(w.y, f + 4);
-    e4m3x4_to_f4(w.z, f + 8);
-    e4m3x4_to_f4(w.w, f + 12);
+    e4m3x4_to_f4(w[k].x, f);
+    e4m3x4_to_f4(w[k].y, f + 4);
+    e4m3x4_to_f4(w[k].z, f + 8);
+    e4m3x4_to_f4(w[k].w, f + 12);
     float acc = 0.0f;
 #pragma unroll
     for (int i = 0; i < 16; ++i) acc = fmaf(f[i], Tl[i], acc);
     acc += __shfl_xor_sync(0xffffffffu, acc, 1);
     acc += __shfl_xor_sync(0xffffffffu, acc, 2);
     acc += __shfl_xor_sync(0xffffffffu, acc, 4);
-    if (c == 0) {
-      const float sc = load_scalar(p.sc, int64_t(b) * p.sc_sb + int64_t(hv) * p.sc_sh + int64_t(r / VBLOCK) * p.sc_sv,
-                                   p.sc_dt);
-      float o = acc * sc;
-      for (int t = 0; t < n; ++t)
-        o = fmaf(cf_s[t], bf16_to_f(p.vr[int64_t(b) * p.vr_sb + int64_t(t) * p.vr_st + int64_t(hv) * p.vr_sh + r]), o);
-      store_scalar(p.out, int64_t(b) * p.o_sb + int64_t(hv) * p.o_sh + int64_t(r) * p.o_sv, p.o_dt, o * KSCALE_AUX);
-    }
+    // V^T c of this row: the row's 8 lanes take the slots t = c (mod 8), then reduce
+    float ring = 0.0f;
+    for (int t = c; t < n; t += 8) ring = fmaf(cf_s[t], bf16_to_f(vr_s[t][rl]), ring);
+    ring += __shfl_xor_sync(0xffffffffu, ring, 1);
+    ring += __shfl_xor_sync(0xffffffffu, ring, 2);
+    ring += __shfl_xor_sync(0xffffffffu, ring, 4);
+    if (c == 0)
+      store_scalar(p.out, int64_t(b) * p.o_sb + int64_t(hv) * p.o_sh + int64_t(r) * p.o_sv, p.o_dt,
+                   fmaf(acc, sc_s[r / VBLOCK], ring) * KSCALE_AUX);
   }
 }
 
@@ -492,6 +525,16 @@ int gdnr_replay_split(const gdnr_replay_split_args* a, void* stream) {
   p.B = int(B); p.H = int(H); p.HV = int(HV); p.L = int(L); p.G = int(HV / H); p.rows = rows;
   if (B == 0) return GDNR_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // the persistent step kernel in replay mode, writing T and c as it goes, where it
+  // takes the layout; else the precompute + apply kernels below
+  {
+    const int64_t tq_s[3] = {a->tq.stride[0], a->tq.stride[1], a->tq.stride[2]};
+    const int64_t co_s[3] = {a->coef.stride[0], a->coef.stride[1], a->coef.stride[2]};
+    int done = 0;
+    CK(replay_split_step5(a->checkpoint, a->scale, a->q, a->k_ring, a->v_ring, a->g_ring, a->beta_ring, a->valid_len,
+                          a->out, p.tq, tq_s, p.coef, co_s, static_cast<uint32_t*>(a->error_flag), st, &done));
+    if (done) return GDNR_OK;
+  }
   split_precompute_kernel<<<dim3(unsigned(H), unsigned(B)), 32 * p.G, 0, st>>>(p);
   CK(cuda_status(cudaGetLastError(), "gdnr_replay_split precompute launch"));
   split_apply_kernel<<<dim3(unsigned(HV), unsigned(B), unsigned(128 / rows)), 256, 0, st>>>(p);

@@ -81,6 +81,13 @@ struct StepParams {
   // persistent step without the flush path: the gate rings are read by TMA
   // (set by its launcher when their layout allows)
   int32_t gtma;
+  // split replay (gdnr_replay_split): the persistent kernel also writes the
+  // transformed query T [B,HV,K] (innermost contiguous) and the coefficients c_t
+  // (t < valid_len) [B,HV,L] to these caller buffers; null otherwise
+  float* tqo;
+  int64_t tqo_sb, tqo_sh;
+  float* coo;
+  int64_t coo_sb, coo_sh, coo_st;
 };
 
 struct SmemLayout {
@@ -169,6 +176,12 @@ cudaError_t launch_dequantize(const CodecParams& p, cudaStream_t stream);
 // ---------------------------------------------------------------- host helpers
 int set_error(int code, const char* fmt, ...);
 uint32_t* default_error_word();
+// The split replay through the persistent step kernel (replay without flush that
+// also writes T and c); *done = 0 when the layout is not one it takes.
+int replay_split_step5(const gdnr_tensor& ck, const gdnr_tensor& sc, const gdnr_tensor& q, const gdnr_tensor& kr,
+                       const gdnr_tensor& vr, const gdnr_tensor& gr, const gdnr_tensor& br, const gdnr_tensor& vl,
+                       const gdnr_tensor& out, float* tq, const int64_t* tq_s, float* co, const int64_t* co_s,
+                       uint32_t* err, cudaStream_t st, int* done);
 
 inline bool present(const gdnr_tensor& t) { return t.ndim > 0 && t.data != nullptr; }
 

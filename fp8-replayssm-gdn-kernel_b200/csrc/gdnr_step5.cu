@@ -362,7 +362,7 @@ __device__ __forceinline__ void s5_tc_after_sync() { asm volatile("tcgen05.fence
 // failure in *abort (then every later wait returns at once).
 // (The waiting part is one out-of-line copy: every inlined copy of it would
 // cost instruction-cache space next to the hot code.)
-__device__ __noinline__ bool s5_wait_slow(uint64_t* bar, uint32_t parity, uint32_t* err, volatile int* abort) {
+static __device__ __noinline__ bool s5_wait_slow(uint64_t* bar, uint32_t parity, uint32_t* err, volatile int* abort) {
   const uint32_t a = smem_addr(bar);
   if (*abort) return false;
   const uint64_t t0 = globaltimer_ns();
@@ -381,7 +381,7 @@ __device__ __noinline__ bool s5_wait_slow(uint64_t* bar, uint32_t parity, uint32
 // Abort path only: a bounded wait for an mbarrier phase that ignores *abort, so
 // that copies and tensor-core work this CTA has already issued are finished
 // before it releases its tensor memory or exits.
-__device__ __noinline__ bool s5_drain_wait(uint64_t* bar, uint32_t parity) {
+static __device__ __noinline__ bool s5_drain_wait(uint64_t* bar, uint32_t parity) {
   const uint32_t a = smem_addr(bar);
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 1; it < WAIT_LIMIT_ITERS; ++it) {
@@ -394,7 +394,7 @@ __device__ __noinline__ bool s5_drain_wait(uint64_t* bar, uint32_t parity) {
 // Abort path only: the stage loads of the last min(issued, S5_NS) units, the
 // only ones that can still be in flight (a stage is reloaded only after its
 // previous load was waited for, and no load is issued once *abort is set).
-__device__ __noinline__ void s5_drain_stages(uint64_t* full, int issued) {
+static __device__ __noinline__ void s5_drain_stages(uint64_t* full, int issued) {
   for (int u = issued > S5_NS ? issued - S5_NS : 0; u < issued; ++u)
     s5_drain_wait(&full[u % S5_NS], uint32_t((u / S5_NS) & 1));
 }
@@ -681,7 +681,7 @@ __device__ __forceinline__ S5In s5_fetch(const StepParams& p, const S5Unit& U, i
     in.a = in.bb = 0u;
     in.alog = in.dtb = 0.0f;
     in.pos = p.valid_len[int64_t(U.b) * p.vl_s];
-    in.flag = s5_ld_flag(p.flush, int64_t(U.b) * p.fl_s, p.fl_dt);
+    in.flag = p.flush ? s5_ld_flag(p.flush, int64_t(U.b) * p.fl_s, p.fl_dt) : 0;
   }
   return in;
 }
@@ -784,7 +784,9 @@ __device__ __forceinline__ void s5_tloop(const uint8_t* kbuf, float wj, int n, f
 
 // The chain of one unit (one warp, both heads).  kbuf: the unit's key ring
 // (swizzled, slots < nmem loaded); res: this warp's result block.
-template <bool FUSED, int HPU, bool FLUSH, bool I8 = false>
+// WT: also write T (fp32, before its split) and the replay coefficients c_t of the
+// slots t < n to the split replay's buffers (StepParams::tqo / coo)
+template <bool FUSED, int HPU, bool FLUSH, bool I8 = false, bool WT = false>
 __device__ __forceinline__ S5Append s5_chain(const StepParams& p, const S5Unit& U, int code, const S5In& in,
                                              uint8_t* kbuf, const uint8_t* gbuf, uint8_t* res, const S5Layout& lay,
                                              int lane) {
@@ -1087,6 +1089,14 @@ __device__ __forceinline__ S5Append s5_chain(const StepParams& p, const S5Unit& 
     for (int i = 0; i < 4; ++i) T[h][i] = al * qv[i];
   }
   s5_tloop<HPU>(kbuf, wj, n, T, lane);
+  if constexpr (WT) {
+#pragma unroll
+    for (int h = 0; h < HPU; ++h)
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        p.tqo[int64_t(U.b) * p.tqo_sb + int64_t(U.hv0 + h) * p.tqo_sh + 4 * lane + i] = T[h][i];
+    if (e < HPU && t < n) p.coo[int64_t(U.b) * p.coo_sb + int64_t(U.hv0 + e) * p.coo_sh + int64_t(t) * p.coo_st] = cval;
+  }
   __syncwarp();  // q-split / Gram scratch (aliases t8) is dead from here on
   s5_tsplit<HPU, s5_tc<HPU, FLUSH>(), I8>(T, res + lay.t8, misc, lane);
   return ap;
@@ -1438,7 +1448,7 @@ __device__ __forceinline__ void s5_st_release(uint32_t* p, uint32_t v) {
 // unit commits it issued when it stops; the commit of the last one arrives
 // once every tensor-core operation of the CTA has completed.  Bounded waits
 // for both, ignoring *abort, before the tensor memory is released.
-__device__ __noinline__ void s5_drain_mma(uint64_t* mmab, const uint32_t* ncommit) {
+static __device__ __noinline__ void s5_drain_mma(uint64_t* mmab, const uint32_t* ncommit) {
   const uint64_t t0 = globaltimer_ns();
   uint32_t n = s5_ld_acquire(ncommit);
   for (uint32_t it = 1; n == 0xffffffffu && it < WAIT_LIMIT_ITERS; ++it) {
@@ -1540,7 +1550,8 @@ __device__ __forceinline__ void s5_flush_task(const StepParams& p, uint8_t* smem
 
 // SIDX: packed decode (state slots through StepParams::sidx)
 // I8: int8 checkpoint codes ("vblock_int8"); the variant without the flush path only
-template <bool FUSED, int HPU, bool FLUSH, bool SIDX, bool I8 = false>
+// WT: the split replay (replay mode, no flush): T and c also go to the caller's buffers
+template <bool FUSED, int HPU, bool FLUSH, bool SIDX, bool I8 = false, bool WT = false>
 __global__ void __launch_bounds__(S5_THREADS, 1)
     step5_kernel(const __grid_constant__ StepParams p, const __grid_constant__ CUtensorMap ck_map,
                  const __grid_constant__ CUtensorMap kr_map, const __grid_constant__ CUtensorMap vr_map,
@@ -1707,7 +1718,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       raw0 = U.s >= 0 ? p.pos[int64_t(U.s) * p.pos_s] : INT_MIN;  // null / bad slot: skipped
     } else {
       raw0 = p.valid_len[int64_t(U.b) * p.vl_s];
-      raw1 = s5_ld_flag(p.flush, int64_t(U.b) * p.fl_s, p.fl_dt);
+      raw1 = p.flush ? s5_ld_flag(p.flush, int64_t(U.b) * p.fl_s, p.fl_dt) : 0;
     }
   }
   if (tid == S5_THREADS - 1) griddep_launch();
@@ -2056,7 +2067,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       const int code = s5_code<FUSED>(in0.pos, in0.flag, L, FLUSH);
       const bool work = ok && !s5_skip(code);
       S5Append ap{};
-      if (work) ap = s5_chain<FUSED, HPU, FLUSH, I8>(p, U, code, in0, kbuf, gbuf, res, lay, lane);
+      if (work) ap = s5_chain<FUSED, HPU, FLUSH, I8, WT>(p, U, code, in0, kbuf, gbuf, res, lay, lane);
       // the T operand is read by the tensor cores (async proxy)
       if (TC) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
@@ -2355,6 +2366,15 @@ static bool s5_grid(const StepParams& p, int& grid, S5Layout& lay) {
   return true;
 }
 
+// The split replay's kernel instantiations (WT) are compiled in a translation unit
+// of their own (gdnr_step5_split.cu includes this file with GDNR_S5_SPLIT_TU):
+// kept in the same module they shift the code of the flush-capable kernel and
+// slow it down (68.3 -> 71.5 us per flush launch, same box).
+cudaError_t launch_step5_split(const StepParams& q, const CUtensorMap& ck, const CUtensorMap& kr,
+                               const CUtensorMap& vr, const CUtensorMap& gm, const CUtensorMap& bm, int hpu, int grid,
+                               uint32_t smem, bool pdl, cudaStream_t stream);
+
+#ifndef GDNR_S5_SPLIT_TU
 bool step5_eligible(const StepParams& p, bool fused, bool f32ck) {
   if (f32ck || p.L < 4 || p.L > STEP2_MAX_L) return false;
   // int8 checkpoints: the non-flush variant only (a flush-capable call runs the
@@ -2380,6 +2400,7 @@ bool step5_eligible(const StepParams& p, bool fused, bool f32ck) {
   if (!s5_grid(p, grid, lay)) return false;
   return lay.total <= MAX_DYN_SMEM;
 }
+#endif  // GDNR_S5_SPLIT_TU
 
 using S5EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -2397,11 +2418,11 @@ static S5EncodeFn s5_encode_fn() {
   return fn;
 }
 
-template <bool FUSED, int HPU, bool FLUSH, bool SIDX = false, bool I8 = false>
+template <bool FUSED, int HPU, bool FLUSH, bool SIDX = false, bool I8 = false, bool WT = false>
 static cudaError_t s5_launch(const StepParams& p, const CUtensorMap& ck, const CUtensorMap& kr,
                              const CUtensorMap& vr, const CUtensorMap& gm, const CUtensorMap& bm, int grid,
                              uint32_t smem, bool pdl, cudaStream_t stream) {
-  auto kern = step5_kernel<FUSED, HPU, FLUSH, SIDX, I8>;
+  auto kern = step5_kernel<FUSED, HPU, FLUSH, SIDX, I8, WT>;
   static DynSmemCache smem_cache;  // per device: dynamic smem already allowed for this instance
   cudaError_t e = ensure_dyn_smem(reinterpret_cast<const void*>(kern), int(smem), smem_cache);
   if (e != cudaSuccess) return e;
@@ -2418,6 +2439,7 @@ static cudaError_t s5_launch(const StepParams& p, const CUtensorMap& ck, const C
   return cudaLaunchKernelEx(&cfg, kern, p, ck, kr, vr, gm, bm);
 }
 
+#ifndef GDNR_S5_SPLIT_TU
 cudaError_t launch_step5(const StepParams& p, bool fused, bool pdl, cudaStream_t stream) {
   S5EncodeFn enc = s5_encode_fn();
   if (!enc) return cudaErrorNotSupported;
@@ -2494,6 +2516,10 @@ cudaError_t launch_step5(const StepParams& p, bool fused, bool pdl, cudaStream_t
                  : s5_launch<true, 1, false, true>(q, ck, kr, vr, gm, bm, grid, sm, pdl, stream);
   }
   if (p.sidx) return cudaErrorNotSupported;  // packed decode: fused steps only
+  if (p.tqo) {  // split replay: replay mode, no flush
+    if (fused || flush || p.ck_i8) return cudaErrorNotSupported;
+    return launch_step5_split(q, ck, kr, vr, gm, bm, g.hpu, grid, sm, pdl, stream);
+  }
   if (fused) {
     if (g.hpu == 2)
       return flush ? s5_launch<true, 2, true>(q, ck, kr, vr, gm, bm, grid, sm, pdl, stream)
@@ -2508,9 +2534,19 @@ cudaError_t launch_step5(const StepParams& p, bool fused, bool pdl, cudaStream_t
                : s5_launch<false, 1, false>(q, ck, kr, vr, gm, bm, grid, sm, pdl, stream);
 }
 
+#else   // GDNR_S5_SPLIT_TU
+cudaError_t launch_step5_split(const StepParams& q, const CUtensorMap& ck, const CUtensorMap& kr,
+                               const CUtensorMap& vr, const CUtensorMap& gm, const CUtensorMap& bm, int hpu, int grid,
+                               uint32_t smem, bool pdl, cudaStream_t stream) {
+  return hpu == 2 ? s5_launch<false, 2, false, false, false, true>(q, ck, kr, vr, gm, bm, grid, smem, pdl, stream)
+                  : s5_launch<false, 1, false, false, false, true>(q, ck, kr, vr, gm, bm, grid, smem, pdl, stream);
+}
+#endif  // GDNR_S5_SPLIT_TU
+
 }  // namespace gdnr
 
 // ---------------------------------------------------------------- bounded-wait self-test
+#ifndef GDNR_S5_SPLIT_TU
 namespace gdnr {
 
 // One CTA, two warps, exercising the error path of the persistent kernel's
@@ -2564,3 +2600,4 @@ extern "C" int gdnr_selftest_wait_timeout(uint32_t* error_flag, unsigned long lo
   s5_wait_selftest_kernel<<<1, 64, 0, static_cast<cudaStream_t>(stream)>>>(err, report);
   return cuda_status(cudaGetLastError(), "gdnr_selftest_wait_timeout launch");
 }
+#endif  // GDNR_S5_SPLIT_TU
