@@ -1108,7 +1108,13 @@ __device__ __forceinline__ S5Append s5_chain(const StepParams& p, const S5Unit& 
 // I8: the tile holds int8 codes and t8 four int8 limbs of T (s5_tsplit): the
 // tile product runs on the integer tensor path (exact s32 sums, below 2^24 so
 // they convert to f32 exactly) and the ring product into its own f32 accumulator.
-template <int MW, bool I8 = false>
+// REG: o of row rbase + 32 pr + s5_rd_row(lane) goes to ost[pr] (registers once
+// inlined) instead of shared memory.
+__device__ __forceinline__ int s5_rd_row(int lane) {
+  const int g8 = lane >> 2, t4 = lane & 3;
+  return 16 * (t4 & 1) + g8 + 8 * (t4 >> 1);
+}
+template <int MW, bool I8 = false, bool REG = false>
 __device__ __forceinline__ void s5_readout(const uint8_t* ck_s, const uint8_t* vr_s, const uint8_t* t8,
                                            const uint16_t* cb, float inv_sig, float sc, int sc_base, int rbase,
                                            int nmem, float* ost, int lane) {
@@ -1129,7 +1135,7 @@ __device__ __forceinline__ void s5_readout(const uint8_t* ck_s, const uint8_t* v
   const uint32_t ck_addr = smem_addr(ck_s), vr_addr = smem_addr(vr_s);
   const int mi = lane >> 3, r8 = lane & 7;
   // m-tiles in pairs (one vblock of 32 rows per pair)
-#pragma unroll 1
+#pragma unroll(REG ? MW / 2 : (MW == 4 ? 2 : 1))
   for (int pr = 0; pr < MW / 2; ++pr) {
     const int rp = rbase + 32 * pr;
     float acc[2][4];
@@ -1191,7 +1197,10 @@ __device__ __forceinline__ void s5_readout(const uint8_t* ck_s, const uint8_t* v
     const bool hi = t4 & 2;
     float r = hi ? x1 : x0;
     r += __shfl_xor_sync(0xffffffffu, hi ? x0 : x1, 2);
-    ost[32 * pr + 16 * (t4 & 1) + g8 + 8 * (t4 >> 1)] = r;
+    if constexpr (REG)
+      ost[pr] = r;
+    else
+      ost[32 * pr + s5_rd_row(lane)] = r;
   }
 }
 
@@ -2174,8 +2183,8 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
   // q VPW of the unit (heads in order); the unit's WPU warps release its stage
   // and chain results as they finish.
   constexpr int NG = S5_NRW / WPU;  // readout groups (units in flight)
-  float* ost = reinterpret_cast<float*>(smem + lay.ost0 + rw * 512);
   const float sc_pre = s5_cvt(scl_raw, p.sc_dt);
+  const int orow = rbase + s5_rd_row(lane);  // the lane's rows: orow + 32 v, v < VPW
   for (int i = rw / WPU; i < nu; i += NG) {
     const int s = i % S5_NS;
     const int ccw = i % S5_NCW, k = i / S5_NCW;
@@ -2192,26 +2201,29 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
                          p.sc_dt);
       }
     }
-    bool ok = s5_warp_wait(&full[s], (i / S5_NS) & 1, p.err, abort, lane);
-    ok = s5_warp_wait(&cbar[ccw], uint32_t(k & 1), p.err, abort, lane) && ok;
+    // the unit's indices ahead of the waits (integer divisions)
+    const S5Unit U = s5_unit<SIDX>(bid + i * grid, p, G, geo);
+    int okw = 1;
+    if (lane == 0) {
+      okw = s5_wait(&full[s], (i / S5_NS) & 1, p.err, abort) ? 1 : 0;
+      okw = (s5_wait(&cbar[ccw], uint32_t(k & 1), p.err, abort) && okw) ? 1 : 0;
+    }
+    const bool ok = __shfl_sync(0xffffffffu, okw, 0) != 0;
     uint8_t* sb = smem + lay.stage0 + s * lay.stage_bytes;
     if (ok && !s5_skip(code)) {
-      const S5Unit U = s5_unit<SIDX>(bid + i * grid, p, G, geo);
       const uint8_t* res = smem + lay.res0 + ccw * lay.res_bytes;
       const float* misc = reinterpret_cast<const float*>(res + lay.misc) + head_r * 4;
-      s5_readout<2 * VPW, I8>(sb + lay.ck + head_r * 16384, sb + lay.vr + head_r * 4096,
-                              res + lay.t8 + head_r * 8 * T8STR,
-                              reinterpret_cast<const uint16_t*>(res + lay.cb + head_r * 96), misc[0], sc, sc_base,
-                              rbase, s5_nmem(code), ost, lane);
-      __syncwarp();
-      // this token's own slot (fused) as a rank-one term, K^-1/2, VPW rows per lane
       float o[VPW];
-#pragma unroll
-      for (int r = 0; r < VPW; ++r) o[r] = ost[VPW * lane + r];
+      s5_readout<2 * VPW, I8, true>(sb + lay.ck + head_r * 16384, sb + lay.vr + head_r * 4096,
+                                    res + lay.t8 + head_r * 8 * T8STR,
+                                    reinterpret_cast<const uint16_t*>(res + lay.cb + head_r * 96), misc[0], sc,
+                                    sc_base, rbase, s5_nmem(code), o, lane);
+      // this token's own slot (fused) as a rank-one term
       if (FUSED) {
-        const uint16_t* vnew = reinterpret_cast<const uint16_t*>(res + lay.vnew + head_r * 256) + rbase;
+        const uint16_t* vnew = reinterpret_cast<const uint16_t*>(res + lay.vnew + head_r * 256);
+        const float c1 = misc[1];
 #pragma unroll
-        for (int r = 0; r < VPW; ++r) o[r] = fmaf(misc[1], bf16_to_f(vnew[VPW * lane + r]), o[r]);
+        for (int r = 0; r < VPW; ++r) o[r] = fmaf(c1, bf16_to_f(vnew[orow + 32 * r]), o[r]);
       }
       __syncwarp();
       // every read of the stage and the chain's results has returned its value (all
@@ -2221,11 +2233,9 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
         s5_arrive_relaxed(&empty[s]);
         s5_arrive_relaxed(&rbar[ccw]);
       }
+      const int64_t ob = int64_t(U.b) * p.o_sb + int64_t(U.hv0 + head_r) * p.o_sh;
 #pragma unroll
-      for (int r = 0; r < VPW; ++r)
-        store_scalar(p.out,
-                     int64_t(U.b) * p.o_sb + int64_t(U.hv0 + head_r) * p.o_sh + int64_t(rbase + VPW * lane + r) * p.o_sv,
-                     p.o_dt, o[r] * KSCALE_H);
+      for (int r = 0; r < VPW; ++r) store_scalar(p.out, ob + int64_t(orow + 32 * r) * p.o_sv, p.o_dt, o[r] * KSCALE_H);
     } else {
       __syncwarp();
       if (lane == 0) {
