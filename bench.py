@@ -713,10 +713,21 @@ def run_heterogeneous(args, stack, device, stream, uniform_us):
     per = time_cycles(graphs, stream, cycles=4)
     del graphs
     us = 1e3 * statistics.fmean(per) / NL
+    # the uniform cycle again under the default hint ("auto" on every step: the
+    # flush-capable kernel also on the steps where no sequence flushes)
+    upos = uniform_positions(B, L, device)
+    graphs = capture_positions(lambda s: stack.launch(s, upos[s], "auto", err), L, stream)
+    uper = time_cycles(graphs, stream, cycles=4)
+    del graphs
+    auto_us = 1e3 * statistics.fmean(uper) / NL
     return {"us_per_layer_step": us, "steps_seq_per_s": B / (us * 1e-6), "uniform_cycle_us_per_layer_step": uniform_us,
             "ratio_to_uniform": us / uniform_us, "device_error_word": int(err.item()),
+            "uniform_cycle_default_hint": {"us_per_layer_step": auto_us, "steps_seq_per_s": B / (auto_us * 1e-6),
+                                           "us_nonflush": 1e3 * statistics.fmean(uper[:-1]) / NL,
+                                           "us_flush": 1e3 * uper[-1] / NL},
             "workload": f"batch {B}, L={L}, {NL} layers, sequence b at ring position (b + s) % L on step s (1/L flush "
-                        "on every step), flush_hint 'auto', 4 cycles"}
+                        "on every step), flush_hint 'auto', 4 cycles; uniform_cycle_default_hint: the headline's "
+                        "uniform positions with flush_hint 'auto' on every step"}
 
 
 def run_sweep(args, device, stream):

@@ -57,6 +57,18 @@ template <int HPU, bool FLUSH>
 __host__ __device__ constexpr bool s5_tc() {
   return HPU == 2 && FLUSH;
 }
+// In that variant the entries that do not flush are read out either on the
+// tensor cores through tensor memory (S5_VBF 0) or, with S5_VBF, by the
+// register-fragment vblock readout of the variant without the flush path (four
+// warps per entry, two 32-row vblocks each); the flush entries, the claims and
+// the tensor-memory stash of the flush tasks are the same in both.
+#ifndef S5_VBF
+#define S5_VBF 1
+#endif
+template <int HPU, bool FLUSH>
+__host__ __device__ constexpr bool s5_tcr() {
+  return s5_tc<HPU, FLUSH>() && !S5_VBF;
+}
 // Readout of the variant without the flush path ("vblock readout"): every
 // readout warp takes one 32-row vblock of a unit (warp w: head w / 4, rows
 // 32 (w % 4) ..), so that a unit is read out by 4 x hpu warps at once (one-head
@@ -1061,7 +1073,7 @@ __device__ __forceinline__ S5Append s5_chain(const StepParams& p, const S5Unit& 
   s5_solve(em, bsel, acc, cval, t);
   // ---- c -> [c_hi; c_mid; c_lo] bf16 over the slots read from memory (ring
   // columns of the readout); this token's own slot is a rank-one term
-  constexpr bool TC = s5_tc<HPU, FLUSH>();
+  constexpr bool TC = s5_tcr<HPU, FLUSH>();
   if (TC && e < HPU) reinterpret_cast<float*>(res + lay.cf)[e * 16 + t] = t < nmem ? cval : 0.0f;
   if (!TC && e < HPU) {
     uint16_t* cb = reinterpret_cast<uint16_t*>(res + lay.cb + e * 96);
@@ -1098,7 +1110,7 @@ __device__ __forceinline__ S5Append s5_chain(const StepParams& p, const S5Unit& 
     if (e < HPU && t < n) p.coo[int64_t(U.b) * p.coo_sb + int64_t(U.hv0 + e) * p.coo_sh + int64_t(t) * p.coo_st] = cval;
   }
   __syncwarp();  // q-split / Gram scratch (aliases t8) is dead from here on
-  s5_tsplit<HPU, s5_tc<HPU, FLUSH>(), I8>(T, res + lay.t8, misc, lane);
+  s5_tsplit<HPU, s5_tcr<HPU, FLUSH>(), I8>(T, res + lay.t8, misc, lane);
   return ap;
 }
 
@@ -1568,6 +1580,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
   static_assert(!(I8 && (FLUSH || SIDX)), "int8 checkpoints: the non-flush, slot-free variant only");
   extern __shared__ __align__(1024) uint8_t smem[];
   constexpr bool TC = s5_tc<HPU, FLUSH>();
+  constexpr bool TCR = s5_tcr<HPU, FLUSH>();  // non-flush entries on the tensor cores
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int L = p.L, G = p.HV / p.H;
   const S5Geo geo = s5_geo(p.H, p.HV, L);
@@ -1850,7 +1863,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
         }
       }
     };
-    if constexpr (TC) {
+    if constexpr (TCR) {
       // Tensor-memory readout: this thread also issues each unit's tensor-core readout
       // as soon as its stage has landed and its chain is done -- per head 4 x
       // tcgen05.mma (M = 128 rows, N = 16: five T terms + zeros, K = 32) from the
@@ -2025,6 +2038,62 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
                      o[h] * KSCALE_H);
     }
   };
+  // ---- vblock readout of one entry that does not flush (S5_VBF), by one warp of a
+  // readout group of 4: warp position q = warp % 4 reads the two 32-row vblocks
+  // 2q, 2q + 1 of the unit (head q / 2) as the variant without the flush path
+  // does; the group's 4 warps owe the 8 arrivals of the entry (2 each).
+  auto vb_group_entry = [&](int i, int code) {
+    constexpr int VP = s5_vpw<HPU>();
+    const int s = i % S5_NS;
+    const uint32_t par = (i / S5_NS) & 1;
+    const int ui = s5_uidx(code);
+    const int ccw = ui % S5_NCW, k = ui / S5_NCW;
+    const int vqw = (warp & 3) * VP;
+    const int hr = vqw / 4, rb = 32 * (vqw % 4);
+    const S5Unit U = s5_unit<SIDX>(bid + ui * grid, p, G, geo);
+    const bool skip = s5_skip(code);
+    // lane v < VP: the scale of vblock rb / 32 + v, issued before the waits
+    uint32_t scr = 0u;
+    if (!skip && lane < VP)
+      scr = s5_ld_raw(p.sc, int64_t(U.s) * p.sc_sb + int64_t(U.hv0 + hr) * p.sc_sh + int64_t(rb / VBLOCK + lane) * p.sc_sv,
+                      p.sc_dt);
+    int okw = 1;
+    if (lane == 0) {
+      okw = s5_wait(&full[s], par, p.err, abort) ? 1 : 0;
+      okw = (s5_wait(&cbar[ccw], uint32_t(k & 1), p.err, abort) && okw) ? 1 : 0;
+    }
+    const bool ok = __shfl_sync(0xffffffffu, okw, 0) != 0;
+    if (ok && !skip) {
+      const uint8_t* sb = smem + lay.stage0 + s * lay.stage_bytes;
+      const uint8_t* res = smem + lay.res0 + ccw * lay.res_bytes;
+      const float* misc = reinterpret_cast<const float*>(res + lay.misc) + hr * 4;
+      const int orow = rb + s5_rd_row(lane);
+      float o[VP];
+      s5_readout<2 * VP, I8, true>(sb + lay.ck + hr * 16384, sb + lay.vr + hr * 4096, res + lay.t8 + hr * 8 * T8STR,
+                                   reinterpret_cast<const uint16_t*>(res + lay.cb + hr * 96), misc[0],
+                                   s5_cvt(scr, p.sc_dt), 0, rb, s5_nmem(code), o, lane);
+      if (FUSED) {
+        const uint16_t* vnew = reinterpret_cast<const uint16_t*>(res + lay.vnew + hr * 256);
+        const float c1 = misc[1];
+#pragma unroll
+        for (int r = 0; r < VP; ++r) o[r] = fmaf(c1, bf16_to_f(vnew[orow + 32 * r]), o[r]);
+      }
+      __syncwarp();
+      if (lane == 0) {
+        s5_arrive_relaxed_n(&empty[s], 2u);
+        s5_arrive_relaxed_n(&rbar[ccw], 2u);
+      }
+      const int64_t ob = int64_t(U.b) * p.o_sb + int64_t(U.hv0 + hr) * p.o_sh;
+#pragma unroll
+      for (int r = 0; r < VP; ++r) store_scalar(p.out, ob + int64_t(orow + 32 * r) * p.o_sv, p.o_dt, o[r] * KSCALE_H);
+    } else {
+      __syncwarp();
+      if (lane == 0) {
+        s5_arrive_n(&empty[s], 2u);
+        s5_arrive_n(&rbar[ccw], 2u);
+      }
+    }
+  };
   // Claim mode: the group's first warp claims the next entry after the flush
   // entries (a shared counter), the group syncs on a named barrier of its own and
   // reads the claim (double-buffered, so that a claim is never overwritten before
@@ -2039,7 +2108,10 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       const int r = int(*slot);
       if (r >= ncl) break;
       const int i = int(gw[8 + r]);
-      tc_group_entry(i, table[i]);
+      if constexpr (TCR)
+        tc_group_entry(i, table[i]);
+      else
+        vb_group_entry(i, table[i]);
     }
   };
 
@@ -2078,7 +2150,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       S5Append ap{};
       if (work) ap = s5_chain<FUSED, HPU, FLUSH, I8, WT>(p, U, code, in0, kbuf, gbuf, res, lay, lane);
       // the T operand is read by the tensor cores (async proxy)
-      if (TC) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      if (TCR) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0) s5_arrive(&cbar[cw]);
       if (work) s5_append<FUSED, HPU>(p, U, code, ap, lane);
@@ -2122,7 +2194,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       ok = s5_warp_wait(&cbar[ccw], uint32_t(k & 1), p.err, abort, lane) && ok;
       uint8_t* sb = smem + lay.stage0 + s * lay.stage_bytes;
       const S5Unit U = s5_unit<SIDX>(bid + ui * grid, p, G, geo);
-      s5_warp_wait(&mmab[s], par, p.err, abort, lane);  // keeps the commits in step (none issued for it)
+      if constexpr (TCR) s5_warp_wait(&mmab[s], par, p.err, abort, lane);  // keeps the commits in step (none issued for it)
       // The unit's 4 x 2 vblock tasks, one per readout warp (task rw), then one
       // tensor-map store by the warp whose acquire-release increment of the unit's
       // done count completes it (the other tasks' released rows are visible to
@@ -2157,14 +2229,19 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
         if (FLUSH && s5_flush(code)) {
           flush_entry(i);
         } else {
-          if ((rank & 1) == g) tc_group_entry(i, code);
+          if ((rank & 1) == g) {
+            if constexpr (TCR)
+              tc_group_entry(i, code);
+            else
+              vb_group_entry(i, code);
+          }
           ++rank;
         }
       }
     }
     // the last commit covers every MMA this CTA issued: complete before the
     // tensor memory is released (and the third group is done with it)
-    if (rw == 0 && nu > 0 &&
+    if (TCR && rw == 0 && nu > 0 &&
         !s5_warp_wait(&mmab[(nu - 1) % S5_NS], uint32_t(((nu - 1) / S5_NS) & 1), p.err, abort, lane) && lane == 0)
       s5_drain_mma(mmab, reinterpret_cast<const uint32_t*>(smem + lay.tmem) + 1);
     s5_tc_before_sync();
