@@ -81,6 +81,9 @@ struct StepParams {
   // persistent step without the flush path: the gate rings are read by TMA
   // (set by its launcher when their layout allows)
   int32_t gtma;
+  // persistent step: one value head per work unit even when two share a key head
+  // (set by its launcher for steps without the flush path on small batches)
+  int32_t hpu1;
   // split replay (gdnr_replay_split): the persistent kernel also writes the
   // transformed query T [B,HV,K] (innermost contiguous) and the coefficients c_t
   // (t < valid_len) [B,HV,L] to these caller buffers; null otherwise

@@ -118,10 +118,10 @@ struct S5Geo {
   int rb;   // ring slots per TMA request (8, or 4 when L < 8)
 };
 
-__host__ __device__ inline S5Geo s5_geo(int H, int HV, int L) {
+__host__ __device__ inline S5Geo s5_geo(int H, int HV, int L, bool one_head = false) {
   S5Geo g;
   const int G = HV / H;
-  g.hpu = G >= 2 ? 2 : 1;
+  g.hpu = G >= 2 && !one_head ? 2 : 1;
   g.upk = G / g.hpu;
   g.rb = L >= 8 ? 8 : 4;
   return g;
@@ -1583,7 +1583,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
   constexpr bool TCR = s5_tcr<HPU, FLUSH>();  // non-flush entries on the tensor cores
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int L = p.L, G = p.HV / p.H;
-  const S5Geo geo = s5_geo(p.H, p.HV, L);
+  const S5Geo geo = s5_geo(p.H, p.HV, L, p.hpu1 != 0);
   const int total = p.B * p.H * geo.upk;
   const int grid = int(gridDim.x), bid = int(blockIdx.x);
   const int nu = total > bid ? (total - bid + grid - 1) / grid : 0;
@@ -1606,7 +1606,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
   // the layout must fit the dynamic shared memory the launch was given
   uint32_t dyn_smem;
   asm("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn_smem));
-  if ((smem_addr(smem) & 1023u) != 0 || lay.total > dyn_smem) {
+  if ((smem_addr(smem) & 1023u) != 0 || lay.total > dyn_smem || geo.hpu != HPU) {
     if (tid == 0) atomicOr(p.err, GDNR_DEVERR_LAYOUT);
     return;
   }
@@ -2443,7 +2443,7 @@ static bool s5_grid(const StepParams& p, int& grid, S5Layout& lay) {
   const bool flush = p.flush_hint != GDNR_FLUSH_NONE;
   const int nsm = s5_sm_count();
   if (nsm <= 0) return false;
-  const S5Geo g = s5_geo(p.H, p.HV, p.L);
+  const S5Geo g = s5_geo(p.H, p.HV, p.L, p.hpu1 != 0);
   const int64_t total = int64_t(p.B) * p.H * g.upk;
   if (total <= 0 || total > (int64_t(1) << 30)) return false;
   grid = int(total < nsm ? total : nsm);
@@ -2527,10 +2527,21 @@ static cudaError_t s5_launch(const StepParams& p, const CUtensorMap& ck, const C
 }
 
 #ifndef GDNR_S5_SPLIT_TU
-cudaError_t launch_step5(const StepParams& p, bool fused, bool pdl, cudaStream_t stream) {
+cudaError_t launch_step5(const StepParams& p_in, bool fused, bool pdl, cudaStream_t stream) {
   S5EncodeFn enc = s5_encode_fn();
   if (!enc) return cudaErrorNotSupported;
-  const S5Geo g = s5_geo(p.H, p.HV, p.L);
+  // Steps without the flush path on a batch of at most 4 value heads per SM: one
+  // value head per unit (twice the units, each chain half as long), which is
+  // slightly shorter there (B = 1 / 4 / 16, L = 16: 0.16-0.30 / 0.06-0.59 /
+  // 0.14-0.34 us less per launch, two boxes); with more value heads (B = 64:
+  // 14.4 -> 22.2 us) or with the flush path (one-head units use the team
+  // readout: 17.0 -> 22.8 us at B = 1) the two-head units are faster.
+  StepParams p = p_in;
+  p.hpu1 = (p.flush_hint == GDNR_FLUSH_NONE && p.HV >= 2 * p.H &&
+            int64_t(p.B) * p.HV <= 4 * int64_t(s5_sm_count()))
+               ? 1
+               : 0;
+  const S5Geo g = s5_geo(p.H, p.HV, p.L, p.hpu1 != 0);
   int grid;
   S5Layout lay;
   if (!s5_grid(p, grid, lay)) return cudaErrorInvalidValue;
