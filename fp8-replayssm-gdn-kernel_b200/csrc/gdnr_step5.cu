@@ -2157,15 +2157,13 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
     }
     if constexpr (TC) {
       // claim mode: chain warps 1..4 (lane quarters 1, 2, 3, 0) are readout group 2
-      if (claim && warp <= 4) {
-        asm volatile("bar.sync 10, %0;" ::"n"(32 * (S5_NRW + 4)) : "memory");
-        s5_tc_after_sync();
-        tc_claim_loop(2);
-        s5_tc_before_sync();
-        asm volatile("bar.sync 11, %0;" ::"n"(32 * (S5_NRW + 4)) : "memory");
-      }
+      // (they continue into the readout below, so that one copy of its code serves
+      // all three groups)
+      if (!(claim && warp <= 4)) return;
+      asm volatile("bar.sync 10, %0;" ::"n"(32 * (S5_NRW + 4)) : "memory");
+    } else {
+      return;
     }
-    return;
   }
 
   if constexpr (TC) {
@@ -2217,10 +2215,12 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
         s5_arrive(&rbar[ccw]);
       }
     };
-    const int g = rw >> 2;
+    // claim mode: chain warps 1..4 arrive here as group 2 (no flush tasks)
+    const int g = chain_warp ? 2 : (rw >> 2);
     if (claim) {
-      for (int i = 0; i < nu; ++i)
-        if (FLUSH && s5_flush(table[i])) flush_entry(i);
+      if (!chain_warp)
+        for (int i = 0; i < nu; ++i)
+          if (FLUSH && s5_flush(table[i])) flush_entry(i);
       tc_claim_loop(g);
     } else {
       int rank = 0;
