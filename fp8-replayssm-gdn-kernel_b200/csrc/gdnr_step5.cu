@@ -95,10 +95,12 @@ __host__ __device__ constexpr int s5_rpu() {  // readout warps per unit
 }
 // Tensor memory of the tensor-memory readout: columns 0..127 the readout's
 // accumulators (stages x heads x 16); from S5_TM_STASH, 128 columns per readout
-// warp of a lane quarter, where a flush task parks its rebuilt state between
-// the amax and the re-quantisation pass.
+// warp of a lane quarter (two per quarter), then 128 for the chain warp of the
+// quarter among chain warps 1..4, where a flush task parks its rebuilt state
+// between the amax and the re-quantisation pass.
 constexpr uint32_t S5_TM_STASH = 128;
-constexpr uint32_t S5_TMEM_COLS = 512;  // power of two >= S5_TM_STASH + 2 x 128
+constexpr uint32_t S5_TMEM_COLS = 512;  // power of two >= S5_TM_STASH + 3 x 128
+static_assert(S5_TMEM_COLS >= S5_TM_STASH + 3 * 128, "tensor memory: stash of two readout warps and a chain warp per quarter");
 // A chain warp's result area: T terms of a non-flush unit (2 x 8 x T8STR), or the
 // flush data of a flush unit -- q split as f16 x 256 [2][128], then per head
 // (float offsets) a_t [16] at S5_FA, beta_t [16] at S5_FB, 1 / (operand scale) at
@@ -187,7 +189,7 @@ __host__ __device__ inline S5Layout s5_layout(const S5Geo& g, int max_units, boo
   s.res0 = o;
   o += S5_NCW * s.res_bytes;
   s.ost0 = o;
-  o += S5_NRW * 512u;
+  o += (S5_NRW + (flush ? 4u : 0u)) * 512u;  // flush-capable: also chain warps 1..4 (flush tasks)
   s.zb = smem_take(o, 1024u);  // zeros: rows 8..15 of every T operand (N = 16)
   s.gbuf0 = smem_take(o, flush ? 0u : S5_NCW * 512u);
   s.total = o;
@@ -2180,9 +2182,19 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + lay.tmem);
     const int qd = warp & 3;
     // this warp's flush stash: its lane quarter, 128 columns (two warps share a quarter)
-    const uint32_t stash = tmem + (uint32_t(32 * qd) << 16) + S5_TM_STASH + 128u * uint32_t(rw >> 2);
-    float* ost = reinterpret_cast<float*>(smem + lay.ost0 + rw * 512);
-    auto flush_entry = [&](int i) {
+    // Flush-task workers: the readout warps (worker rw), and in claim mode when
+    // every unit of the CTA flushes (no entries to claim) also chain warps 1..4
+    // (workers 8..11); a worker takes task (f S5_NRW + t) mod workers of the f-th
+    // flush entry, entries in order, so every wait is on an earlier entry.
+    const bool allflush = claim && int(reinterpret_cast<const uint32_t*>(smem + lay.gwords)[0]) == nu;
+    const int nwk = allflush ? S5_NRW + 4 : S5_NRW;
+    const int wk = chain_warp ? S5_NRW + (warp - 1) : rw;
+    // the worker's flush stash: its lane quarter, 128 columns (readout warps: two
+    // per quarter from S5_TM_STASH; chain warps 1..4: one per quarter after them)
+    const uint32_t stash = tmem + (uint32_t(32 * qd) << 16) + S5_TM_STASH +
+                           (chain_warp ? 256u : 128u * uint32_t(rw >> 2));
+    float* ost = reinterpret_cast<float*>(smem + lay.ost0 + wk * 512);
+    auto flush_entry = [&](int i, int task) {
       const int s = i % S5_NS;
       const uint32_t par = (i / S5_NS) & 1;
       const int code = table[i];
@@ -2200,7 +2212,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       static_assert(4 * HPU == S5_NRW, "one flush task per readout warp");
       int last = 0;
       if (ok) {
-        s5_flush_task<FUSED, HPU>(p, smem, lay, U, s, ccw, code, rw, ost, stash, lane);
+        s5_flush_task<FUSED, HPU>(p, smem, lay, U, s, ccw, code, task, ost, stash, lane);
         if (lane == 0 && s5_add_acq_rel(&tdone[i], 1u) == uint32_t(S5_NRW - 1)) last = 1;
       }
       if (__shfl_sync(0xffffffffu, last, 0) && lane == 0 && *abort == 0) {
@@ -2218,16 +2230,22 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
     // claim mode: chain warps 1..4 arrive here as group 2 (no flush tasks)
     const int g = chain_warp ? 2 : (rw >> 2);
     if (claim) {
-      if (!chain_warp)
+      if (!chain_warp || allflush) {
+        int fo = 0;  // flush entries so far
         for (int i = 0; i < nu; ++i)
-          if (FLUSH && s5_flush(table[i])) flush_entry(i);
+          if (FLUSH && s5_flush(table[i])) {
+            const int t = ((wk - fo * S5_NRW) % nwk + nwk) % nwk;
+            if (t < S5_NRW) flush_entry(i, t);
+            ++fo;
+          }
+      }
       tc_claim_loop(g);
     } else {
       int rank = 0;
       for (int i = 0; i < nu; ++i) {
         const int code = table[i];
         if (FLUSH && s5_flush(code)) {
-          flush_entry(i);
+          flush_entry(i, rw);
         } else {
           if ((rank & 1) == g) {
             if constexpr (TCR)
