@@ -311,22 +311,26 @@ def reference_torch_cpu(args):
         beta = torch.sigmoid(torch.randn(B, T, HV, generator=gen))
         return q, k, v, g, beta
 
-    # replay_decode(T tokens) runs all T steps of the chain; one cycle = L steps
-    q, k, v, g, beta = inputs(1)
+    # replay_decode(T tokens) runs all T steps of the chain; one cycle = L steps.
+    # Warm-up: --warmup single steps (untimed); then whole cycles, as many as
+    # --steps asks for within about a minute of host time.
+    warm = max(1, args.warmup)
     t0 = time.perf_counter()
-    ref.replay_decode(state, q, k, v, g, beta, L, "vblock", 32)
-    one = time.perf_counter() - t0  # one step at fill 1: sizes the sample
-    cycles = 1
+    for _ in range(warm):
+        q, k, v, g, beta = inputs(1)
+        ref.replay_decode(state, q, k, v, g, beta, L, "vblock", 32)
+    one = (time.perf_counter() - t0) / warm  # one step at fill 1: sizes the sample
+    cycles = max(1, min(args.steps // L, int(60.0 / max(one * L * (L + 1) / 2, 1e-3))))
     t0 = time.perf_counter()
     q, k, v, g, beta = inputs(L * cycles)
     ref.replay_decode(state, q, k, v, g, beta, L, "vblock", 32)
     wall = time.perf_counter() - t0
     steps = L * cycles
     value = steps * B / wall
-    return {"value": value, "unit": UNIT, "cores": threads, "kind": "reference", "steps": steps,
+    return {"value": value, "unit": UNIT, "cores": threads, "kind": "reference", "steps": steps, "warmup": warm,
             "sample": f"the reference's replay_decode (gdn_replay_fp8_reference.py, torch on CPU, {threads} threads) "
                       f"over {steps} decode steps (whole L={L} cycles incl. the flush) of batch {B}, H={H}, HV={HV}; "
-                      f"{wall:.1f} s wall (first step probe {one:.2f} s)"}
+                      f"{wall:.1f} s wall after {warm} warm-up step(s) of {one:.2f} s each"}
 
 
 def run_reference(args, world, rank):
@@ -344,6 +348,7 @@ def run_reference(args, world, rank):
         ref_err = None
     if ref is not None:
         value, steps, ms = ref["value"], ref["steps"], 1e3 * args.batch / ref["value"]
+        warm = ref["warmup"]
         cpu = {k: ref[k] for k in ("value", "unit", "cores", "kind", "sample")}
         cfg_batch, note = args.batch, "the reference's own torch replay_decode, imported from baseline/_ref"
     else:
@@ -356,6 +361,7 @@ def run_reference(args, world, rank):
             steps //= 2
         t_units, t_wall = cpu_units(max(1, steps), workers, args.seed, args.ring)
         value, ms, cfg_batch = t_units / t_wall, 1e3 * t_wall / max(1, steps), workers
+        warm = 1
         cpu = {"value": value, "unit": UNIT, "cores": workers, "kind": "port",
                "sample": f"{t_units} sequence-layer steps ({workers} sequences per step, {steps} steps) of the numpy "
                          "oracle port of replay_decode"}
@@ -368,7 +374,7 @@ def run_reference(args, world, rank):
         "unit": UNIT,
         "n_gpus": args.gpus,
         "steps": steps,
-        "warmup": 1,
+        "warmup": warm,
         "ms_per_step": ms,
         "higher_is_better": True,
         "scaling": "weak",
