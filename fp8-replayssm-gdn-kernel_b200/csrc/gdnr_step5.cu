@@ -21,14 +21,15 @@
 //    its key ring (4 KB, loaded by the chain warp's own TMA), so all chains of
 //    the SM run while the checkpoints are still streaming in.
 //  * readout (S5_NRW warps): consumes the stages in order; in the variant
-//    without the flush path each warp reads out one 32-row vblock of every unit
-//    (both heads of a unit at once) on tensor cores: S_fp8 . T as an e4m3 MMA
-//    against T split into five e4m3 terms, V^T c as a bf16 MMA into the spare
-//    accumulator columns, plus this token's value row (rank one).
+//    without the flush path two groups of four warps take alternate units, each
+//    warp two 32-row vblocks of its unit, on tensor cores: S_fp8 . T as an e4m3
+//    MMA against T split into five e4m3 terms, V^T c as a bf16 MMA into the
+//    spare accumulator columns, plus this token's value row (rank one).
 //
 // Units whose ring is full (flush) take the same stages: their chain warp
-// hands the decayed Gram matrix and gates to the readout team, whose warps
-// rebuild the state in WY form on tensor cores one vblock of 32 rows at a time
+// hands the decayed Gram matrix and gates to the flush-task workers (the
+// readout warps; when every unit of the CTA flushes, also chain warps 1..4),
+// which rebuild the state in WY form on tensor cores one vblock of 32 rows at a time
 // (E = S0 [K; q]^T, the u recurrence, S_L = a S0 + W K), re-quantise it into
 // the stage (vblock32 scales, ref.py:40-106) and write both heads back with one
 // tensor-map store.  With GDNR_FLUSH_NONE they are skipped and reported.
@@ -47,12 +48,12 @@ constexpr int S5_NRW = 8;   // readout warps
 constexpr int S5_TEAM = S5_NRW / S5_NS;  // readout warps per stage
 constexpr int S5_THREADS = 32 * (1 + S5_NCW + S5_NRW);
 constexpr int S5_GSTR = 20;  // Gram scratch row (floats): 16 key columns + 3 query terms + pad
-// Readout structure.  The flush-capable variant with two-head units ("TC") reads
-// out through tensor memory with all readout warps on every unit (warp w: head
-// (w - 1 - S5_NCW) / 4, tensor-memory lanes 32 (w % 4) ..), so that a flush
-// unit's vblock tasks are shared by all of them.  Otherwise a team of S5_TEAM
-// warps per stage reads out a unit with register-fragment MMAs, four units at a
-// time -- faster when no unit flushes.
+// Readout structure.  The flush-capable variant with two-head units ("TC")
+// shares a flush unit's eight vblock tasks among all readout warps (task w: head
+// w / 4, rows 32 (w % 4) ..; their rebuilt state parks in tensor memory) and
+// reads the other units out with groups of four warps that claim them in order.
+// The flush-capable variant with one-head units uses a team of S5_TEAM warps per
+// stage, four units at a time.
 template <int HPU, bool FLUSH>
 __host__ __device__ constexpr bool s5_tc() {
   return HPU == 2 && FLUSH;
