@@ -2206,7 +2206,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
       uint8_t* sb = smem + lay.stage0 + s * lay.stage_bytes;
       const S5Unit U = s5_unit<SIDX>(bid + ui * grid, p, G, geo);
       if constexpr (TCR) s5_warp_wait(&mmab[s], par, p.err, abort, lane);  // keeps the commits in step (none issued for it)
-      // The unit's 4 x 2 vblock tasks, one per readout warp (task rw), then one
+      // The unit's 4 x 2 vblock tasks, one per worker (task `task`), then one
       // tensor-map store by the warp whose acquire-release increment of the unit's
       // done count completes it (the other tasks' released rows are visible to
       // it); the others release the stage now (it is reloaded only after all have).
@@ -2228,7 +2228,8 @@ __global__ void __launch_bounds__(S5_THREADS, 1)
         s5_arrive(&rbar[ccw]);
       }
     };
-    // claim mode: chain warps 1..4 arrive here as group 2 (no flush tasks)
+    // claim mode: chain warps 1..4 arrive here as group 2 (flush tasks too when
+    // every unit of the CTA flushes; there is then nothing to claim)
     const int g = chain_warp ? 2 : (rw >> 2);
     if (claim) {
       if (!chain_warp || allflush) {
